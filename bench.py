@@ -1,0 +1,546 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 grouped-convolution engine (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload NAME]
+    python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...
+    python bench.py --impl reference ...     # the reference's CPU implementation
+
+A step is one gc_cuda_conv call (implementation 3, the production choice)
+over one batch of synthetic input already resident in HBM.  Default workload:
+the depthwise N32 C256 56x56 convolution, one batch per GPU ("weak": every
+rank runs its own batch, no collective on the data path).  ``--workload
+config5_g32 --scaling strong`` shards the N1024 batch across the ranks.
+
+Reported: ``value`` (GB/s of algorithmic bytes, whole job, device time of K
+back-to-back steps, max over ranks), ``e2e`` (same metric through the C ABI
+with the batch in pinned host memory and both copies inside the timed
+region), ``roofline`` of the kernel, ``cudnn`` (torch.nn.functional.conv2d,
+TF32 off, benchmark mode, same buffers), ``cpu_baseline`` (the reference's CPU
+library on the host cores), ``clocks`` sampled through NVML while timing.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as ct
+import datetime
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+
+METRIC = 'grouped-conv GB/s & GFLOP/s (% of B200 roofline), latency ratio vs cuDNN, 1/2/4/8 GPU'
+UNIT = 'GB/s'
+L2_BYTES = 126 * 1024 * 1024
+FALLBACK_PEAKS = {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0}
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=2000)
+    ap.add_argument('--warmup', type=int, default=20)
+    ap.add_argument('--impl', choices=['ours', 'reference'], default='ours')
+    ap.add_argument('--workload', default='config2',
+                    choices=['config1', 'config2', 'config4_leaf', 'config5_g32', 'config5_g4'])
+    ap.add_argument('--scaling', choices=['weak', 'strong'], default=None,
+                    help='weak: each rank runs the full workload batch; strong: the batch is sharded')
+    ap.add_argument('--e2e-steps', type=int, default=20)
+    ap.add_argument('--no-e2e', action='store_true')
+    ap.add_argument('--no-cudnn', action='store_true')
+    ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--cpu-seconds', type=float, default=10.0, help='CPU baseline sample budget')
+    args = ap.parse_args(argv)
+    if args.warmup < 3:
+        ap.error('--warmup must be at least 3')
+    if args.scaling is None:
+        args.scaling = 'strong' if args.workload.startswith('config5') else 'weak'
+    return args
+
+
+def measured_peaks():
+    path = ROOT / 'MEASURED_PEAKS.json'
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {'hbm_gbs': float(data['hbm_gbs']), 'bf16_tflops': float(data.get('bf16_tflops', 0))}, 'measured'
+    return dict(FALLBACK_PEAKS), 'fallback'
+
+
+def recorded_traffic(workload):
+    """DRAM bytes per launch of the dominant kernel, from a committed ncu summary."""
+    path = ROOT / 'profiles' / 'traffic.json'
+    if not path.exists():
+        return None
+    entry = json.loads(path.read_text()).get(workload)
+    return None if entry is None else entry.get('dram_bytes_per_launch')
+
+
+class ClockSampler:
+    """Samples SM clock, power and clock-event reasons through NVML (read only)."""
+    REASONS = {
+        'hw_slowdown': 'nvmlClocksEventReasonHwSlowdown',
+        'hw_thermal_slowdown': 'nvmlClocksEventReasonHwThermalSlowdown',
+        'sw_thermal_slowdown': 'nvmlClocksEventReasonSwThermalSlowdown',
+        'sw_power_cap': 'nvmlClocksEventReasonSwPowerCap',
+        'hw_power_brake_slowdown': 'nvmlClocksEventReasonHwPowerBrakeSlowdown',
+    }
+
+    def __init__(self, device_index, period=0.005):
+        self.period = period
+        self.samples = []
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nvml = pynvml
+            # NVML enumerates physical GPUs; map through CUDA_VISIBLE_DEVICES if set.
+            visible = os.environ.get('CUDA_VISIBLE_DEVICES')
+            index = device_index
+            if visible:
+                ids = [v.strip() for v in visible.split(',') if v.strip()]
+                if device_index < len(ids) and ids[device_index].isdigit():
+                    index = int(ids[device_index])
+            self.handle = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
+        except Exception as exc:  # no NVML: report why instead of clocks
+            self.nvml = None
+            self.error = str(exc)
+
+    def _run(self):
+        n = self.nvml
+        while not self._stop.is_set():
+            try:
+                sm = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+                reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+                power = n.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
+                self.samples.append((sm, reasons, power))
+            except Exception:
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self):
+        if self.nvml is None:
+            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': [], 'error': self.error}
+        if not self.samples:
+            return {'sm_mhz': None, 'sm_max_mhz': self.max_mhz, 'reasons': [], 'samples': 0}
+        active = set()
+        for _, mask, _ in self.samples:
+            for name, const in self.REASONS.items():
+                if mask & getattr(self.nvml, const):
+                    active.add(name)
+        return {'sm_mhz': statistics.median(s[0] for s in self.samples), 'sm_max_mhz': self.max_mhz,
+                'reasons': sorted(active), 'samples': len(self.samples),
+                'power_w_max': max(s[2] for s in self.samples)}
+
+
+def dist_setup():
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local = int(os.environ.get('LOCAL_RANK', '0'))
+    return rank, world, local
+
+
+def barrier():
+    import torch.distributed as dist
+    if dist.is_available() and dist.is_initialized():
+        dist.barrier()
+
+
+def workload_host(name, images_first, images_count):
+    """Host arrays (x for images [first, first+count), w) of a workload."""
+    from groupconv_atlas_b200 import workloads
+    wl = workloads.by_name(name, with_x=False)
+    x = workloads.images(wl.shape, wl.seed, wl.dist, images_first, images_count)
+    return wl, x, wl.w
+
+
+# ---------------------------------------------------------------------------------------
+# The reference arm: the reference's CPU implementation on the host cores.
+# ---------------------------------------------------------------------------------------
+def cpu_reference_runner(shape, x, w):
+    """Returns (run(out), kind, cores): the reference library compiled from the
+    reference's sources (kind 'reference') or the oracle's C restatement of it
+    (kind 'port'), GC_BLOCKED schedule on every host thread."""
+    from oracle import oracle as orc
+    cores = os.cpu_count() or 1
+    if orc.reference_available():
+        return (lambda out: orc.reference_conv(shape, x, w, impl=2, threads=cores, out=out)), 'reference', cores
+    return (lambda out: orc.conv_f32_blocked(shape, x, w, threads=cores)), 'port', cores
+
+
+def sample_images(name, total_images, budget_s):
+    """Largest image count (<= total) whose one blocked CPU pass stays within
+    budget_s, measured on one image."""
+    wl, x1, w = workload_host(name, 0, 1)
+    import dataclasses
+    one = dataclasses.replace(wl.shape, n=1)
+    run, _, _ = cpu_reference_runner(one, x1, w)
+    out = np.empty(one.output, np.float32)
+    run(out)
+    t0 = time.perf_counter()
+    run(out)
+    per_image = max(time.perf_counter() - t0, 1e-6)
+    return int(max(1, min(total_images, budget_s // per_image or 1)))
+
+
+def cpu_baseline(name, images_total, seconds):
+    """Times the reference CPU implementation on a bounded sample of the workload."""
+    import dataclasses
+    m = sample_images(name, images_total, seconds / 4)
+    wl, x, w = workload_host(name, 0, m)
+    shape = dataclasses.replace(wl.shape, n=m)
+    run, kind, cores = cpu_reference_runner(shape, x, w)
+    out = np.empty(shape.output, np.float32)
+    run(out)  # warm-up
+    passes, t0 = 0, time.perf_counter()
+    while True:
+        run(out)
+        passes += 1
+        elapsed = time.perf_counter() - t0
+        if elapsed >= seconds or passes >= 200:
+            break
+    bytes_per_pass = 4 * (math.prod(shape.input) + math.prod(shape.weight) + math.prod(shape.output))
+    return {'value': bytes_per_pass * passes / elapsed / 1e9, 'unit': UNIT, 'cores': cores, 'kind': kind,
+            'sample': f'{m} of {images_total} images x {passes} passes ({elapsed:.1f} s), GC_BLOCKED, '
+                      f'{cores} threads'}
+
+
+def run_reference(args):
+    rank, world, _ = dist_setup()
+    if rank != 0:
+        return 0  # the CPU reference runs on rank 0 only
+    import dataclasses
+    from groupconv_atlas_b200 import workloads
+    wl = workloads.by_name(args.workload, with_x=False)
+    m = sample_images(args.workload, wl.shape.n, 0.25)
+    wl, x, w = workload_host(args.workload, 0, m)
+    shape = dataclasses.replace(wl.shape, n=m)
+    run, kind, cores = cpu_reference_runner(shape, x, w)
+    out = np.empty(shape.output, np.float32)
+    for _ in range(args.warmup):
+        run(out)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        run(out)
+    elapsed = time.perf_counter() - t0
+    step_bytes = 4 * (math.prod(shape.input) + math.prod(shape.weight) + math.prod(shape.output))
+    step_flops = 2 * math.prod(shape.output) * shape.cpg * 9
+    value = step_bytes * args.steps / elapsed / 1e9
+    line = {'impl': 'reference', 'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': args.gpus,
+            'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': elapsed / args.steps * 1e3,
+            'higher_is_better': True, 'scaling': args.scaling, 'vs_baseline': None, 'dtype': 'f32',
+            'data': 'synthetic (seeded, per-image generators)',
+            'gflops': step_flops * args.steps / elapsed / 1e9,
+            'config': {'workload': args.workload, 'shape': dataclasses.asdict(wl.shape),
+                       'step': f'{m} images of the batch per step'},
+            'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': cores, 'kind': kind,
+                             'sample': f'{m} images per step, GC_BLOCKED, {cores} threads'},
+            'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------------------
+# Our arm.
+# ---------------------------------------------------------------------------------------
+class Call:
+    """Pre-built C ABI arguments of one gc_cuda_conv call (descriptors built once)."""
+
+    def __init__(self, native, shape, x, w, y, stream, impl=3):
+        from groupconv_atlas_b200.api import cshape, tensor
+        self.fn = native.lib.gc_cuda_conv
+        self.native = native
+        self.p, self.xd, self.wd, self.yd = cshape(shape), tensor(x), tensor(w), tensor(y)
+        self.args = (ct.byref(self.p), ct.byref(self.xd), ct.byref(self.wd), ct.byref(self.yd), impl,
+                     ct.c_void_p(stream))
+
+    def __call__(self):
+        status = self.fn(*self.args)
+        if status:
+            self.native.check(status)
+
+
+def run_ours(args):
+    import dataclasses
+    import torch
+    import torch.distributed as dist
+    from groupconv_atlas_b200 import api, shard, workloads
+    from oracle import oracle as orc
+
+    rank, world, local = dist_setup()
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device('cuda', local))
+    native = api.Native()
+    full = workloads.by_name(args.workload, with_x=False)
+    if args.scaling == 'weak':
+        units = [shard.Unit(0, full.shape.n, 0, full.shape.cin)]
+        first_image = rank * full.shape.n  # each rank: its own batch of the same shape
+        job_images = full.shape.n * world
+    else:
+        units = shard.units_for_rank(full.shape, world, rank)
+        first_image = units[0].n0 if units else 0
+        job_images = full.shape.n
+    n_images = sum(u.images() for u in units) if args.scaling == 'strong' else full.shape.n
+    local_shape = dataclasses.replace(full.shape, n=max(1, units[-1].n1 - units[0].n0) if args.scaling == 'strong'
+                                      else full.shape.n)
+    # Host data of this rank's images (pinned), weights.
+    x_host = workloads.images(full.shape, full.seed, full.dist, first_image, local_shape.n)
+    w_host = full.w
+    xh = torch.from_numpy(x_host).pin_memory()
+    wh = torch.from_numpy(w_host).pin_memory()
+    set_bytes = 4 * (math.prod(local_shape.input) + math.prod(local_shape.output))
+    sets = int(min(4096, max(1, math.ceil(3 * L2_BYTES / set_bytes))))
+    stream = torch.cuda.Stream()
+    dw = wh.to('cuda')
+    xs = [xh.to('cuda') for _ in range(sets)]
+    ys = [torch.empty(local_shape.output, device='cuda') for _ in range(sets)]
+    torch.cuda.synchronize()
+
+    def unit_views(xt, yt):
+        out = []
+        for u in units if args.scaling == 'strong' else [shard.Unit(0, local_shape.n, 0, local_shape.cin)]:
+            if args.scaling == 'strong':
+                u = shard.Unit(u.n0 - units[0].n0, u.n1 - units[0].n0, u.c0, u.c1)
+            sub = u.shape(local_shape)
+            ox, ow, oy = u.offsets(local_shape)
+            xv = xt.view(-1)[ox:ox + math.prod(sub.input)].view(sub.input)
+            wv = dw.view(-1)[ow:ow + math.prod(sub.weight)].view(sub.weight)
+            yv = yt.view(-1)[oy:oy + math.prod(sub.output)].view(sub.output)
+            out.append((sub, xv, wv, yv))
+        return out
+
+    calls = [[Call(native, sub, xv, wv, yv, stream.cuda_stream) for sub, xv, wv, yv in unit_views(xs[i], ys[i])]
+             for i in range(sets)]
+    launches_per_step = len(calls[0])
+    step_bytes = sum(4 * (math.prod(s.input) + math.prod(s.weight) + math.prod(s.output))
+                     for s, *_ in unit_views(xs[0], ys[0]))
+    step_flops = sum(2 * math.prod(s.output) * s.cpg * 9 for s, *_ in unit_views(xs[0], ys[0]))
+
+    # Correctness gate before timing: 64 FP64 points of this rank's output.
+    with torch.cuda.stream(stream):
+        for c in calls[0]:
+            c()
+    plan = native.last_plan()
+    stream.synchronize()
+    y0 = ys[0].cpu().numpy()
+    check = orc.check_points(local_shape, x_host, w_host, y0)
+    if not check['passed']:
+        raise SystemExit(f'correctness gate failed on rank {rank}: {check["failed_points"]} points [{plan}]')
+    if native.device_status(clear=True):
+        raise SystemExit('device status word set after the correctness gate')
+
+    # Device-timed region: K back-to-back steps, events around every step.
+    with torch.cuda.stream(stream):
+        for k in range(args.warmup):
+            for c in calls[k % sets]:
+                c()
+    stream.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    region0, region1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    with sampler, torch.cuda.stream(stream):
+        region0.record(stream)
+        for k in range(args.steps):
+            starts[k].record(stream)
+            for c in calls[k % sets]:
+                c()
+            ends[k].record(stream)
+        region1.record(stream)
+        stream.synchronize()
+    torch.cuda.synchronize()
+    barrier()
+    elapsed_ms = region0.elapsed_time(region1)
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    kernel_ms = statistics.fmean(step_ms) / launches_per_step
+    max_elapsed = shard.max_over_ranks(elapsed_ms)
+    job_bytes = shard.sum_over_ranks(step_bytes)
+    job_flops = shard.sum_over_ranks(step_flops)
+    value = job_bytes * args.steps / (max_elapsed / 1e3) / 1e9
+    gflops = job_flops * args.steps / (max_elapsed / 1e3) / 1e9
+
+    # End to end through the C ABI: pinned host batch -> device -> conv -> host,
+    # pipelined in chunks over three streams, copies inside the timed region.
+    e2e = None
+    if not args.no_e2e:
+        e2e = end_to_end(args, native, local_shape, units, xh, wh, torch, api, shard)
+
+    cudnn = None
+    if not args.no_cudnn and rank == 0:
+        cudnn = cudnn_baseline(args, torch, local_shape, xs, dw, sets, kernel_ms * launches_per_step)
+
+    cpu = None
+    if not args.no_cpu_baseline and rank == 0 and world == 1:
+        cpu = cpu_baseline(args.workload, local_shape.n, args.cpu_seconds)
+
+    status = native.device_status(clear=True)
+    if status:
+        raise SystemExit(f'device status word set during timing: {status:#x}')
+    peaks, peak_kind = measured_peaks()
+    achieved = (step_bytes / launches_per_step) / (kernel_ms / 1e3) / 1e9
+    traffic = recorded_traffic(args.workload)
+    clocks = sampler.summary()
+    if world > 1:
+        import torch.distributed as dist
+        gathered = [None] * world
+        dist.all_gather_object(gathered, clocks)
+        clocks = gathered[0] | {'per_rank_reasons': [g.get('reasons') for g in gathered]}
+    if rank == 0:
+        line = {
+            'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
+            'warmup': args.warmup, 'ms_per_step': max_elapsed / args.steps, 'higher_is_better': True,
+            'scaling': args.scaling, 'vs_baseline': None, 'dtype': 'f32',
+            'data': 'synthetic (seeded per-image generators, distributions of the workload definition)',
+            'gflops': gflops,
+            'config': {'workload': args.workload, 'shape': dataclasses.asdict(full.shape),
+                       'images_per_step': job_images, 'implementation': 3, 'kernel_plan': plan,
+                       'l2': f'{sets} rotating input/output sets per rank, {sets * set_bytes / 2**20:.0f} MiB '
+                             f'> L2 {L2_BYTES / 2**20:.0f} MiB',
+                       'parallelism': f'{args.scaling} batch sharding over {world} GPU(s), no collective'},
+            'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peaks['hbm_gbs'], 'unit': 'GB/s',
+                         'frac': achieved / peaks['hbm_gbs'], 'traffic': traffic,
+                         'peak_source': peak_kind, 'kernel_ms': kernel_ms,
+                         'algorithmic_bytes_per_launch': step_bytes / launches_per_step,
+                         'fp32_tflops': (step_flops / launches_per_step) / (kernel_ms / 1e3) / 1e12},
+            'e2e': e2e, 'gpu_launches': args.steps * launches_per_step, 'clocks': clocks,
+            'cudnn': cudnn, 'cpu_baseline': cpu,
+        }
+        print(json.dumps(line), flush=True)
+    del calls
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def end_to_end(args, native, shape, units, xh, wh, torch, api, shard):
+    """Same metric, through the C ABI with host buffers: per step the batch is
+    copied host->device in chunks (pinned), convolved chunk by chunk as soon
+    as its copy lands, and copied back; three streams overlap the two copy
+    directions with compute."""
+    import dataclasses
+    n = shape.n
+    chunks = max(1, min(8, n))
+    bounds = [(i * n // chunks, (i + 1) * n // chunks) for i in range(chunks)]
+    bounds = [b for b in bounds if b[1] > b[0]]
+    dx = torch.empty(shape.input, device='cuda')
+    dw = torch.empty(shape.weight, device='cuda')
+    dy = torch.empty(shape.output, device='cuda')
+    yh = torch.empty(shape.output, pin_memory=True)
+    s_in, s_cmp, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
+    calls = []
+    for lo, hi in bounds:
+        sub = dataclasses.replace(shape, n=hi - lo)
+        calls.append(Call(native, sub, dx[lo:hi], dw, dy[lo:hi], s_cmp.cuda_stream))
+    ev_in = [torch.cuda.Event() for _ in bounds]
+    ev_cmp = [torch.cuda.Event() for _ in bounds]
+    ev_out = [torch.cuda.Event() for _ in bounds]
+
+    def step(first):
+        with torch.cuda.stream(s_in):
+            dw.copy_(wh, non_blocking=True)
+            for j, (lo, hi) in enumerate(bounds):
+                if not first:
+                    s_in.wait_event(ev_cmp[j])  # previous step finished reading dx chunk
+                dx[lo:hi].copy_(xh[lo:hi], non_blocking=True)
+                ev_in[j].record(s_in)
+        for j in range(len(bounds)):
+            s_cmp.wait_event(ev_in[j])
+            if not first:
+                s_cmp.wait_event(ev_out[j])  # previous step finished reading dy chunk
+            calls[j]()
+            ev_cmp[j].record(s_cmp)
+        with torch.cuda.stream(s_out):
+            for j, (lo, hi) in enumerate(bounds):
+                s_out.wait_event(ev_cmp[j])
+                yh[lo:hi].copy_(dy[lo:hi], non_blocking=True)
+                ev_out[j].record(s_out)
+
+    for i in range(3):
+        step(i == 0)
+    torch.cuda.synchronize()
+    barrier()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(s_in)
+    for _ in range(args.e2e_steps):
+        step(False)
+    t1.record(s_out)
+    torch.cuda.synchronize()
+    barrier()
+    ms = shard.max_over_ranks(t0.elapsed_time(t1))
+    step_bytes = 4 * (math.prod(shape.input) + math.prod(shape.weight) + math.prod(shape.output))
+    job_bytes = shard.sum_over_ranks(step_bytes)
+    return {'value': job_bytes * args.e2e_steps / (ms / 1e3) / 1e9, 'unit': UNIT,
+            'h2d_bytes_per_step': 4 * (math.prod(shape.input) + math.prod(shape.weight)),
+            'd2h_bytes_per_step': 4 * math.prod(shape.output), 'steps': args.e2e_steps,
+            'ms_per_step': ms / args.e2e_steps, 'chunks': len(bounds),
+            'path': 'pinned host -> gc_cuda_conv per chunk (C ABI via ctypes) -> pinned host'}
+
+
+def cudnn_baseline(args, torch, shape, xs, dw, sets, our_step_ms):
+    """torch.nn.functional.conv2d on the same device buffers: TF32 off and read
+    back, cudnn.benchmark on, device time of back-to-back calls."""
+    import torch.nn.functional as F
+    if hasattr(torch.backends, 'fp32_precision'):
+        for target in (torch.backends, torch.backends.cuda.matmul, torch.backends.cudnn,
+                       torch.backends.cudnn.conv):
+            target.fp32_precision = 'ieee'
+        tf32 = torch.backends.cudnn.conv.fp32_precision != 'ieee'
+    else:
+        torch.backends.cuda.matmul.allow_tf32 = False
+        torch.backends.cudnn.allow_tf32 = False
+        tf32 = torch.backends.cudnn.allow_tf32
+    if tf32:
+        raise SystemExit('could not disable TF32 for the cuDNN baseline')
+    torch.backends.cudnn.benchmark = True
+    stream = torch.cuda.Stream()
+    steps = max(20, min(args.steps, 500))
+    with torch.inference_mode(), torch.cuda.stream(stream):
+        for k in range(10):
+            F.conv2d(xs[k % sets], dw, padding=1, groups=shape.groups)
+        stream.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for k in range(steps):
+            F.conv2d(xs[k % sets], dw, padding=1, groups=shape.groups)
+        b.record(stream)
+        stream.synchronize()
+    ms = a.elapsed_time(b) / steps
+    return {'ms_per_step': ms, 'ours_ms_per_step': our_step_ms, 'speedup_vs_cudnn': ms / our_step_ms,
+            'api': 'torch.nn.functional.conv2d', 'tf32': False, 'benchmark': True,
+            'cudnn_version': torch.backends.cudnn.version()}
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    if args.impl == 'reference':
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == '__main__':
+    raise SystemExit(main())

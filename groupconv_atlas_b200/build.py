@@ -1,0 +1,91 @@
+"""Build recipe for the in-tree drop-in library ``libgroupconv.so``.
+
+One nvcc invocation compiles the C ABI (``csrc/common.cpp``) and the sm_100a
+CUDA engine (``csrc/conv_cuda.cu``) into a shared library that sits next to
+this file.  The CUDA runtime is linked as a shared library so that, inside a
+process that already loaded PyTorch's CUDA runtime, both use one runtime
+instance (one current device per thread, one primary context).
+
+    python -m groupconv_atlas_b200.build          # build if stale
+    python -m groupconv_atlas_b200.build --force  # always rebuild
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PACKAGE = Path(__file__).resolve().parent
+ROOT = PACKAGE.parent
+CSRC = PACKAGE / 'csrc'
+INCLUDE = ROOT / 'include'
+LIBRARY = PACKAGE / 'libgroupconv.so'
+ARCH = ['-gencode', 'arch=compute_100a,code=sm_100a']
+
+
+def nvcc() -> str:
+    for candidate in (os.environ.get('NVCC'), '/usr/local/cuda/bin/nvcc', shutil.which('nvcc')):
+        if candidate and Path(candidate).exists():
+            return candidate
+    raise FileNotFoundError('nvcc not found: the B200 library needs the CUDA 12.9 toolkit')
+
+
+def sources() -> list[Path]:
+    return sorted(CSRC.glob('*.cu')) + sorted(CSRC.glob('*.cpp'))
+
+
+def dependencies() -> list[Path]:
+    return sources() + sorted(CSRC.glob('*.cuh')) + sorted(CSRC.glob('*.h')) + [INCLUDE / 'groupconv.h', Path(__file__)]
+
+
+def stale(target: Path = LIBRARY) -> bool:
+    if not target.exists():
+        return True
+    built = target.stat().st_mtime
+    return any(p.stat().st_mtime > built for p in dependencies())
+
+
+def command(output: Path = LIBRARY, extra: list[str] | None = None) -> list[str]:
+    cuda_lib = Path(nvcc()).resolve().parent.parent / 'lib64'
+    return [nvcc(), *ARCH, '-O3', '-lineinfo', '-std=c++17', '-shared',
+            '-Xcompiler', '-fPIC,-Wall', '-Xptxas', '-warn-spills',
+            '-cudart', 'shared', f'-I{INCLUDE}', f'-I{CSRC}',
+            f'-Xlinker', f'-rpath,{cuda_lib}',
+            *(extra or []), '-o', str(output), *map(str, sources())]
+
+
+def build(force: bool = False, verbose: bool = False, extra: list[str] | None = None) -> Path:
+    """Compile the library when a source is newer than it (or when forced)."""
+    if not force and not stale():
+        return LIBRARY
+    tmp = LIBRARY.with_suffix('.so.part')
+    cmd = command(tmp, extra)
+    if verbose:
+        print(' '.join(cmd), flush=True)
+    result = subprocess.run(cmd, capture_output=True, text=True)
+    if result.returncode != 0:
+        sys.stderr.write(result.stdout + result.stderr)
+        raise RuntimeError(f'nvcc failed with exit code {result.returncode}')
+    if verbose and (result.stdout or result.stderr):
+        sys.stderr.write(result.stdout + result.stderr)
+    tmp.replace(LIBRARY)
+    return LIBRARY
+
+
+def main(argv=None) -> int:
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument('--force', action='store_true')
+    parser.add_argument('--verbose', action='store_true')
+    parser.add_argument('--ptxas-info', action='store_true', help='print registers/spills per kernel')
+    args = parser.parse_args(argv)
+    extra = ['-Xptxas', '-v'] if args.ptxas_info else None
+    path = build(force=args.force or args.ptxas_info, verbose=args.verbose or args.ptxas_info, extra=extra)
+    print(path)
+    return 0
+
+
+if __name__ == '__main__':
+    raise SystemExit(main())

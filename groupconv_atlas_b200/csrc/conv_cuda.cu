@@ -1,0 +1,683 @@
+// CUDA backend of the C ABI: gc_cuda_conv (reference csrc/cuda/groupconv.cu:
+// 156-222 contract) and the gc_b200_* extensions.
+//
+// Call path: validate descriptors (common.cpp) -> support matrix of the
+// requested implementation -> pointer and stream checks -> plan (cached per
+// shape) -> one kernel launch on the caller's stream -> cudaGetLastError.
+// Nothing here allocates memory or synchronizes; the TMA descriptor is built
+// on the host and passed as a __grid_constant__ kernel parameter, so a call
+// can be captured into a CUDA graph.
+#include "groupconv.h"
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "device_util.cuh"
+#include "kernel_direct.cuh"
+#include "kernel_general.cuh"
+#include "kernel_wide.cuh"
+
+namespace {
+
+using gcb::DirectParams;
+using gcb::GeneralParams;
+
+constexpr int kStages = 3;
+
+thread_local std::string g_plan;
+
+long long round_up(long long v, long long m) { return (v + m - 1) / m * m; }
+long long ceil_div(long long a, long long b) { return (a + b - 1) / b; }
+
+// ---- device facts, cached per device -----------------------------------------
+struct DeviceFacts {
+    int sms = 0;
+    int smem_optin = 0;   // max dynamic shared memory per block (opt-in)
+    int smem_per_sm = 0;  // shared memory per multiprocessor
+};
+
+std::mutex g_mutex;
+std::map<int, DeviceFacts> g_facts;
+std::map<std::pair<int, const void *>, bool> g_attr_done;
+std::map<std::tuple<int, const void *, int, size_t>, int> g_occupancy;
+
+int device_facts(int dev, DeviceFacts &out) {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    auto it = g_facts.find(dev);
+    if (it != g_facts.end()) {
+        out = it->second;
+        return GC_OK;
+    }
+    DeviceFacts f;
+    cudaError_t e = cudaDeviceGetAttribute(&f.sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e == cudaSuccess)
+        e = cudaDeviceGetAttribute(&f.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e == cudaSuccess)
+        e = cudaDeviceGetAttribute(&f.smem_per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
+    if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+    g_facts[dev] = f;
+    out = f;
+    return GC_OK;
+}
+
+// Opt a kernel into the device's full dynamic shared memory once, then ask
+// the occupancy calculator (cached) how many CTAs fit per SM.
+int kernel_occupancy(int dev, const void *fn, int threads, size_t smem, int smem_optin,
+                     int &ctas) {
+    std::lock_guard<std::mutex> lock(g_mutex);
+    auto key = std::make_tuple(dev, fn, threads, smem);
+    auto it = g_occupancy.find(key);
+    if (it != g_occupancy.end()) {
+        ctas = it->second;
+        return GC_OK;
+    }
+    auto akey = std::make_pair(dev, fn);
+    if (!g_attr_done[akey]) {
+        cudaError_t e =
+            cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_optin);
+        if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+        g_attr_done[akey] = true;
+    }
+    int n = 0;
+    cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, fn, threads, smem);
+    if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+    g_occupancy[key] = n;
+    ctas = n;
+    return GC_OK;
+}
+
+// ---- TMA descriptor encoding ---------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+cudaError_t g_encode_error = cudaSuccess;
+
+int tensor_map_encoder(PFN_cuTensorMapEncodeTiled_v12000 &fn) {
+    std::call_once(g_encode_once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        g_encode_error =
+            cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q);
+        if (g_encode_error == cudaSuccess && q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    if (g_encode == nullptr) {
+        const char *why = g_encode_error != cudaSuccess ? cudaGetErrorString(g_encode_error)
+                                                        : "cuTensorMapEncodeTiled not found";
+        return gc_error(GC_DEVICE_ERROR, why);
+    }
+    fn = g_encode;
+    return GC_OK;
+}
+
+// 4-D map over an NCHW float tensor: dims (W, H, C, N), box (bw, bh, bc, 1),
+// out-of-range elements read as zero.
+int encode_nchw_map(CUtensorMap &map, const float *base, long long n, long long c, long long h,
+                    long long w, int bw, int bh, int bc) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode;
+    int st = tensor_map_encoder(encode);
+    if (st != GC_OK) return st;
+    cuuint64_t dims[4] = {static_cast<cuuint64_t>(w), static_cast<cuuint64_t>(h),
+                          static_cast<cuuint64_t>(c), static_cast<cuuint64_t>(n)};
+    cuuint64_t strides[3] = {static_cast<cuuint64_t>(w) * 4, static_cast<cuuint64_t>(h * w) * 4,
+                             static_cast<cuuint64_t>(c * h * w) * 4};
+    cuuint32_t box[4] = {static_cast<cuuint32_t>(bw), static_cast<cuuint32_t>(bh),
+                         static_cast<cuuint32_t>(bc), 1u};
+    cuuint32_t estride[4] = {1, 1, 1, 1};
+    CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float *>(base), dims,
+                        strides, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return gc_error(GC_DEVICE_ERROR, "cuTensorMapEncodeTiled failed");
+    return GC_OK;
+}
+
+// ---- direct engines: variants, planning, launch ----------------------------------
+struct Variant {
+    const char *name;
+    int cob, vr;
+    const void *fn_tma;
+    const void *fn_ldg;
+};
+
+template <int CPG, int COB, int VR>
+Variant make_variant(const char *name) {
+    return Variant{name, COB, VR,
+                   reinterpret_cast<const void *>(&gcb::direct_conv_kernel<CPG, COB, VR, true, kStages>),
+                   reinterpret_cast<const void *>(&gcb::direct_conv_kernel<CPG, COB, VR, false, kStages>)};
+}
+
+template <int COB, int VR>
+Variant make_wide(const char *name) {
+    return Variant{name, COB, VR,
+                   reinterpret_cast<const void *>(&gcb::wide_conv_kernel<COB, VR, true, kStages>),
+                   reinterpret_cast<const void *>(&gcb::wide_conv_kernel<COB, VR, false, kStages>)};
+}
+
+// Full-group kernel variant for small groups.
+const Variant &small_variant(long long cpg) {
+    static const Variant d1 = make_variant<1, 1, 4>("d1");
+    static const Variant d2 = make_variant<2, 2, 4>("d2");
+    static const Variant d4 = make_variant<4, 4, 4>("d4");
+    static const Variant d8 = make_variant<8, 8, 2>("d8");
+    static const Variant gen = make_variant<0, 1, 4>("g1");
+    if (cpg == 1) return d1;
+    if (cpg == 2) return d2;
+    if (cpg == 4) return d4;
+    if (cpg == 8) return d8;
+    return gen;
+}
+
+// Channel-chunked kernel variant for wide groups.
+const Variant &wide_variant(long long cpg) {
+    static const Variant w8 = make_wide<8, 2>("w8");
+    static const Variant w4 = make_wide<4, 2>("w4");
+    static const Variant w1 = make_wide<1, 4>("w1");
+    if (cpg % 8 == 0) return w8;
+    if (cpg % 4 == 0) return w4;
+    return w1;
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Whether the TMA staging can serve this shape and this input pointer.
+bool tma_eligible(const gc_shape *p, const void *x) {
+    return p->w % 4 == 0 && p->w + 8 <= 256 && aligned16(x) && p->h < (1ll << 30) &&
+           p->cin < (1ll << 30) && p->n < (1ll << 30);
+}
+
+// Everything a launch needs except the three data pointers.
+struct EnginePlan {
+    bool wide = false;
+    const Variant *var = nullptr;
+    bool tma = false;
+    int threads = 0;
+    size_t smem = 0;
+    int grid = 0;
+    int ctas_per_sm = 0;
+    DirectParams D;  // valid when !wide
+    gcb::WideParams Wp;  // valid when wide
+};
+
+// Shared scoring of a candidate tiling: load balance of the persistent grid,
+// thread utilisation, the input re-read factor (halo rows, output-channel
+// blocks) and the latency-hiding capacity of the SM.
+double score_tiling(long long items, long long slots, long long cells, int threads, double reread,
+                    int ctas, double stage_bytes) {
+    const long long waves = ceil_div(items, slots);
+    const double balance = static_cast<double>(items) / (static_cast<double>(waves) * slots);
+    const double cell_eff = static_cast<double>(cells) / (ceil_div(cells, threads) * threads);
+    double score = balance * cell_eff / (1.0 + 0.15 * (reread - 1.0));
+    const double warps = ctas * threads / 32.0;
+    if (warps < 16) score *= 0.75 + 0.25 * warps / 16.0;
+    const double inflight = ctas * (kStages - 1) * stage_bytes;
+    if (inflight < 48.0 * 1024) score *= 0.8 + 0.2 * inflight / (48.0 * 1024);
+    return score;
+}
+
+const std::vector<long long> band_candidates(long long H) {
+    return {H, ceil_div(H, 2), ceil_div(H, 3), ceil_div(H, 4), ceil_div(H, 7), 64, 32, 28, 16, 14, 8, 4, 2, 1};
+}
+
+// Full-group tiling (kernel_direct.cuh) for groups of fewer than 16 channels.
+int plan_small(const gc_shape *p, bool tma, bool w_aligned, bool y_aligned, int dev,
+               const DeviceFacts &facts, EnginePlan &out, bool &found) {
+    const long long N = p->n, C = p->cin, H = p->h, W = p->w, cpg = p->cin / p->groups;
+    const Variant &var = small_variant(cpg);
+    const int vr = var.vr;
+    const int pitch = round_up((W) + 8, 4);
+    const long long groups = p->groups;
+    double best = -1.0;
+    found = false;
+    for (long long gpi = 1; gpi <= groups; ++gpi) {
+        if (groups % gpi != 0) continue;
+        const long long cb = gpi * cpg;
+        if (cb > std::max<long long>(cpg, 64)) break;
+        for (long long bh : band_candidates(H)) {
+            if (bh < 1 || bh > H) continue;
+            if (bh != H && bh % vr != 0) continue;
+            const long long rows = round_up((bh), vr) + 2;
+            if (tma && (rows > 256 || cb > 256)) continue;
+            const long long xf = round_up((cb * rows * pitch), 32);
+            const long long wf = round_up((cb * cpg * 9), 32);
+            const long long wtf = cpg == 1 ? 0 : wf;
+            const size_t smem = static_cast<size_t>((kStages * (xf + wf) + wtf) * 4 + 64);
+            if (smem > static_cast<size_t>(facts.smem_optin)) continue;
+            const long long bands = ceil_div(H, bh);
+            const long long items = N * (C / cb) * bands;
+            const long long cells = (cb / var.cob) * ceil_div(bh, vr) * ceil_div(W, 4);
+            for (int threads : {128, 256}) {
+                int ctas = 0;
+                int st = kernel_occupancy(dev, tma ? var.fn_tma : var.fn_ldg, threads, smem,
+                                          facts.smem_optin, ctas);
+                if (st != GC_OK) return st;
+                if (ctas < 1) continue;
+                const long long slots = static_cast<long long>(facts.sms) * ctas;
+                const double score = score_tiling(items, slots, cells, threads,
+                                                  static_cast<double>(rows) / bh, ctas, (xf + wf) * 4.0);
+                if (score <= best + 1e-9) continue;
+                best = score;
+                found = true;
+                DirectParams &P = out.D;
+                std::memset(&P, 0, sizeof(P));
+                P.n = static_cast<int>(N);
+                P.c = static_cast<int>(C);
+                P.h = static_cast<int>(H);
+                P.wd = static_cast<int>(W);
+                P.cpg = static_cast<int>(cpg);
+                P.cb = static_cast<int>(cb);
+                P.bh = static_cast<int>(bh);
+                P.bands = static_cast<int>(bands);
+                P.cblocks = static_cast<int>(C / cb);
+                P.items = items;
+                P.pitch = pitch;
+                P.rows = static_cast<int>(rows);
+                P.x_floats = static_cast<int>(xf);
+                P.wraw_floats = static_cast<int>(wf);
+                P.stage_floats = static_cast<int>(xf + wf);
+                P.wt_floats = static_cast<int>(wtf);
+                P.qcols = static_cast<int>(ceil_div(W, 4));
+                P.rblocks = static_cast<int>(ceil_div(bh, vr));
+                P.cells = static_cast<int>(cells);
+                P.vec_store = (W % 4 == 0 && y_aligned) ? 1 : 0;
+                P.bulk_w = (tma && w_aligned && (cb * cpg) % 4 == 0) ? 1 : 0;
+                P.x_bytes = static_cast<unsigned>(pitch * rows * cb * 4);
+                P.w_bytes = static_cast<unsigned>(cb * cpg * 9 * 4);
+                out.wide = false;
+                out.var = &var;
+                out.tma = tma;
+                out.threads = threads;
+                out.smem = smem;
+                out.ctas_per_sm = ctas;
+                out.grid = static_cast<int>(std::min<long long>(items, slots));
+            }
+        }
+    }
+    return GC_OK;
+}
+
+// Channel-chunked tiling (kernel_wide.cuh): any group width.
+int plan_wide(const gc_shape *p, bool tma, bool y_aligned, int dev, const DeviceFacts &facts,
+              EnginePlan &out, bool &found) {
+    const long long N = p->n, C = p->cin, H = p->h, W = p->w, cpg = p->cin / p->groups;
+    const Variant &var = wide_variant(cpg);
+    const int vr = var.vr, cob = var.cob;
+    const int pitch = round_up((W) + 8, 4);
+    const long long qcols = ceil_div(W, 4);
+    const size_t budget = std::min<size_t>(static_cast<size_t>(facts.smem_optin), 112 * 1024);
+    double best = -1.0;
+    found = false;
+    for (int threads : {256, 128}) {
+        for (long long co_item = cob; co_item < cpg + cob; co_item += cob) {
+            const long long coblocks = ceil_div(cpg, co_item);
+            for (long long bh : band_candidates(H)) {
+                if (bh < 1 || bh > H) continue;
+                if (bh != H && bh % vr != 0) continue;
+                const long long cells = (co_item / cob) * ceil_div(bh, vr) * qcols;
+                if (cells > threads) continue;
+                const long long rows = round_up((bh), vr) + 2;
+                if (tma && rows > 256) continue;
+                const long long row_floats = rows * pitch;
+                // Largest chunk whose stages fit the budget, at most the group.
+                long long kc = std::min<long long>(cpg, 256);
+                while (kc > 1 && kStages * round_up((kc * row_floats), 32) * 4 + 64 >
+                                     static_cast<long long>(budget))
+                    --kc;
+                const long long xf = round_up((kc * row_floats), 32);
+                const size_t smem = static_cast<size_t>(kStages * xf * 4 + 64);
+                if (smem > static_cast<size_t>(facts.smem_optin)) continue;
+                const long long bands = ceil_div(H, bh);
+                const long long items = N * p->groups * bands * coblocks;
+                int ctas = 0;
+                int st = kernel_occupancy(dev, tma ? var.fn_tma : var.fn_ldg, threads, smem,
+                                          facts.smem_optin, ctas);
+                if (st != GC_OK) return st;
+                if (ctas < 1) continue;
+                const long long slots = static_cast<long long>(facts.sms) * ctas;
+                const double reread = static_cast<double>(rows) / bh * coblocks;
+                const double score = score_tiling(items, slots, cells, threads, reread, ctas, xf * 4.0);
+                if (score <= best + 1e-9) continue;
+                best = score;
+                found = true;
+                gcb::WideParams &P = out.Wp;
+                std::memset(&P, 0, sizeof(P));
+                P.n = static_cast<int>(N);
+                P.c = static_cast<int>(C);
+                P.h = static_cast<int>(H);
+                P.wd = static_cast<int>(W);
+                P.cpg = static_cast<int>(cpg);
+                P.groups = static_cast<int>(p->groups);
+                P.kc = static_cast<int>(kc);
+                P.chunks = static_cast<int>(ceil_div(cpg, kc));
+                P.co_item = static_cast<int>(co_item);
+                P.coblocks = static_cast<int>(coblocks);
+                P.bh = static_cast<int>(bh);
+                P.bands = static_cast<int>(bands);
+                P.items = items;
+                P.pitch = pitch;
+                P.rows = static_cast<int>(rows);
+                P.x_floats = static_cast<int>(xf);
+                P.qcols = static_cast<int>(qcols);
+                P.rblocks = static_cast<int>(ceil_div(bh, vr));
+                P.cells = static_cast<int>(cells);
+                P.vec_store = (W % 4 == 0 && y_aligned) ? 1 : 0;
+                P.x_bytes = static_cast<unsigned>(pitch * rows * kc * 4);
+                out.wide = true;
+                out.var = &var;
+                out.tma = tma;
+                out.threads = threads;
+                out.smem = smem;
+                out.ctas_per_sm = ctas;
+                out.grid = static_cast<int>(std::min<long long>(items, slots));
+            }
+        }
+    }
+    return GC_OK;
+}
+
+using PlanKey = std::tuple<int, long long, long long, long long, long long, long long, int>;
+std::map<PlanKey, EnginePlan> g_plans;
+
+// Plan for the direct engines, cached per (device, shape, staging, alignment).
+int plan_engine(const gc_shape *p, const float *w, const float *y, bool tma, int dev,
+                EnginePlan &plan) {
+    const bool w_al = aligned16(w), y_al = aligned16(y);
+    const PlanKey key{dev, p->n, p->cin, p->h, p->w, p->groups,
+                      (tma ? 1 : 0) | (w_al ? 2 : 0) | (y_al ? 4 : 0)};
+    {
+        std::lock_guard<std::mutex> lock(g_mutex);
+        auto it = g_plans.find(key);
+        if (it != g_plans.end()) {
+            plan = it->second;
+            return GC_OK;
+        }
+    }
+    const long long N = p->n, C = p->cin, H = p->h, W = p->w;
+    if (H > (1 << 30) || W > (1 << 20) || C > (1 << 30) || N > (1 << 30))
+        return gc_error(GC_UNSUPPORTED, "direct engine: tensor extent beyond its 32-bit tile indices");
+    DeviceFacts facts;
+    int st = device_facts(dev, facts);
+    if (st != GC_OK) return st;
+    bool found = false;
+    const long long cpg = p->cin / p->groups;
+    if (cpg < 16) {
+        st = plan_small(p, tma, w_al, y_al, dev, facts, plan, found);
+        if (st != GC_OK) return st;
+    }
+    if (!found) {
+        st = plan_wide(p, tma, y_al, dev, facts, plan, found);
+        if (st != GC_OK) return st;
+    }
+    if (!found) return gc_error(GC_UNSUPPORTED, "direct engine: no tile fits in shared memory");
+    std::lock_guard<std::mutex> lock(g_mutex);
+    g_plans[key] = plan;
+    return GC_OK;
+}
+
+int launch_direct(const gc_shape *p, const float *x, const float *w, float *y, bool tma, int dev,
+                  cudaStream_t stream) {
+    EnginePlan plan;
+    int st = plan_engine(p, w, y, tma, dev, plan);
+    if (st != GC_OK) return st;
+    CUtensorMap map;
+    std::memset(&map, 0, sizeof(map));
+    void *args[2];
+    char buf[360];
+    if (!plan.wide) {
+        plan.D.x = x;
+        plan.D.w = w;
+        plan.D.y = y;
+        if (tma) {
+            st = encode_nchw_map(map, x, p->n, p->cin, p->h, p->w, plan.D.pitch, plan.D.rows, plan.D.cb);
+            if (st != GC_OK) return st;
+        }
+        args[0] = &plan.D;
+        std::snprintf(buf, sizeof(buf),
+                      "kernel=direct_%s engine=group variant=%s grid=%d block=%d smem=%zu ctas_per_sm=%d "
+                      "cb=%d bh=%d items=%lld cells=%d pitch=%d rows=%d bulk_w=%d vec_store=%d",
+                      tma ? "tma" : "ldg", plan.var->name, plan.grid, plan.threads, plan.smem,
+                      plan.ctas_per_sm, plan.D.cb, plan.D.bh, plan.D.items, plan.D.cells, plan.D.pitch,
+                      plan.D.rows, plan.D.bulk_w, plan.D.vec_store);
+    } else {
+        plan.Wp.x = x;
+        plan.Wp.w = w;
+        plan.Wp.y = y;
+        if (tma) {
+            st = encode_nchw_map(map, x, p->n, p->cin, p->h, p->w, plan.Wp.pitch, plan.Wp.rows, plan.Wp.kc);
+            if (st != GC_OK) return st;
+        }
+        args[0] = &plan.Wp;
+        std::snprintf(buf, sizeof(buf),
+                      "kernel=direct_%s engine=wide variant=%s grid=%d block=%d smem=%zu ctas_per_sm=%d "
+                      "kc=%d chunks=%d co_item=%d bh=%d items=%lld cells=%d pitch=%d rows=%d vec_store=%d",
+                      tma ? "tma" : "ldg", plan.var->name, plan.grid, plan.threads, plan.smem,
+                      plan.ctas_per_sm, plan.Wp.kc, plan.Wp.chunks, plan.Wp.co_item, plan.Wp.bh,
+                      plan.Wp.items, plan.Wp.cells, plan.Wp.pitch, plan.Wp.rows, plan.Wp.vec_store);
+    }
+    args[1] = &map;
+    const void *fn = tma ? plan.var->fn_tma : plan.var->fn_ldg;
+    cudaError_t e = cudaLaunchKernel(fn, dim3(plan.grid), dim3(plan.threads), args, plan.smem, stream);
+    if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+    g_plan = buf;
+    return GC_OK;
+}
+
+// ---- general kernel ------------------------------------------------------------------
+constexpr int kGeneralRun = 4;
+
+int launch_general(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const float *w,
+                   float *y, int dev, cudaStream_t stream) {
+    DeviceFacts facts;
+    int st = device_facts(dev, facts);
+    if (st != GC_OK) return st;
+    GeneralParams P;
+    P.xp = x;
+    P.wp = w;
+    P.yp = y;
+    P.n = p->n;
+    P.cin = p->cin;
+    P.cout = p->cout;
+    P.h = p->h;
+    P.w = p->w;
+    P.r = p->r;
+    P.s = p->s;
+    P.groups = p->groups;
+    P.sh = p->sh;
+    P.sw = p->sw;
+    P.ph = p->ph;
+    P.pw = p->pw;
+    P.dh = p->dh;
+    P.dw = p->dw;
+    P.ho = ho;
+    P.wo = wo;
+    P.runs_per_row = ceil_div(wo, kGeneralRun);
+    P.total_runs = p->n * p->cout * ho * P.runs_per_row;
+    const int threads = 256;
+    const long long blocks = std::min<long long>(ceil_div(P.total_runs, threads),
+                                                 static_cast<long long>(facts.sms) * 8);
+    gcb::general_conv_kernel<kGeneralRun><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(P);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+    char buf[160];
+    std::snprintf(buf, sizeof(buf), "kernel=general grid=%lld block=%d run=%d runs=%lld", blocks,
+                  threads, kGeneralRun, P.total_runs);
+    g_plan = buf;
+    return GC_OK;
+}
+
+// ---- contract checks shared by both entry points ----------------------------------------
+bool b_geometry(const gc_shape *p) {
+    return p->cin == p->cout && p->r == 3 && p->s == 3 && p->sh == 1 && p->sw == 1 && p->ph == 1 &&
+           p->pw == 1 && p->dh == 1 && p->dw == 1;
+}
+
+// Device memory on the descriptor's device, which must be the current device
+// (reference groupconv.cu:130-139).  Managed and mapped host memory are
+// outside the contract.
+int check_pointer(const gc_tensor *t, int current) {
+    cudaPointerAttributes attr;
+    std::memset(&attr, 0, sizeof(attr));
+    cudaError_t e = cudaPointerGetAttributes(&attr, t->data);
+    if (e != cudaSuccess) {
+        cudaGetLastError();  // the failed query must not poison the next launch check
+        return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+    }
+    if (attr.type != cudaMemoryTypeDevice || attr.device != t->device_index || attr.device != current)
+        return gc_error(GC_INVALID, "CUDA pointer must be device memory on descriptor/current device");
+    return GC_OK;
+}
+
+int device_and_stream_checks(const gc_tensor *x, const gc_tensor *w, const gc_tensor *y,
+                             void *stream, int &current) {
+    cudaError_t e = cudaGetDevice(&current);
+    if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+    for (const gc_tensor *t : {x, w, y}) {
+        int st = check_pointer(t, current);
+        if (st != GC_OK) return st;
+    }
+    // Capture-status lookup validates the handle in eager and captured use
+    // alike (stream-flag queries are rejected during capture).
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    e = cudaStreamIsCapturing(reinterpret_cast<cudaStream_t>(stream), &cs);
+    if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+    return GC_OK;
+}
+
+// Launches one kernel family.  With general_when_no_tile, a B-geometry request
+// whose image is too wide for any shared-memory tile of the direct engines
+// runs on the general kernel instead (the v1 implementations 1-3 support every
+// B-geometry shape); gc_b200_conv asks for one family and gets GC_UNSUPPORTED.
+int run_kernel(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_tensor *y, int kernel,
+               int dev, void *stream, bool general_when_no_tile = false) {
+    int64_t ho = 0, wo = 0;
+    int st = gc_validate_shape(p, &ho, &wo);
+    if (st != GC_OK) return st;
+    const float *xp = static_cast<const float *>(x->data);
+    const float *wp = static_cast<const float *>(w->data);
+    float *yp = static_cast<float *>(y->data);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    switch (kernel) {
+    case GC_B200_GENERAL:
+        st = launch_general(p, ho, wo, xp, wp, yp, dev, s);
+        break;
+    case GC_B200_DIRECT_LDG:
+        st = launch_direct(p, xp, wp, yp, false, dev, s);
+        break;
+    case GC_B200_DIRECT_TMA:
+        st = launch_direct(p, xp, wp, yp, true, dev, s);
+        break;
+    default:
+        return gc_error(GC_UNSUPPORTED, "unknown B200 kernel family");
+    }
+    if (st == GC_UNSUPPORTED && general_when_no_tile && kernel != GC_B200_GENERAL)
+        st = launch_general(p, ho, wo, xp, wp, yp, dev, s);
+    if (st != GC_OK) return st;
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? gc_error(GC_OK, "") : gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+}
+
+// Production choice for B geometry.
+int auto_kernel(const gc_shape *p, const gc_tensor *x) {
+    return tma_eligible(p, x->data) ? GC_B200_DIRECT_TMA : GC_B200_DIRECT_LDG;
+}
+
+__global__ void wait_timeout_selftest_kernel(uint64_t limit_ns) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        gcb::mbar_init(&bar, 1);
+        gcb::fence_barrier_init();
+    }
+    __syncthreads();
+    // Nothing ever arrives on the barrier, so phase 0 never completes.
+    if (threadIdx.x == 0 && !gcb::mbar_wait_bounded(&bar, 0, limit_ns))
+        gcb::raise_status(gcb::kStatusTmaTimeout);
+}
+
+}  // namespace
+
+extern "C" {
+
+int gc_cuda_available(void) {
+    int count = 0;
+    return cudaGetDeviceCount(&count) == cudaSuccess && count > 0;
+}
+
+int gc_cuda_conv(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_tensor *y,
+                 int implementation, void *stream) {
+    int st = gc_validate_tensors(p, x, w, y, GC_CUDA, GC_F32);
+    if (st != GC_OK) return st;
+    if (implementation < 0 || implementation > 3)
+        return gc_error(GC_UNSUPPORTED, "Unknown CUDA implementation");
+    const bool b = b_geometry(p);
+    if (implementation != 0 && !b)
+        return gc_error(GC_UNSUPPORTED, "Optimized CUDA kernels require B geometry");
+    const int64_t cpg = p->cin / p->groups;
+    if (implementation == 2 && cpg != 1 && cpg != 2 && cpg != 4)
+        return gc_error(GC_UNSUPPORTED, "CUDA shared halo supports cpg 1, 2, or 4");
+    int dev = -1;
+    st = device_and_stream_checks(x, w, y, stream, dev);
+    if (st != GC_OK) return st;
+    int kernel = GC_B200_GENERAL;
+    if (implementation == 1) kernel = GC_B200_DIRECT_LDG;
+    if (implementation == 2)
+        kernel = tma_eligible(p, x->data) ? GC_B200_DIRECT_TMA : GC_B200_DIRECT_LDG;
+    if (implementation == 3) kernel = auto_kernel(p, x);
+    return run_kernel(p, x, w, y, kernel, dev, stream, true);
+}
+
+int gc_b200_conv(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_tensor *y,
+                 int kernel, void *stream) {
+    int st = gc_validate_tensors(p, x, w, y, GC_CUDA, GC_F32);
+    if (st != GC_OK) return st;
+    if (kernel < GC_B200_AUTO || kernel > GC_B200_TF32X3)
+        return gc_error(GC_UNSUPPORTED, "unknown B200 kernel family");
+    const bool b = b_geometry(p);
+    if (kernel != GC_B200_GENERAL && kernel != GC_B200_AUTO && !b)
+        return gc_error(GC_UNSUPPORTED, "this kernel family requires 3x3/s1/p1/d1 with Cin == Cout");
+    if (kernel == GC_B200_DIRECT_TMA && !tma_eligible(p, x->data))
+        return gc_error(GC_UNSUPPORTED,
+                        "TMA staging needs width % 4 == 0, width <= 248 and a 16-byte aligned input");
+    if (kernel == GC_B200_TF32X3)
+        return gc_error(GC_UNSUPPORTED, "3xTF32 tensor-core path is not built in this library");
+    int dev = -1;
+    st = device_and_stream_checks(x, w, y, stream, dev);
+    if (st != GC_OK) return st;
+    if (kernel == GC_B200_AUTO) kernel = b ? auto_kernel(p, x) : GC_B200_GENERAL;
+    return run_kernel(p, x, w, y, kernel, dev, stream);
+}
+
+const char *gc_b200_last_plan(void) { return g_plan.c_str(); }
+
+int gc_b200_device_status(uint32_t *status, int clear) {
+    if (status == nullptr) return gc_error(GC_INVALID, "null status pointer");
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(status, gcb::g_status, sizeof(uint32_t));
+    if (e == cudaSuccess && clear) {
+        const uint32_t zero = 0;
+        e = cudaMemcpyToSymbol(gcb::g_status, &zero, sizeof(uint32_t));
+    }
+    if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+    return gc_error(GC_OK, "");
+}
+
+int gc_b200_selftest_wait_timeout(uint32_t limit_us, void *stream) {
+    if (limit_us == 0 || limit_us > 10000000u)
+        return gc_error(GC_INVALID, "limit_us must be in 1..10000000");
+    wait_timeout_selftest_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        static_cast<uint64_t>(limit_us) * 1000ull);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+    return gc_error(GC_OK, "");
+}
+
+}  // extern "C"

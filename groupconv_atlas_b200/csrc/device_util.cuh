@@ -1,0 +1,133 @@
+// Device-side building blocks shared by the kernels: the status word, bounded
+// mbarrier waits, TMA tensor/bulk loads and cp.async copies, as inline PTX for
+// sm_100a.  No TMA load here uses cluster multicast: every copy reads this
+// GPU's own global memory into the issuing CTA's shared memory.
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+
+namespace gcb {
+
+// Bits of the device status word (mirrors GC_B200_STATUS_* in groupconv.h).
+constexpr unsigned kStatusTmaTimeout = 0x1u;
+constexpr unsigned kStatusMmaTimeout = 0x2u;
+
+// Longest a single wait on an asynchronous copy may take before the kernel
+// gives up: two seconds of GPU global time.  Normal waits take microseconds.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+// Status word of this library on each device (one translation unit holds
+// all device code, so the definition lives here).
+__device__ unsigned int g_status = 0;
+
+__device__ __forceinline__ void raise_status(unsigned bits) { atomicOr(&g_status, bits); }
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---- mbarrier ---------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count)
+                 : "memory");
+}
+
+// Makes barrier initialisation visible to the async proxy (TMA) before use.
+__device__ __forceinline__ void fence_barrier_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar_addr), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Waits for the phase with the given parity to complete, for at most
+// limit_ns of global time.  Returns false when it gave up.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
+                                                  uint64_t limit_ns = kWaitLimitNs) {
+    const uint32_t a = smem_addr(bar);
+    if (mbar_try_wait(a, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (true) {
+        if (mbar_try_wait(a, parity)) return true;
+        if (global_ns() - t0 > limit_ns) return false;
+    }
+}
+
+// ---- TMA ----------------------------------------------------------------------
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// 4-D tiled tensor load into shared memory; completion is signalled on bar as
+// transaction bytes.  c0 is the innermost coordinate.
+__device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, int c0, int c1,
+                                            int c2, int c3, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+        "r"(smem_addr(bar))
+        : "memory");
+}
+
+// Contiguous bulk copy global -> shared (addresses 16-byte aligned, size a
+// multiple of 16), completion signalled on bar.
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,
+                                          uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_addr(bar))
+        : "memory");
+}
+
+// ---- cp.async (per-thread asynchronous copies) ----------------------------------
+// 4-byte copy; when valid is false nothing is read and the destination is
+// zero-filled.
+__device__ __forceinline__ void cp_async_4(void *dst, const void *src, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_addr(dst)), "l"(src),
+                 "r"(valid ? 4 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+    asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// ---- stores -----------------------------------------------------------------------
+// Streaming 16-byte store: the output is not re-read by this kernel, so it is
+// marked evict-first to keep the input halo rows resident in L2.
+__device__ __forceinline__ void st_stream_v4(float *p, float a, float b, float c, float d) {
+    asm volatile("st.global.cs.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
+                 "f"(d)
+                 : "memory");
+}
+__device__ __forceinline__ void st_stream(float *p, float a) {
+    asm volatile("st.global.cs.f32 [%0], %1;" ::"l"(p), "f"(a) : "memory");
+}
+
+}  // namespace gcb

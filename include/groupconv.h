@@ -1,0 +1,147 @@
+/*
+ * groupconv.h - C ABI v1 of the grouped 2-D convolution library, B200 build.
+ *
+ * The types and the v1 entry points below keep the exact layout, names,
+ * argument meaning and status codes of the reference interface
+ * (csrc/common/groupconv.h:1-58 of LucisZhang/groupconv-atlas), so that a
+ * caller bound to that header (its ctypes binding bench/api.py:90-126) loads
+ * this library unchanged.  Everything prefixed gc_b200_ is an extension with
+ * no counterpart in the reference; callers of the v1 ABI never need it.
+ *
+ * Conventions (reference csrc/common/groupconv.h:8, :36-37):
+ *   - Buffers are borrowed; no function takes ownership.
+ *   - Strides are in elements.  Only dense contiguous NCHW is computed.
+ *   - CUDA buffers and the stream belong to the caller.  gc_cuda_conv launches
+ *     asynchronously on the given stream, never synchronizes and never
+ *     allocates device or pinned host memory, so it may be captured in a CUDA
+ *     graph.
+ *   - Every entry point returns a gc_status; the message of the last call on
+ *     the calling thread is available from gc_last_error() (thread local).
+ */
+#ifndef GROUPCONV_ATLAS_H
+#define GROUPCONV_ATLAS_H
+#include <stddef.h>
+#include <stdint.h>
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GC_ABI_VERSION 1
+
+/* Status codes: reference csrc/common/groupconv.h:10-11. */
+typedef enum {
+    GC_OK = 0,
+    GC_INVALID = 1,      /* malformed metadata, pointers or sizes           */
+    GC_UNSUPPORTED = 2,  /* valid request outside this implementation's set */
+    GC_DEVICE_ERROR = 3, /* a CUDA runtime call failed                       */
+    GC_UNAVAILABLE = 4   /* backend not built into this library              */
+} gc_status;
+
+/* reference csrc/common/groupconv.h:12-14 */
+typedef enum { GC_F32 = 0, GC_F64 = 1 } gc_dtype;
+typedef enum { GC_CPU = 0, GC_CUDA = 1 } gc_device;
+typedef enum { GC_SERIAL = 0, GC_OPENMP = 1, GC_BLOCKED = 2 } gc_cpu_impl;
+
+/* Convolution geometry: 14 x int64 (reference csrc/common/groupconv.h:15-17).
+ * x is [n, cin, h, w], weights [cout, cin/groups, r, s],
+ * y is [n, cout, ho, wo] with ho = (h + 2ph - dh(r-1) - 1)/sh + 1. */
+typedef struct {
+    int64_t n, cin, cout, h, w, r, s, groups, sh, sw, ph, pw, dh, dw;
+} gc_shape;
+
+/* Borrowed tensor descriptor (reference csrc/common/groupconv.h:18-23). */
+typedef struct {
+    void *data;
+    uint64_t bytes;
+    int32_t dtype, device, device_index, rank;
+    int64_t dims[4], strides[4];
+} gc_tensor;
+
+/* ---- v1 introspection and validation -------------------------------------
+ * replaces reference csrc/common/groupconv.h:25-30 (common.cpp:56-109) */
+int gc_abi_version(void);
+const char *gc_last_error(void);
+const char *gc_build_info(void);
+int gc_has_openmp(void);
+int gc_validate_shape(const gc_shape *p, int64_t *ho, int64_t *wo);
+int gc_validate_tensors(const gc_shape *p, const gc_tensor *x,
+                        const gc_tensor *w, const gc_tensor *y,
+                        int device, int dtype);
+
+/* ---- v1 CPU backend -------------------------------------------------------
+ * replaces reference csrc/common/groupconv.h:33-34 (csrc/cpu/cpu.cpp:3-24).
+ * This library validates exactly as the reference does (same status for every
+ * malformed call) and then answers GC_UNAVAILABLE: the CPU backend is not part
+ * of the B200 build, and nothing in it computes a convolution on the host. */
+int gc_cpu_conv(const gc_shape *p, const gc_tensor *x, const gc_tensor *w,
+                gc_tensor *y, int implementation, int threads);
+
+/* ---- v1 CUDA backend (the hot path) ---------------------------------------
+ * replaces reference csrc/common/groupconv.h:38-40 (csrc/cuda/groupconv.cu:
+ * 156-222).  implementation (reference support matrix, bench/check.py:106-112):
+ *   0  general direct kernel: any valid geometry, any Cin/Cout/groups;
+ *   1  3x3/s1/p1/d1, Cin == Cout ("B geometry"), any channels per group;
+ *   2  B geometry, channels per group in {1, 2, 4}, otherwise GC_UNSUPPORTED;
+ *   3  B geometry, fastest kernel for the shape (the production choice);
+ *   any other value: GC_UNSUPPORTED.
+ * Implementations 1-3 answer GC_UNSUPPORTED outside B geometry. */
+int gc_cuda_available(void);
+int gc_cuda_conv(const gc_shape *p, const gc_tensor *x, const gc_tensor *w,
+                 gc_tensor *y, int implementation, void *stream);
+
+/* ---- v1 OpenCL backend ----------------------------------------------------
+ * replaces reference csrc/common/groupconv.h:44-51.  Not built for B200:
+ * every call answers GC_UNAVAILABLE like the reference's csrc/opencl/stub.cpp. */
+int gc_opencl_create(void **context);
+const char *gc_opencl_info(void *context);
+int gc_opencl_upload(void *context, const gc_shape *p, const gc_tensor *x,
+                     const gc_tensor *w, const gc_tensor *y);
+int gc_opencl_run(void *context, int implementation, int repeats,
+                  double *device_op_us);
+int gc_opencl_download(void *context, gc_tensor *y);
+void gc_opencl_destroy(void *context);
+
+/* ---- B200 extensions (no counterpart in the reference) ------------------- */
+
+/* Kernel families of the B200 engine, for gc_b200_conv. */
+typedef enum {
+    GC_B200_AUTO = 0,       /* same choice as gc_cuda_conv implementation 3     */
+    GC_B200_GENERAL = 1,    /* any geometry, one output column run per thread   */
+    GC_B200_DIRECT_LDG = 2, /* B geometry, smem band staged by cp.async         */
+    GC_B200_DIRECT_TMA = 3, /* B geometry, smem band staged by TMA tensor loads */
+    GC_B200_TF32X3 = 4      /* B geometry, cpg >= 16: tcgen05 3xTF32 implicit GEMM */
+} gc_b200_kernel;
+
+/* Same contract as gc_cuda_conv (validation, stream, no allocation, no sync),
+ * but runs the named kernel family or answers GC_UNSUPPORTED when that family
+ * cannot serve the request (geometry, channels per group, alignment). */
+int gc_b200_conv(const gc_shape *p, const gc_tensor *x, const gc_tensor *w,
+                 gc_tensor *y, int kernel, void *stream);
+
+/* Launch plan chosen by the last successful gc_cuda_conv / gc_b200_conv call
+ * on the calling thread: kernel family name, grid, block, shared memory and
+ * work split, as one line of text.  Empty before the first launch. */
+const char *gc_b200_last_plan(void);
+
+/* Device-side status word shared by every kernel of this library on the
+ * current device.  Kernels set a bit when a bounded wait on the asynchronous
+ * copy engine gave up (the kernel then leaves its outputs incomplete and
+ * returns instead of hanging).  Synchronizes the current device, stores the
+ * word in *status and, when clear != 0, resets it to zero. */
+#define GC_B200_STATUS_TMA_TIMEOUT 0x1u
+#define GC_B200_STATUS_MMA_TIMEOUT 0x2u
+int gc_b200_device_status(uint32_t *status, int clear);
+
+/* Self-test of the bounded wait: launches one block on `stream` that waits on
+ * a shared-memory barrier nothing will ever complete, gives up after roughly
+ * limit_us microseconds, sets GC_B200_STATUS_TMA_TIMEOUT and returns.  Lets a
+ * test check the timeout path without faulting or hanging the GPU. */
+int gc_b200_selftest_wait_timeout(uint32_t limit_us, void *stream);
+
+#ifdef __cplusplus
+}
+/* Internal shared error helper; returns the supplied status
+ * (reference csrc/common/groupconv.h:55-56). */
+int gc_error(int status, const char *message);
+#endif
+#endif

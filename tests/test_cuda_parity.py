@@ -1,0 +1,121 @@
+"""GPU parity: every kernel family, through the C ABI, against the oracle on
+the same seeded inputs.  Acceptance per output element:
+|y - y_fp64| <= 1e-5 * sum|x*w| (FP64 oracle), plus the reference's own gates
+(1e-4 atol/rtol vs its FP32 output, 64 FP64 points)."""
+import numpy as np
+import pytest
+
+from groupconv_atlas_b200.api import Shape, NativeError, inputs, GC_UNSUPPORTED
+from groupconv_atlas_b200 import workloads
+from oracle import oracle as orc
+from tests.gpu_helpers import run, assert_matches
+
+pytestmark = pytest.mark.gpu
+
+
+def expected_support(shape, impl):
+    """The reference's support matrix (bench/check.py:106-112)."""
+    if impl == 0:
+        return True
+    return shape.b_geometry and (impl != 2 or shape.cpg in (1, 2, 4))
+
+
+def test_golden_all_implementations(native, torch_cuda, golden_cases):
+    """Reference boundary suite, special patterns, native-runner matrix and the
+    general-geometry sweep, through gc_cuda_conv implementations 0-3."""
+    for c in golden_cases:
+        for impl in range(4):
+            if not expected_support(c.shape, impl):
+                with pytest.raises(NativeError) as err:
+                    run(native, torch_cuda, c.shape, c.x, c.w, impl=impl)
+                assert err.value.status == GC_UNSUPPORTED, (c.name, impl)
+                continue
+            y, plan = run(native, torch_cuda, c.shape, c.x, c.w, impl=impl)
+            assert_matches(c.shape, c.x, c.w, y, c.y32, label=f'{c.name} impl{impl} [{plan}]')
+
+
+@pytest.mark.parametrize('kernel', ['general', 'direct_ldg', 'direct_tma'])
+def test_golden_kernel_families(native, torch_cuda, golden_cases, kernel):
+    """Each kernel family on every golden case it serves; the others must be
+    refused with GC_UNSUPPORTED, never silently rerouted."""
+    ran = 0
+    for c in golden_cases:
+        eligible = kernel == 'general' or c.shape.b_geometry
+        if kernel == 'direct_tma':
+            eligible = eligible and c.shape.w % 4 == 0
+        if not eligible:
+            with pytest.raises(NativeError) as err:
+                run(native, torch_cuda, c.shape, c.x, c.w, kernel=kernel)
+            assert err.value.status == GC_UNSUPPORTED
+            continue
+        y, plan = run(native, torch_cuda, c.shape, c.x, c.w, kernel=kernel)
+        assert plan.startswith(f'kernel={kernel}'), plan
+        assert_matches(c.shape, c.x, c.w, y, c.y32, label=f'{c.name} {kernel}')
+        ran += 1
+    assert ran > 0
+
+
+SMALL_B = [
+    # (n, c, h, w, cpg): tails in both axes, multi-band items, wide cpg
+    (1, 8, 56, 56, 1), (3, 12, 30, 44, 2), (2, 16, 57, 60, 4), (2, 32, 23, 40, 8),
+    (1, 48, 19, 28, 16), (1, 64, 14, 16, 32), (1, 128, 9, 12, 64), (2, 6, 33, 17, 3),
+    (1, 10, 70, 72, 5), (1, 24, 112, 112, 1), (1, 16, 112, 112, 4), (1, 8, 7, 7, 8),
+    (5, 4, 14, 14, 2), (1, 2, 200, 248, 1), (1, 4, 5, 252, 2),
+]
+
+
+@pytest.mark.parametrize('n,c,h,w,cpg', SMALL_B)
+@pytest.mark.parametrize('kernel', ['direct_ldg', 'direct_tma', 'auto'])
+def test_b_geometry_shapes(native, torch_cuda, n, c, h, w, cpg, kernel):
+    s = Shape(n=n, cin=c, cout=c, h=h, w=w, groups=c // cpg)
+    x, wt = inputs(s, 7)
+    if kernel == 'direct_tma' and w % 4:
+        pytest.skip('TMA staging needs width % 4 == 0')
+    if kernel == 'direct_tma' and w + 8 > 256:
+        pytest.skip('TMA box is at most 256 columns')
+    y, plan = run(native, torch_cuda, s, x, wt, kernel=kernel)
+    assert_matches(s, x, wt, y, label=f'{s} {plan}')
+
+
+def test_config1_full(native, torch_cuda):
+    """BASELINE config 1 (N1 C32 56x56 g8), full output, all implementations."""
+    wl = workloads.config1()
+    for impl in (0, 1, 2, 3):
+        y, plan = run(native, torch_cuda, wl.shape, wl.x, wl.w, impl=impl)
+        assert_matches(wl.shape, wl.x, wl.w, y, label=f'config1 impl{impl} {plan}')
+
+
+def test_config4_leaf_full(native, torch_cuda):
+    """MobileNetV2 depthwise leaf of config 4 (N4 C144 56x56), full output."""
+    s = Shape(n=4, cin=144, cout=144, h=56, w=56, groups=144)
+    x, w = inputs(s, 2)
+    y, plan = run(native, torch_cuda, s, x, w, impl=3)
+    assert_matches(s, x, w, y, label=f'config4 leaf {plan}')
+
+
+@pytest.mark.parametrize('name', ['config2', 'config5_g32', 'config5_g4'])
+def test_config_batch_slices(native, torch_cuda, name):
+    """Configs 2 and 5 at their channel/spatial sizes on a 2-image batch slice
+    (full outputs checked against the FP64 oracle)."""
+    wl = workloads.by_name(name, batch=2)
+    y, plan = run(native, torch_cuda, wl.shape, wl.x, wl.w, impl=3)
+    assert_matches(wl.shape, wl.x, wl.w, y, label=f'{name} slice {plan}')
+
+
+def test_sweep_config3(native, torch_cuda):
+    """All 80 shapes of the config-3 sweep.  Shapes whose oracle finishes
+    quickly are checked in full; the others on a one-image slice of the same
+    channels and spatial size plus 64 FP64 points of the full batch."""
+    shapes = workloads.sweep_shapes()
+    assert len(shapes) == 80
+    for s in shapes:
+        work = s.n * s.cout * s.h * s.w * s.cpg * 9
+        check = s if work <= 3e8 else Shape(**{**s.__dict__, 'n': 1})
+        x, w = workloads.sweep_inputs(check)
+        y, plan = run(native, torch_cuda, check, x, w, impl=3)
+        assert_matches(check, x, w, y, label=f'sweep {s} {plan}', points=check is s)
+        if check is not s:
+            x, w = workloads.sweep_inputs(s)
+            y, _ = run(native, torch_cuda, s, x, w, impl=3)
+            p = orc.check_points(s, x, w, y)
+            assert p['passed'], f'sweep points {s}'
