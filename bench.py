@@ -54,6 +54,8 @@ def parse_args(argv=None):
                     choices=['config1', 'config2', 'config4_leaf', 'config5_g32', 'config5_g4'])
     ap.add_argument('--scaling', choices=['weak', 'strong'], default=None,
                     help='weak: each rank runs the full workload batch; strong: the batch is sharded')
+    ap.add_argument('--batch', type=int, default=None,
+                    help='override the workload batch (small cases for profiling)')
     ap.add_argument('--e2e-steps', type=int, default=20)
     ap.add_argument('--no-e2e', action='store_true')
     ap.add_argument('--no-cudnn', action='store_true')
@@ -294,7 +296,7 @@ def run_ours(args):
         dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device('cuda', local))
     native = api.Native()
-    full = workloads.by_name(args.workload, with_x=False)
+    full = workloads.by_name(args.workload, batch=args.batch, with_x=False)
     if args.scaling == 'weak':
         units = [shard.Unit(0, full.shape.n, 0, full.shape.cin)]
         first_image = rank * full.shape.n  # each rank: its own batch of the same shape
@@ -377,7 +379,16 @@ def run_ours(args):
     barrier()
     elapsed_ms = region0.elapsed_time(region1)
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    # Kernel duration for the roofline: events around every step of the timed
+    # region above.  The CUDA-graph replay figure (no host launch cost in the
+    # gaps) is reported beside it.
     kernel_ms = statistics.fmean(step_ms) / launches_per_step
+
+    def graph_step(k):
+        for c in calls[k % sets]:
+            c()
+    with torch.cuda.stream(stream):
+        graph_kernel_ms = graph_step_ms(torch, stream, graph_step, min(args.steps, 50)) / launches_per_step
     max_elapsed = shard.max_over_ranks(elapsed_ms)
     job_bytes = shard.sum_over_ranks(step_bytes)
     job_flops = shard.sum_over_ranks(step_flops)
@@ -392,7 +403,7 @@ def run_ours(args):
 
     cudnn = None
     if not args.no_cudnn and rank == 0:
-        cudnn = cudnn_baseline(args, torch, local_shape, xs, dw, sets, kernel_ms * launches_per_step)
+        cudnn = cudnn_baseline(args, torch, local_shape, xs, dw, sets, graph_kernel_ms * launches_per_step)
 
     cpu = None
     if not args.no_cpu_baseline and rank == 0 and world == 1:
@@ -425,6 +436,8 @@ def run_ours(args):
             'roofline': {'bound': 'hbm', 'achieved': achieved, 'peak': peaks['hbm_gbs'], 'unit': 'GB/s',
                          'frac': achieved / peaks['hbm_gbs'], 'traffic': traffic,
                          'peak_source': peak_kind, 'kernel_ms': kernel_ms,
+                         'kernel_ms_timing': 'CUDA events around each step of the timed region, launch stream',
+                         'graph_kernel_ms': graph_kernel_ms,
                          'algorithmic_bytes_per_launch': step_bytes / launches_per_step,
                          'fp32_tflops': (step_flops / launches_per_step) / (kernel_ms / 1e3) / 1e12},
             'e2e': e2e, 'gpu_launches': args.steps * launches_per_step, 'clocks': clocks,
@@ -501,6 +514,28 @@ def end_to_end(args, native, shape, units, xh, wh, torch, api, shard):
             'path': 'pinned host -> gc_cuda_conv per chunk (C ABI via ctypes) -> pinned host'}
 
 
+def graph_step_ms(torch, stream, step, count, replays=3):
+    """Device time of one step from CUDA-graph replay: `count` steps captured
+    back to back (host launch cost excluded, as the reference's graph timing
+    bench/cuda_run.py:92-121), mean over `replays` replays."""
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for k in range(count):
+            step(k)
+    graph.replay()
+    stream.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(replays):
+        graph.replay()
+    b.record(stream)
+    stream.synchronize()
+    ms = a.elapsed_time(b) / (replays * count)
+    del graph
+    return ms
+
+
 def cudnn_baseline(args, torch, shape, xs, dw, sets, our_step_ms):
     """torch.nn.functional.conv2d on the same device buffers: TF32 off and read
     back, cudnn.benchmark on, device time of back-to-back calls."""
@@ -518,7 +553,7 @@ def cudnn_baseline(args, torch, shape, xs, dw, sets, our_step_ms):
         raise SystemExit('could not disable TF32 for the cuDNN baseline')
     torch.backends.cudnn.benchmark = True
     stream = torch.cuda.Stream()
-    steps = max(20, min(args.steps, 500))
+    steps = max(20, min(args.steps, 200))
     with torch.inference_mode(), torch.cuda.stream(stream):
         for k in range(10):
             F.conv2d(xs[k % sets], dw, padding=1, groups=shape.groups)
@@ -529,8 +564,14 @@ def cudnn_baseline(args, torch, shape, xs, dw, sets, our_step_ms):
             F.conv2d(xs[k % sets], dw, padding=1, groups=shape.groups)
         b.record(stream)
         stream.synchronize()
-    ms = a.elapsed_time(b) / steps
-    return {'ms_per_step': ms, 'ours_ms_per_step': our_step_ms, 'speedup_vs_cudnn': ms / our_step_ms,
+        eager_ms = a.elapsed_time(b) / steps
+        outs = [None] * sets
+
+        def step(k):
+            outs[k % sets] = F.conv2d(xs[k % sets], dw, padding=1, groups=shape.groups)
+        graph_ms = graph_step_ms(torch, stream, step, min(steps, 50))
+    return {'ms_per_step': graph_ms, 'eager_ms_per_step': eager_ms, 'ours_ms_per_step': our_step_ms,
+            'speedup_vs_cudnn': graph_ms / our_step_ms, 'timing': 'CUDA-graph replay, both sides',
             'api': 'torch.nn.functional.conv2d', 'tf32': False, 'benchmark': True,
             'cudnn_version': torch.backends.cudnn.version()}
 

@@ -124,7 +124,7 @@ int tensor_map_encoder(PFN_cuTensorMapEncodeTiled_v12000 &fn) {
 // out-of-range elements read as zero.
 int encode_nchw_map(CUtensorMap &map, const float *base, long long n, long long c, long long h,
                     long long w, int bw, int bh, int bc) {
-    PFN_cuTensorMapEncodeTiled_v12000 encode;
+    PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     int st = tensor_map_encoder(encode);
     if (st != GC_OK) return st;
     cuuint64_t dims[4] = {static_cast<cuuint64_t>(w), static_cast<cuuint64_t>(h),
@@ -153,8 +153,8 @@ struct Variant {
 template <int CPG, int COB, int VR>
 Variant make_variant(const char *name) {
     return Variant{name, COB, VR,
-                   reinterpret_cast<const void *>(&gcb::direct_conv_kernel<CPG, COB, VR, true, kStages>),
-                   reinterpret_cast<const void *>(&gcb::direct_conv_kernel<CPG, COB, VR, false, kStages>)};
+                   reinterpret_cast<const void *>(&gcb::direct_conv_kernel<CPG, COB, VR, true>),
+                   reinterpret_cast<const void *>(&gcb::direct_conv_kernel<CPG, COB, VR, false>)};
 }
 
 template <int COB, int VR>
@@ -164,18 +164,21 @@ Variant make_wide(const char *name) {
                    reinterpret_cast<const void *>(&gcb::wide_conv_kernel<COB, VR, false, kStages>)};
 }
 
-// Full-group kernel variant for small groups.
-const Variant &small_variant(long long cpg) {
+// Full-group kernel variants that can serve a group width (first = preferred).
+std::vector<const Variant *> small_variants(long long cpg) {
     static const Variant d1 = make_variant<1, 1, 4>("d1");
+    static const Variant d1r8 = make_variant<1, 1, 8>("d1r8");
+    static const Variant d1r14 = make_variant<1, 1, 14>("d1r14");
     static const Variant d2 = make_variant<2, 2, 4>("d2");
-    static const Variant d4 = make_variant<4, 4, 4>("d4");
+    static const Variant d4 = make_variant<4, 4, 2>("d4");
     static const Variant d8 = make_variant<8, 8, 2>("d8");
+    static const Variant d8h = make_variant<8, 4, 2>("d8h");
     static const Variant gen = make_variant<0, 1, 4>("g1");
-    if (cpg == 1) return d1;
-    if (cpg == 2) return d2;
-    if (cpg == 4) return d4;
-    if (cpg == 8) return d8;
-    return gen;
+    if (cpg == 1) return {&d1, &d1r8, &d1r14};
+    if (cpg == 2) return {&d2};
+    if (cpg == 4) return {&d4};
+    if (cpg == 8) return {&d8, &d8h};
+    return {&gen};
 }
 
 // Channel-chunked kernel variant for wide groups.
@@ -209,6 +212,18 @@ struct EnginePlan {
     gcb::WideParams Wp;  // valid when wide
 };
 
+// Fraction of the machine a persistent grid keeps busy: with fewer items than
+// CTA slots, the share of SMs that get work; otherwise the fill of the last
+// wave.
+double grid_balance(long long items, long long slots, int sms) {
+    if (items <= slots) {
+        const long long per_sm = ceil_div(items, sms);
+        return static_cast<double>(items) / (static_cast<double>(per_sm) * sms);
+    }
+    const long long waves = ceil_div(items, slots);
+    return static_cast<double>(items) / (static_cast<double>(waves) * slots);
+}
+
 // Shared scoring of a candidate tiling: load balance of the persistent grid,
 // thread utilisation, the input re-read factor (halo rows, output-channel
 // blocks) and the latency-hiding capacity of the SM.
@@ -217,7 +232,7 @@ double score_tiling(long long items, long long slots, long long cells, int threa
     const long long waves = ceil_div(items, slots);
     const double balance = static_cast<double>(items) / (static_cast<double>(waves) * slots);
     const double cell_eff = static_cast<double>(cells) / (ceil_div(cells, threads) * threads);
-    double score = balance * cell_eff / (1.0 + 0.15 * (reread - 1.0));
+    double score = std::min(balance, 1.0) * cell_eff / (1.0 + 0.15 * (reread - 1.0));
     const double warps = ctas * threads / 32.0;
     if (warps < 16) score *= 0.75 + 0.25 * warps / 16.0;
     const double inflight = ctas * (kStages - 1) * stage_bytes;
@@ -229,77 +244,168 @@ const std::vector<long long> band_candidates(long long H) {
     return {H, ceil_div(H, 2), ceil_div(H, 3), ceil_div(H, 4), ceil_div(H, 7), 64, 32, 28, 16, 14, 8, 4, 2, 1};
 }
 
+// Estimated fraction of a direct-kernel thread's instructions that are FFMA:
+// per input channel a cell loads VR+2 row segments (one 16-byte load, two
+// shuffles, two predicated edge loads, two selects each) and its weights, and
+// per item it pays a fixed cost (item decode, barriers, output addresses) plus
+// its stores.
+double issue_efficiency(const Variant &var, long long cpg) {
+    const double vr = var.vr, cob = var.cob;
+    const double ffma = cob * vr * 36.0 * cpg;
+    const double rows = (vr + 2) * 7.0 * cpg;
+    const double weights = cpg == 1 ? 9.0 : 9.0 * std::ceil(cob / 4.0) * cpg;
+    const double fixed = 40.0 + vr * cob * 3.0;
+    return ffma / (ffma + rows + weights + fixed);
+}
+
+// Row pitch (floats) of the direct kernel's tile: the smallest multiple of 4
+// holding 4*qcols + 8 columns whose warp-wide 16-byte loads need the fewest
+// shared-memory wavefronts, found by replaying the lane -> address map of
+// the first warps (8 lanes of 16 bytes fill the 32 banks once; distinct
+// addresses in the same 16-byte bank group serialize).
+int choose_pitch(int W, int qcols, int rblocks, int vr, int rows, int cells, int cob, int cpg,
+                 bool tma) {
+    const int base = static_cast<int>(round_up(4LL * qcols + 8, 4));
+    int best = base, best_cost = 1 << 30;
+    for (int p = base; p <= base + 60; p += 4) {
+        if (tma && p > 256) break;
+        // exact per-lane addresses: channel block, row block (rb * vr rows), quad
+        const int warps = std::min((cells + 31) / 32, 8);
+        int cost = 0;
+        for (int wp = 0; wp < warps; ++wp) {
+            long long addr[32];
+            for (int lane = 0; lane < 32; ++lane) {
+                const int cell = std::min(wp * 32 + lane, cells - 1);
+                const int q = cell % qcols, rbc = cell / qcols;
+                const int rb = rbc % rblocks, cbk = rbc / rblocks;
+                const int g = cbk * cob / cpg;
+                addr[lane] = ((static_cast<long long>(g) * cpg * rows + rb * vr) * p + q * 4 + 4) * 4;
+            }
+            int worst = 0;
+            for (int bank = 0; bank < 8; ++bank) {
+                long long seen[32];
+                int n = 0;
+                for (int lane = 0; lane < 32; ++lane) {
+                    if ((addr[lane] / 16) % 8 != bank) continue;
+                    bool dup = false;
+                    for (int i = 0; i < n; ++i) dup |= seen[i] == addr[lane];
+                    if (!dup) seen[n++] = addr[lane];
+                }
+                worst = std::max(worst, n);
+            }
+            cost += worst;
+        }
+        if (cost < best_cost) {
+            best_cost = cost;
+            best = p;
+        }
+    }
+    (void)W;
+    return best;
+}
+
 // Full-group tiling (kernel_direct.cuh) for groups of fewer than 16 channels.
+// Every CTA thread owns one cell, so a candidate needs cells <= 256; the
+// block is the cells rounded up to whole warps.
 int plan_small(const gc_shape *p, bool tma, bool w_aligned, bool y_aligned, int dev,
                const DeviceFacts &facts, EnginePlan &out, bool &found) {
     const long long N = p->n, C = p->cin, H = p->h, W = p->w, cpg = p->cin / p->groups;
-    const Variant &var = small_variant(cpg);
-    const int vr = var.vr;
-    const int pitch = round_up((W) + 8, 4);
     const long long groups = p->groups;
+    const long long qcols = ceil_div(W, 4);
+    const bool compute_bound = cpg >= 4;
     double best = -1.0;
     found = false;
-    for (long long gpi = 1; gpi <= groups; ++gpi) {
-        if (groups % gpi != 0) continue;
-        const long long cb = gpi * cpg;
-        if (cb > std::max<long long>(cpg, 64)) break;
-        for (long long bh : band_candidates(H)) {
-            if (bh < 1 || bh > H) continue;
-            if (bh != H && bh % vr != 0) continue;
-            const long long rows = round_up((bh), vr) + 2;
-            if (tma && (rows > 256 || cb > 256)) continue;
-            const long long xf = round_up((cb * rows * pitch), 32);
-            const long long wf = round_up((cb * cpg * 9), 32);
-            const long long wtf = cpg == 1 ? 0 : wf;
-            const size_t smem = static_cast<size_t>((kStages * (xf + wf) + wtf) * 4 + 64);
-            if (smem > static_cast<size_t>(facts.smem_optin)) continue;
-            const long long bands = ceil_div(H, bh);
-            const long long items = N * (C / cb) * bands;
-            const long long cells = (cb / var.cob) * ceil_div(bh, vr) * ceil_div(W, 4);
-            for (int threads : {128, 256}) {
-                int ctas = 0;
-                int st = kernel_occupancy(dev, tma ? var.fn_tma : var.fn_ldg, threads, smem,
-                                          facts.smem_optin, ctas);
-                if (st != GC_OK) return st;
-                if (ctas < 1) continue;
-                const long long slots = static_cast<long long>(facts.sms) * ctas;
-                const double score = score_tiling(items, slots, cells, threads,
-                                                  static_cast<double>(rows) / bh, ctas, (xf + wf) * 4.0);
-                if (score <= best + 1e-9) continue;
-                best = score;
-                found = true;
-                DirectParams &P = out.D;
-                std::memset(&P, 0, sizeof(P));
-                P.n = static_cast<int>(N);
-                P.c = static_cast<int>(C);
-                P.h = static_cast<int>(H);
-                P.wd = static_cast<int>(W);
-                P.cpg = static_cast<int>(cpg);
-                P.cb = static_cast<int>(cb);
-                P.bh = static_cast<int>(bh);
-                P.bands = static_cast<int>(bands);
-                P.cblocks = static_cast<int>(C / cb);
-                P.items = items;
-                P.pitch = pitch;
-                P.rows = static_cast<int>(rows);
-                P.x_floats = static_cast<int>(xf);
-                P.wraw_floats = static_cast<int>(wf);
-                P.stage_floats = static_cast<int>(xf + wf);
-                P.wt_floats = static_cast<int>(wtf);
-                P.qcols = static_cast<int>(ceil_div(W, 4));
-                P.rblocks = static_cast<int>(ceil_div(bh, vr));
-                P.cells = static_cast<int>(cells);
-                P.vec_store = (W % 4 == 0 && y_aligned) ? 1 : 0;
-                P.bulk_w = (tma && w_aligned && (cb * cpg) % 4 == 0) ? 1 : 0;
-                P.x_bytes = static_cast<unsigned>(pitch * rows * cb * 4);
-                P.w_bytes = static_cast<unsigned>(cb * cpg * 9 * 4);
-                out.wide = false;
-                out.var = &var;
-                out.tma = tma;
-                out.threads = threads;
-                out.smem = smem;
-                out.ctas_per_sm = ctas;
-                out.grid = static_cast<int>(std::min<long long>(items, slots));
+    for (const Variant *vp : small_variants(cpg)) {
+        const Variant &var = *vp;
+        const int vr = var.vr;
+        for (long long gpi = 1; gpi <= groups; ++gpi) {
+            if (groups % gpi != 0) continue;
+            const long long cb = gpi * cpg;
+            if (cb > std::max<long long>(cpg, 64)) break;
+            for (long long bh : band_candidates(H)) {
+                if (bh < 1 || bh > H) continue;
+                if (bh != H && bh % vr != 0) continue;
+                const long long rblocks = ceil_div(bh, vr);
+                const long long cells = (cb / var.cob) * rblocks * qcols;
+                if (cells > 256) continue;
+                const long long rows = rblocks * vr + 2;
+                if (tma && (rows > 256 || cb > 256)) continue;
+                const long long bands = ceil_div(H, bh);
+                const long long items = N * (C / cb) * bands;
+                if (items >= (1LL << 31)) continue;
+                const int threads = static_cast<int>(round_up(cells, 32));
+                const int pitch = choose_pitch(static_cast<int>(W), static_cast<int>(qcols),
+                                               static_cast<int>(rblocks), vr, static_cast<int>(rows),
+                                               static_cast<int>(cells), var.cob, static_cast<int>(cpg), tma);
+                if (tma && pitch > 256) continue;
+                const long long xf = round_up(cb * rows * pitch, 32);
+                const long long wf = round_up(cb * cpg * 9, 32);
+                const long long wtf = cpg == 1 ? 0 : wf;  // transposed copy
+                for (int stages = 2; stages <= gcb::kMaxStages; ++stages) {
+                    const size_t smem =
+                        static_cast<size_t>((stages * (xf + wf) + wtf) * 4 + 8 * gcb::kMaxStages);
+                    if (smem > static_cast<size_t>(facts.smem_optin)) break;
+                    int ctas = 0;
+                    int st = kernel_occupancy(dev, tma ? var.fn_tma : var.fn_ldg, threads, smem,
+                                              facts.smem_optin, ctas);
+                    if (st != GC_OK) return st;
+                    if (ctas < 1) continue;
+                    const long long slots = static_cast<long long>(facts.sms) * ctas;
+                    const double balance = grid_balance(items, slots, facts.sms);
+                    const double cell_eff = static_cast<double>(cells) / threads;
+                    // A CTA overlaps the staging of its next items with compute
+                    // only when it owns several items.
+                    const double per_cta = static_cast<double>(items) / std::min(items, slots);
+                    const double halo = static_cast<double>(rows) / bh;
+                    const double warps = ctas * threads / 32.0;
+                    double score = balance * issue_efficiency(var, cpg);
+                    if (compute_bound) {
+                        score *= cell_eff / (1.0 + 0.05 * (halo - 1.0));
+                        score *= std::min(1.0, 0.55 + 0.45 * warps / 16.0);
+                    } else {
+                        score /= 1.0 + 0.15 * (halo - 1.0);
+                        score *= std::min(1.0, 0.75 + 0.25 * warps / 16.0);
+                        score *= std::min(1.0, 0.6 + 0.4 * (per_cta - 1.0) / 3.0);
+                        const double inflight = ctas * (stages - 1) * (xf + wf) * 4.0;
+                        score *= std::min(1.0, 0.7 + 0.3 * inflight / (64.0 * 1024));
+                    }
+                    if (score <= best + 1e-9) continue;
+                    best = score;
+                    found = true;
+                    DirectParams &P = out.D;
+                    std::memset(&P, 0, sizeof(P));
+                    P.n = static_cast<int>(N);
+                    P.c = static_cast<int>(C);
+                    P.h = static_cast<int>(H);
+                    P.wd = static_cast<int>(W);
+                    P.cpg = static_cast<int>(cpg);
+                    P.cb = static_cast<int>(cb);
+                    P.bh = static_cast<int>(bh);
+                    P.bands = static_cast<int>(bands);
+                    P.cblocks = static_cast<int>(C / cb);
+                    P.items = static_cast<int>(items);
+                    P.pitch = pitch;
+                    P.rows = static_cast<int>(rows);
+                    P.x_floats = static_cast<int>(xf);
+                    P.wraw_floats = static_cast<int>(wf);
+                    P.stage_floats = static_cast<int>(xf + wf);
+                    P.wt_floats = static_cast<int>(wtf);
+                    P.qcols = static_cast<int>(qcols);
+                    P.rblocks = static_cast<int>(rblocks);
+                    P.cells = static_cast<int>(cells);
+                    P.stages = stages;
+                    P.vec_store = (W % 4 == 0 && y_aligned) ? 1 : 0;
+                    P.bulk_w = (tma && w_aligned && (cb * cpg) % 4 == 0) ? 1 : 0;
+                    P.x_bytes = static_cast<unsigned>(pitch * rows * cb * 4);
+                    P.w_bytes = static_cast<unsigned>(cb * cpg * 9 * 4);
+                    out.wide = false;
+                    out.var = &var;
+                    out.tma = tma;
+                    out.threads = threads;
+                    out.smem = smem;
+                    out.ctas_per_sm = ctas;
+                    out.grid = static_cast<int>(std::min<long long>(items, slots));
+                }
             }
         }
     }
@@ -444,10 +550,10 @@ int launch_direct(const gc_shape *p, const float *x, const float *w, float *y, b
         args[0] = &plan.D;
         std::snprintf(buf, sizeof(buf),
                       "kernel=direct_%s engine=group variant=%s grid=%d block=%d smem=%zu ctas_per_sm=%d "
-                      "cb=%d bh=%d items=%lld cells=%d pitch=%d rows=%d bulk_w=%d vec_store=%d",
+                      "cb=%d bh=%d items=%d cells=%d stages=%d pitch=%d rows=%d bulk_w=%d vec_store=%d",
                       tma ? "tma" : "ldg", plan.var->name, plan.grid, plan.threads, plan.smem,
-                      plan.ctas_per_sm, plan.D.cb, plan.D.bh, plan.D.items, plan.D.cells, plan.D.pitch,
-                      plan.D.rows, plan.D.bulk_w, plan.D.vec_store);
+                      plan.ctas_per_sm, plan.D.cb, plan.D.bh, plan.D.items, plan.D.cells, plan.D.stages,
+                      plan.D.pitch, plan.D.rows, plan.D.bulk_w, plan.D.vec_store);
     } else {
         plan.Wp.x = x;
         plan.Wp.w = w;

@@ -117,6 +117,26 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() {
     asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
+// Waits until at most `pending` (0..3) of this thread's newest groups are in flight.
+__device__ __forceinline__ void cp_async_wait_dynamic(int pending) {
+    if (pending <= 0) cp_async_wait<0>();
+    else if (pending == 1) cp_async_wait<1>();
+    else if (pending == 2) cp_async_wait<2>();
+    else cp_async_wait<3>();
+}
+
+// ---- shared-memory loads ------------------------------------------------------------
+// Predicated 4-byte shared load: returns the value at p when pred, else 0.0f,
+// without a branch (no warp divergence around rare edge loads).
+__device__ __forceinline__ float lds_if(const float *p, bool pred) {
+    float v;
+    asm volatile(
+        "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\tmov.b32 %0, 0f00000000;\n\t"
+        "@q ld.shared.f32 %0, [%1];\n\t}"
+        : "=f"(v)
+        : "r"(smem_addr(p)), "r"(pred ? 1 : 0));
+    return v;
+}
 
 // ---- stores -----------------------------------------------------------------------
 // Streaming 16-byte store: the output is not re-read by this kernel, so it is

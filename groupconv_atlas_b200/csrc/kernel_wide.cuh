@@ -119,7 +119,8 @@ __global__ void __launch_bounds__(256) wide_conv_kernel(const __grid_constant__ 
         const long long item = first + (k / P.chunks) * step;
         float *xs = smem + s * P.x_floats;
         if (TMA) {
-            const bool ok = mbar_wait_bounded(&bars[s], static_cast<uint32_t>((k / STAGES) & 1));
+            bool ok = true;
+            if (tid == 0) ok = mbar_wait_bounded(&bars[s], static_cast<uint32_t>((k / STAGES) & 1));
             if (!__syncthreads_and(ok)) {
                 if (tid == 0) {
                     raise_status(kStatusTmaTimeout);
