@@ -27,6 +27,7 @@
 #include "kernel_direct.cuh"
 #include "kernel_general.cuh"
 #include "kernel_wide.cuh"
+#include "kernel_tf32x3.cuh"
 
 namespace {
 
@@ -168,13 +169,12 @@ Variant make_wide(const char *name) {
 std::vector<const Variant *> small_variants(long long cpg) {
     static const Variant d1 = make_variant<1, 1, 4>("d1");
     static const Variant d1r8 = make_variant<1, 1, 8>("d1r8");
-    static const Variant d1r14 = make_variant<1, 1, 14>("d1r14");
     static const Variant d2 = make_variant<2, 2, 4>("d2");
     static const Variant d4 = make_variant<4, 4, 2>("d4");
     static const Variant d8 = make_variant<8, 8, 2>("d8");
     static const Variant d8h = make_variant<8, 4, 2>("d8h");
     static const Variant gen = make_variant<0, 1, 4>("g1");
-    if (cpg == 1) return {&d1, &d1r8, &d1r14};
+    if (cpg == 1) return {&d1r8, &d1};
     if (cpg == 2) return {&d2};
     if (cpg == 4) return {&d4};
     if (cpg == 8) return {&d8, &d8h};
@@ -363,6 +363,7 @@ int plan_small(const gc_shape *p, bool tma, bool w_aligned, bool y_aligned, int 
                         score *= cell_eff / (1.0 + 0.05 * (halo - 1.0));
                         score *= std::min(1.0, 0.55 + 0.45 * warps / 16.0);
                     } else {
+                        score *= cell_eff;
                         score /= 1.0 + 0.15 * (halo - 1.0);
                         score *= std::min(1.0, 0.75 + 0.25 * warps / 16.0);
                         score *= std::min(1.0, 0.6 + 0.4 * (per_cta - 1.0) / 3.0);
@@ -578,6 +579,121 @@ int launch_direct(const gc_shape *p, const float *x, const float *w, float *y, b
     return GC_OK;
 }
 
+// ---- tcgen05 3xTF32 implicit GEMM ------------------------------------------------------
+bool tf32_cpg_supported(long long cpg) { return cpg == 8 || cpg == 16 || cpg == 32 || cpg == 64; }
+
+// Whether the tensor-core path can serve this shape and input pointer: a
+// supported group width, a TMA-stageable row (width % 4 == 0, <= 256
+// floats, 16-byte aligned input) and 32-bit pixel indices.
+bool tf32_eligible(const gc_shape *p, const void *x) {
+    const long long cpg = p->cin / p->groups;
+    return tf32_cpg_supported(cpg) && p->w % 4 == 0 && p->w <= 256 && aligned16(x) &&
+           p->h * (p->w + 2) < (1LL << 30) && p->n < (1LL << 30) && p->cin < (1LL << 30);
+}
+
+struct Tf32Plan {
+    gcb::Tf32Params P;
+    const void *fn = nullptr;
+    size_t smem = 0;
+    int grid = 0;
+};
+
+const void *tf32_kernel_for(long long cpg) {
+    switch (cpg) {
+    case 8: return reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<8>);
+    case 16: return reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<16>);
+    case 32: return reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<32>);
+    case 64: return reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<64>);
+    default: return nullptr;
+    }
+}
+
+// Largest strip of M-tiles whose double-buffered stages fit in shared memory
+// and whose two accumulators fit in the 512 TMEM columns.
+int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
+    DeviceFacts facts;
+    int st = device_facts(dev, facts);
+    if (st != GC_OK) return st;
+    const long long N = p->n, C = p->cin, H = p->h, W = p->w, cpg = C / p->groups;
+    const long long wp = W + 2;
+    const long long tiles = ceil_div(H * wp, 128);
+    int best_t = 0;
+    gcb::Tf32Params best{};
+    size_t best_smem = 0;
+    for (long long T = 1; T <= tiles && 2 * T * cpg <= 512; ++T) {
+        const long long rows_a = round_up(T * 128 + 2 * wp + 2, 8);
+        const long long raw_rows = (rows_a - 1) / wp + 2;
+        if (raw_rows > 256) break;
+        const long long raw_bytes = 8 * raw_rows * W * 4;
+        const long long a_bytes = rows_a * 32;
+        const long long b_bytes = 9 * cpg * 32;
+        const size_t smem = static_cast<size_t>(2 * raw_bytes + 4 * a_bytes + 4 * b_bytes + 64);
+        if (smem > static_cast<size_t>(facts.smem_optin)) break;
+        long long cols = 32;
+        while (cols < 2 * T * cpg) cols *= 2;
+        gcb::Tf32Params P{};
+        P.n = static_cast<int>(N);
+        P.c = static_cast<int>(C);
+        P.h = static_cast<int>(H);
+        P.wd = static_cast<int>(W);
+        P.cpg = static_cast<int>(cpg);
+        P.groups = static_cast<int>(p->groups);
+        P.wp = static_cast<int>(wp);
+        P.tiles = static_cast<int>(tiles);
+        P.T = static_cast<int>(T);
+        P.strips = static_cast<int>(ceil_div(tiles, T));
+        const long long items = static_cast<long long>(p->groups) * N * P.strips;
+        if (items >= (1LL << 31)) break;
+        P.items = static_cast<int>(items);
+        P.chunks = static_cast<int>(cpg / 8);
+        P.rows_a = static_cast<int>(rows_a);
+        P.raw_rows = static_cast<int>(raw_rows);
+        P.raw_pitch = static_cast<int>(W);
+        P.raw_bytes = static_cast<unsigned>(raw_bytes);
+        P.a_bytes = static_cast<unsigned>(a_bytes);
+        P.b_bytes = static_cast<unsigned>(b_bytes);
+        P.tmem_cols = static_cast<unsigned>(cols);
+        best = P;
+        best_t = static_cast<int>(T);
+        best_smem = smem;
+    }
+    if (best_t == 0) return gc_error(GC_UNSUPPORTED, "3xTF32 path: no M-tile strip fits in shared memory");
+    const void *fn = tf32_kernel_for(cpg);
+    int ctas = 0;
+    st = kernel_occupancy(dev, fn, 128, best_smem, facts.smem_optin, ctas);
+    if (st != GC_OK) return st;
+    if (ctas < 1) return gc_error(GC_UNSUPPORTED, "3xTF32 path: kernel does not fit on an SM");
+    out.P = best;
+    out.fn = fn;
+    out.smem = best_smem;
+    out.grid = static_cast<int>(std::min<long long>(best.items, static_cast<long long>(facts.sms)));
+    return GC_OK;
+}
+
+int launch_tf32(const gc_shape *p, const float *x, const float *w, float *y, int dev, cudaStream_t stream) {
+    Tf32Plan plan;
+    int st = plan_tf32(p, dev, plan);
+    if (st != GC_OK) return st;
+    plan.P.x = x;
+    plan.P.w = w;
+    plan.P.y = y;
+    CUtensorMap map;
+    std::memset(&map, 0, sizeof(map));
+    st = encode_nchw_map(map, x, p->n, p->cin, p->h, p->w, plan.P.raw_pitch, plan.P.raw_rows, 8);
+    if (st != GC_OK) return st;
+    void *args[] = {&plan.P, &map};
+    cudaError_t e = cudaLaunchKernel(plan.fn, dim3(plan.grid), dim3(128), args, plan.smem, stream);
+    if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+    char buf[256];
+    std::snprintf(buf, sizeof(buf),
+                  "kernel=tf32x3 engine=tcgen05 n_cta=%d block=128 smem=%zu T=%d strips=%d items=%d chunks=%d "
+                  "rows_a=%d raw_rows=%d tmem_cols=%u",
+                  plan.grid, plan.smem, plan.P.T, plan.P.strips, plan.P.items, plan.P.chunks, plan.P.rows_a,
+                  plan.P.raw_rows, plan.P.tmem_cols);
+    g_plan = buf;
+    return GC_OK;
+}
+
 // ---- general kernel ------------------------------------------------------------------
 constexpr int kGeneralRun = 4;
 
@@ -682,6 +798,9 @@ int run_kernel(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_ten
     case GC_B200_DIRECT_TMA:
         st = launch_direct(p, xp, wp, yp, true, dev, s);
         break;
+    case GC_B200_TF32X3:
+        st = launch_tf32(p, xp, wp, yp, dev, s);
+        break;
     default:
         return gc_error(GC_UNSUPPORTED, "unknown B200 kernel family");
     }
@@ -753,8 +872,10 @@ int gc_b200_conv(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_t
     if (kernel == GC_B200_DIRECT_TMA && !tma_eligible(p, x->data))
         return gc_error(GC_UNSUPPORTED,
                         "TMA staging needs width % 4 == 0, width <= 248 and a 16-byte aligned input");
-    if (kernel == GC_B200_TF32X3)
-        return gc_error(GC_UNSUPPORTED, "3xTF32 tensor-core path is not built in this library");
+    if (kernel == GC_B200_TF32X3 && !tf32_eligible(p, x->data))
+        return gc_error(GC_UNSUPPORTED,
+                        "3xTF32 path needs 8, 16, 32 or 64 channels per group, width % 4 == 0, "
+                        "width <= 256 and a 16-byte aligned input");
     int dev = -1;
     st = device_and_stream_checks(x, w, y, stream, dev);
     if (st != GC_OK) return st;

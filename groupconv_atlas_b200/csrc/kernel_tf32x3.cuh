@@ -1,0 +1,406 @@
+// Grouped 3x3 convolution (stride 1, pad 1, Cin == Cout) as an implicit GEMM
+// on the 5th-generation tensor cores (tcgen05, accumulators in TMEM), with
+// 3xTF32 split precision so the result stays within FP32 tolerance.
+//
+// GEMM view, per (image n, group g):  D[o, co] = sum_tap sum_ci A_tap[o, ci] * B_tap[ci, co]
+//   o   : output pixel in "padded" numbering o = h * Wp + w, Wp = W + 2 (the two
+//         extra columns per row are computed and discarded);
+//   A_tap[o, ci] = Xpad[o + r*Wp + s]  for tap (r, s), where Xpad is the input
+//         with one zero row/column on every side, numbered the same way.  Every
+//         tap is therefore a pure row shift of one shared-memory tile;
+//   B_tap[ci, co] = w[g*cpg + co, ci, r, s].
+// tcgen05.mma.kind::tf32, M = 128 pixels, N = cpg output channels, K = 8 input
+// channels per instruction.  x = hi + lo with hi = tf32(x), lo = tf32(x - hi);
+// D += A_hi B_hi + A_hi B_lo + A_lo B_hi (the lo*lo term is below FP32
+// rounding of the sum).
+//
+// Work item = (group, image, strip of T consecutive 128-pixel M-tiles); pipeline
+// step = (item, chunk of 8 input channels).  Per step, one TMA box brings the
+// raw NCHW rows of the 8 channels (zero-filled outside the image) into a
+// double-buffered staging area; all threads split x and the chunk's weights into
+// hi/lo TF32 in the K-major no-swizzle canonical layout (core matrix = 8 rows x
+// 16 bytes; rows 16 bytes apart, the two 4-channel halves LBO apart), so a
+// shift by one pixel is +16 bytes of descriptor start address; one thread
+// issues 27*T MMAs and commits them to an mbarrier that frees the stage.  The
+// accumulator of item j lives in TMEM buffer j % 2, so the epilogue of item j
+// (tcgen05.ld -> coalesced streaming stores of whole output rows) overlaps the
+// MMAs of item j+1.  Every wait is bounded; on timeout the kernel records it in
+// the status word, drains what it issued, frees its TMEM and returns.
+#pragma once
+#include "device_util.cuh"
+
+namespace gcb {
+
+struct Tf32Params {
+    const float *x;
+    const float *w;
+    float *y;
+    int n, c, h, wd, cpg, groups;
+    int wp;              // padded row pitch W + 2
+    int tiles;           // 128-pixel M-tiles per image: ceil(h * wp / 128)
+    int T;               // M-tiles per item
+    int strips;          // ceil(tiles / T)
+    int items;           // groups * n * strips
+    int chunks;          // cpg / 8
+    int rows_a;          // A rows per step: T*128 + 2*wp + 2, rounded up to 8
+    int raw_rows;        // image rows staged per step
+    int raw_pitch;       // floats per staged row (the TMA box width)
+    unsigned raw_bytes;  // bytes of one staged step: 8 * raw_rows * raw_pitch * 4
+    unsigned a_bytes;    // bytes of one A tile (hi or lo): rows_a * 32
+    unsigned b_bytes;    // bytes of one B tile set (hi or lo): 9 taps * cpg * 32
+    unsigned tmem_cols;  // allocated TMEM columns (power of two)
+    int vec_ok;          // unused (stores are per element)
+};
+
+// ---- tcgen05 helpers -----------------------------------------------------------------
+__device__ __forceinline__ uint32_t tf32_rna(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+
+// Shared-memory matrix descriptor, K-major, no swizzle (canonical layout
+// ((8,m),2):((1,SBO),LBO) in 16-byte units), sm100 version bit set.
+__device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+    d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
+    d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
+    d |= 1ull << 46;  // descriptor version (Blackwell)
+    return d;         // base offset 0, absolute LBO mode 0, layout SWIZZLE_NONE (0)
+}
+
+// Instruction descriptor: D f32, A/B tf32, both K-major, M = 128, N = n.
+__host__ __device__ constexpr uint32_t umma_idesc_tf32(int n) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(n >> 3) << 17) | (8u << 24);
+}
+
+__device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate ? 1 : 0)
+        : "memory");
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_addr(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// Generic-proxy writes to shared memory become visible to the tensor core.
+__device__ __forceinline__ void fence_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t *dst_smem, uint32_t cols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_addr(dst_smem)),
+                 "r"(cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols)
+                 : "memory");
+}
+
+// 16 consecutive accumulator columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
+        "[%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+                   "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr)
+                 : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// ---- the kernel ---------------------------------------------------------------------------
+// Item order: group slowest, so consecutive items of one CTA mostly share the
+// group's weights in L1/L2.
+__device__ __forceinline__ void tf32_decode(const Tf32Params &P, int item, int &g, int &n, int &strip) {
+    const unsigned u = static_cast<unsigned>(item);
+    const unsigned t = u / static_cast<unsigned>(P.strips);
+    strip = static_cast<int>(u - t * static_cast<unsigned>(P.strips));
+    g = static_cast<int>(t / static_cast<unsigned>(P.n));
+    n = static_cast<int>(t - static_cast<unsigned>(g) * static_cast<unsigned>(P.n));
+}
+
+// First padded input row of a strip (the raw tile's row 0 is image row hp0-1).
+__device__ __forceinline__ int strip_hp0(const Tf32Params &P, int strip) {
+    return (strip * P.T * 128) / P.wp;
+}
+
+__device__ __forceinline__ void tf32_issue_tma(const Tf32Params &P, const CUtensorMap *xmap, float *raw,
+                                               uint64_t *bar, int item, int chunk) {
+    int g, n, strip;
+    tf32_decode(P, item, g, n, strip);
+    mbar_arrive_expect_tx(bar, P.raw_bytes);
+    tma_load_4d(raw, xmap, 0, strip_hp0(P, strip) - 1, g * P.cpg + chunk * 8, n, bar);
+}
+
+// Epilogue of one item: wait for the MMAs of its last step, then every warp
+// moves its 32 TMEM lanes (32 consecutive output pixels) of every M-tile to
+// global memory, one output channel per store instruction (coalesced along
+// the row).  Returns false when the wait gave up.
+template <int NCO>
+__device__ __forceinline__ bool tf32_epilogue(const Tf32Params &P, uint32_t tmem_base, int first, int stride,
+                                              int item_k, uint64_t *mma_bar, int last_step) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    bool done = true;
+    if (tid == 0) {
+        done = mbar_wait_bounded(&mma_bar[last_step & 1], static_cast<uint32_t>((last_step >> 1) & 1));
+        if (!done) raise_status(kStatusMmaTimeout);
+    }
+    if (!__syncthreads_and(done)) return false;
+    tc_fence_after();
+    int g, n, strip;
+    tf32_decode(P, first + item_k * stride, g, n, strip);
+    const int o0 = strip * P.T * 128;
+    const uint32_t acc = tmem_base + static_cast<uint32_t>((item_k & 1) * P.T * NCO);
+    const long long plane_out = static_cast<long long>(P.h) * P.wd;
+    float *yg = P.y + (static_cast<long long>(n) * P.c + static_cast<long long>(g) * P.cpg) * plane_out;
+    for (int t = 0; t < P.T; ++t) {
+        if (strip * P.T + t >= P.tiles) break;
+        const int o = o0 + t * 128 + warp * 32 + lane;
+        const int oh = o / P.wp, ow = o - oh * P.wp;
+        const bool store = oh < P.h && ow < P.wd;
+        float *yp = yg + static_cast<long long>(oh) * P.wd + ow;
+        const uint32_t taddr = acc + t * NCO + (static_cast<uint32_t>(warp * 32) << 16);
+        if (NCO % 16 == 0) {
+#pragma unroll
+            for (int c16 = 0; c16 < NCO; c16 += 16) {
+                float v[16];
+                tmem_ld16(taddr + c16, v);
+                if (store) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) st_stream(yp + (c16 + i) * plane_out, v[i]);
+                }
+            }
+        } else {
+#pragma unroll
+            for (int c8 = 0; c8 < NCO; c8 += 8) {
+                float v[8];
+                tmem_ld8(taddr + c8, v);
+                if (store) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) st_stream(yp + (c8 + i) * plane_out, v[i]);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    return true;
+}
+
+template <int NCO>
+__global__ void __launch_bounds__(128, 1) tf32x3_conv_kernel(const __grid_constant__ Tf32Params P,
+                                                             const __grid_constant__ CUtensorMap xmap) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // layout: raw[2] | a_hi[2] | a_lo[2] | b_hi[2] | b_lo[2] | barriers | tmem address
+    unsigned char *const raw0 = smem_raw;
+    unsigned char *const ahi0 = raw0 + 2 * P.raw_bytes;
+    unsigned char *const alo0 = ahi0 + 2 * P.a_bytes;
+    unsigned char *const bhi0 = alo0 + 2 * P.a_bytes;
+    unsigned char *const blo0 = bhi0 + 2 * P.b_bytes;
+    unsigned char *const q = blo0 + 2 * P.b_bytes;
+    uint64_t *tma_bar = reinterpret_cast<uint64_t *>(q);  // [2]
+    uint64_t *mma_bar = tma_bar + 2;                       // [2]
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_bar + 2);
+
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int first = blockIdx.x, stride = gridDim.x;
+    const int my_items = first < P.items ? (P.items - 1 - first) / stride + 1 : 0;
+    const int steps = my_items * P.chunks;
+    constexpr uint32_t kIdesc = umma_idesc_tf32(NCO);
+    const uint32_t lbo_a = P.rows_a * 16u;  // between the two 4-channel halves of A
+    const uint32_t lbo_b = NCO * 16u;       // between the two 4-channel halves of B
+
+    if (tid == 0) {
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&tma_bar[s], 1);
+            mbar_init(&mma_bar[s], 1);
+        }
+        fence_barrier_init();
+        prefetch_tensormap(&xmap);
+    }
+    if (warp == 0) tmem_alloc(tmem_slot, P.tmem_cols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (tid == 0)
+        for (int k = 0; k < 2 && k < steps; ++k)
+            tf32_issue_tma(P, &xmap, reinterpret_cast<float *>(raw0 + k * P.raw_bytes), &tma_bar[k], first + (k / P.chunks) * stride, k % P.chunks);
+
+    bool failed = false;
+    int waited = -1;     // last step whose staged rows were consumed
+    int issued = min(steps, 2) - 1;  // last step whose TMA load was issued
+    int committed = -1;  // last step whose MMAs were committed
+    int pending_item = -1;  // item index (per CTA) whose epilogue is still due
+    for (int k = 0; k < steps; ++k) {
+        const int s = k & 1;
+        const int item_k = k / P.chunks;
+        const int chunk = k - item_k * P.chunks;
+        const int item = first + item_k * stride;
+        int g, n, strip;
+        tf32_decode(P, item, g, n, strip);
+        const int o0 = strip * P.T * 128;
+        const int hp0 = strip_hp0(P, strip);
+
+        // Raw rows of step k landed, and the MMAs of step k-2 (the last reader
+        // of stage s) are done.
+        bool ok = true;
+        if (tid == 0) {
+            ok = mbar_wait_bounded(&tma_bar[s], static_cast<uint32_t>((k >> 1) & 1));
+            if (!ok) raise_status(kStatusTmaTimeout);
+            if (ok && k >= 2) {
+                ok = mbar_wait_bounded(&mma_bar[s], static_cast<uint32_t>(((k - 2) >> 1) & 1));
+                if (!ok) raise_status(kStatusMmaTimeout);
+            }
+        }
+        if (!__syncthreads_and(ok)) {
+            failed = true;
+            break;
+        }
+        waited = k;
+
+        unsigned char *const a_hi = ahi0 + s * P.a_bytes, *const a_lo = alo0 + s * P.a_bytes;
+        unsigned char *const b_hi = bhi0 + s * P.b_bytes, *const b_lo = blo0 + s * P.b_bytes;
+        // Weights of this chunk: thread -> (co, tap), 8 input channels each.
+        const float *wg = P.w + (static_cast<long long>(g) * P.cpg) * P.cpg * 9 + chunk * 8 * 9;
+        for (int p = tid; p < 9 * NCO; p += 128) {
+            const int co = p / 9, tap = p - co * 9;
+            const float *src = wg + co * P.cpg * 9 + tap;
+            float v[8];
+#pragma unroll
+            for (int ci = 0; ci < 8; ++ci) v[ci] = __ldg(src + ci * 9);
+            uint32_t hi[8], lo[8];
+#pragma unroll
+            for (int ci = 0; ci < 8; ++ci) {
+                hi[ci] = tf32_rna(v[ci]);
+                lo[ci] = tf32_rna(v[ci] - __uint_as_float(hi[ci]));
+            }
+            const uint32_t off = tap * NCO * 32u + co * 16u;
+            *reinterpret_cast<uint4 *>(b_hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<uint4 *>(b_hi + off + lbo_b) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+            *reinterpret_cast<uint4 *>(b_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            *reinterpret_cast<uint4 *>(b_lo + off + lbo_b) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+        }
+        // Input rows: A[o - o0] = Xpad[o] for the 8 channels of this chunk.
+        const float *rw = reinterpret_cast<const float *>(raw0 + s * P.raw_bytes);
+        const int plane = P.raw_rows * P.raw_pitch;
+        for (int i = tid; i < P.rows_a; i += 128) {
+            const int o = o0 + i;
+            const int hp = o / P.wp;
+            const int ih = hp - 1, iw = o - hp * P.wp - 1;
+            const bool valid = ih >= 0 && ih < P.h && iw >= 0 && iw < P.wd;
+            const float *src = rw + (hp - hp0) * P.raw_pitch + iw;
+            float v[8];
+#pragma unroll
+            for (int ci = 0; ci < 8; ++ci) v[ci] = valid ? src[ci * plane] : 0.0f;
+            uint32_t hi[8], lo[8];
+#pragma unroll
+            for (int ci = 0; ci < 8; ++ci) {
+                hi[ci] = tf32_rna(v[ci]);
+                lo[ci] = tf32_rna(v[ci] - __uint_as_float(hi[ci]));
+            }
+            const uint32_t off = i * 16u;
+            *reinterpret_cast<uint4 *>(a_hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+            *reinterpret_cast<uint4 *>(a_hi + off + lbo_a) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+            *reinterpret_cast<uint4 *>(a_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            *reinterpret_cast<uint4 *>(a_lo + off + lbo_a) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+        }
+        fence_async_smem();
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+
+        if (tid == 0) {
+            // Raw stage s is free again: stage step k+2.
+            if (k + 2 < steps) {
+                tf32_issue_tma(P, &xmap, reinterpret_cast<float *>(raw0 + s * P.raw_bytes), &tma_bar[s], first + ((k + 2) / P.chunks) * stride,
+                               (k + 2) % P.chunks);
+            }
+            const uint32_t acc = tmem_base + static_cast<uint32_t>((item_k & 1) * P.T * NCO);
+            const uint32_t ahi = smem_addr(a_hi), alo = smem_addr(a_lo);
+            const uint32_t bhi = smem_addr(b_hi), blo = smem_addr(b_lo);
+            for (int t = 0; t < P.T; ++t) {
+                if (strip * P.T + t >= P.tiles) break;
+                const uint32_t d = acc + t * NCO;
+#pragma unroll
+                for (int tap = 0; tap < 9; ++tap) {
+                    const int r = tap / 3, sx = tap - r * 3;
+                    const uint32_t aoff = (t * 128 + r * P.wp + sx) * 16u;
+                    const uint32_t boff = tap * NCO * 32u;
+                    const bool first_mma = chunk == 0 && tap == 0;
+                    umma_tf32(d, umma_desc(ahi + aoff, lbo_a, 128), umma_desc(bhi + boff, lbo_b, 128), kIdesc,
+                              !first_mma);
+                    umma_tf32(d, umma_desc(ahi + aoff, lbo_a, 128), umma_desc(blo + boff, lbo_b, 128), kIdesc,
+                              true);
+                    umma_tf32(d, umma_desc(alo + aoff, lbo_a, 128), umma_desc(bhi + boff, lbo_b, 128), kIdesc,
+                              true);
+                }
+            }
+            umma_commit(&mma_bar[s]);
+        }
+        if (k + 2 < steps) issued = k + 2;
+        committed = k;
+
+        // The previous item's epilogue runs while this step's MMAs execute
+        // (its accumulator is the other TMEM buffer).
+        if (chunk == 0 && pending_item >= 0) {
+            if (!tf32_epilogue<NCO>(P, tmem_base, first, stride, pending_item, mma_bar, k - 1)) {
+                failed = true;
+                break;
+            }
+            pending_item = -1;
+        }
+        if (chunk == P.chunks - 1) pending_item = item_k;
+    }
+    if (!failed && pending_item >= 0)
+        failed = !tf32_epilogue<NCO>(P, tmem_base, first, stride, pending_item, mma_bar, steps - 1);
+
+    if (failed && tid == 0) {
+        // Drain what this CTA issued (bounded) before its shared memory and
+        // TMEM are released: staged loads not yet consumed, and the MMAs of
+        // the last committed step (a commit covers all earlier MMAs).
+        for (int j = waited + 1; j <= issued; ++j)
+            mbar_wait_bounded(&tma_bar[j & 1], static_cast<uint32_t>((j >> 1) & 1), 100000000ull);
+        if (committed >= 0)
+            mbar_wait_bounded(&mma_bar[committed & 1], static_cast<uint32_t>((committed >> 1) & 1),
+                              100000000ull);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 0) tmem_dealloc(tmem_base, P.tmem_cols);
+}
+
+}  // namespace gcb

@@ -34,7 +34,11 @@ def test_golden_all_implementations(native, torch_cuda, golden_cases):
             assert_matches(c.shape, c.x, c.w, y, c.y32, label=f'{c.name} impl{impl} [{plan}]')
 
 
-@pytest.mark.parametrize('kernel', ['general', 'direct_ldg', 'direct_tma'])
+def tf32_eligible(s):
+    return s.b_geometry and s.cpg in (8, 16, 32, 64) and s.w % 4 == 0 and s.w <= 256
+
+
+@pytest.mark.parametrize('kernel', ['general', 'direct_ldg', 'direct_tma', 'tf32x3'])
 def test_golden_kernel_families(native, torch_cuda, golden_cases, kernel):
     """Each kernel family on every golden case it serves; the others must be
     refused with GC_UNSUPPORTED, never silently rerouted."""
@@ -43,6 +47,8 @@ def test_golden_kernel_families(native, torch_cuda, golden_cases, kernel):
         eligible = kernel == 'general' or c.shape.b_geometry
         if kernel == 'direct_tma':
             eligible = eligible and c.shape.w % 4 == 0
+        if kernel == 'tf32x3':
+            eligible = tf32_eligible(c.shape)
         if not eligible:
             with pytest.raises(NativeError) as err:
                 run(native, torch_cuda, c.shape, c.x, c.w, kernel=kernel)
@@ -119,3 +125,23 @@ def test_sweep_config3(native, torch_cuda):
             y, _ = run(native, torch_cuda, s, x, w, impl=3)
             p = orc.check_points(s, x, w, y)
             assert p['passed'], f'sweep points {s}'
+
+
+TF32_SHAPES = [
+    # (n, c, h, w, cpg): one/many strips, partial last strip, tails, N > 1
+    (1, 16, 8, 16, 8), (2, 32, 12, 20, 16), (1, 64, 9, 12, 32), (1, 128, 9, 12, 64),
+    (3, 64, 30, 28, 32), (2, 128, 56, 56, 64), (1, 256, 14, 16, 8), (4, 96, 7, 8, 16),
+    (1, 64, 112, 112, 16), (2, 64, 33, 44, 64),
+]
+
+
+@pytest.mark.parametrize('n,c,h,w,cpg', TF32_SHAPES)
+def test_tf32x3_tensor_core_path(native, torch_cuda, n, c, h, w, cpg):
+    """The tcgen05 3xTF32 implicit GEMM meets the FP32 acceptance bound."""
+    s = Shape(n=n, cin=c, cout=c, h=h, w=w, groups=c // cpg)
+    x, wt = inputs(s, 5)
+    y, plan = run(native, torch_cuda, s, x, wt, kernel='tf32x3')
+    assert plan.startswith('kernel=tf32x3'), plan
+    res = assert_matches(s, x, wt, y, label=f'{s} {plan}')
+    assert res['max_ratio_to_bound'] < 0.5, res
+    assert native.device_status(clear=True) == 0
