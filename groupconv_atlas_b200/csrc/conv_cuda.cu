@@ -143,6 +143,23 @@ int encode_nchw_map(CUtensorMap &map, const float *base, long long n, long long 
     return GC_OK;
 }
 
+// 2-D map over a row-major float matrix [rows][cols] (cols * 4 a multiple of
+// 16 bytes): box (bw, bh), element (col, row) coordinates.
+int encode_rows_map(CUtensorMap &map, const float *base, long long rows, long long cols, int bw, int bh) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    int st = tensor_map_encoder(encode);
+    if (st != GC_OK) return st;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 4};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(bw), static_cast<cuuint32_t>(bh)};
+    cuuint32_t estride[2] = {1, 1};
+    CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box,
+                        estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return gc_error(GC_DEVICE_ERROR, "cuTensorMapEncodeTiled failed");
+    return GC_OK;
+}
+
 // ---- direct engines: variants, planning, launch ----------------------------------
 struct Variant {
     const char *name;
@@ -585,9 +602,9 @@ bool tf32_cpg_supported(long long cpg) { return cpg == 8 || cpg == 16 || cpg == 
 // Whether the tensor-core path can serve this shape and input pointer: a
 // supported group width, a TMA-stageable row (width % 4 == 0, <= 256
 // floats, 16-byte aligned input) and 32-bit pixel indices.
-bool tf32_eligible(const gc_shape *p, const void *x) {
+bool tf32_eligible(const gc_shape *p, const void *x, const void *w) {
     const long long cpg = p->cin / p->groups;
-    return tf32_cpg_supported(cpg) && p->w % 4 == 0 && p->w <= 256 && aligned16(x) &&
+    return tf32_cpg_supported(cpg) && p->w % 4 == 0 && p->w <= 256 && aligned16(x) && aligned16(w) &&
            p->h * (p->w + 2) < (1LL << 30) && p->n < (1LL << 30) && p->cin < (1LL << 30);
 }
 
@@ -625,9 +642,11 @@ int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
         const long long raw_rows = (rows_a - 1) / wp + 2;
         if (raw_rows > 256) break;
         const long long raw_bytes = 8 * raw_rows * W * 4;
+        const long long wraw_bytes = cpg * 72 * 4;
         const long long a_bytes = rows_a * 32;
         const long long b_bytes = 9 * cpg * 32;
-        const size_t smem = static_cast<size_t>(2 * raw_bytes + 4 * a_bytes + 4 * b_bytes + 64);
+        const size_t smem =
+            static_cast<size_t>(2 * raw_bytes + 2 * wraw_bytes + 4 * a_bytes + 4 * b_bytes + 128);
         if (smem > static_cast<size_t>(facts.smem_optin)) break;
         long long cols = 32;
         while (cols < 2 * T * cpg) cols *= 2;
@@ -652,6 +671,7 @@ int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
         P.raw_bytes = static_cast<unsigned>(raw_bytes);
         P.a_bytes = static_cast<unsigned>(a_bytes);
         P.b_bytes = static_cast<unsigned>(b_bytes);
+        P.wraw_bytes = static_cast<unsigned>(wraw_bytes);
         P.tmem_cols = static_cast<unsigned>(cols);
         best = P;
         best_t = static_cast<int>(T);
@@ -660,7 +680,7 @@ int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
     if (best_t == 0) return gc_error(GC_UNSUPPORTED, "3xTF32 path: no M-tile strip fits in shared memory");
     const void *fn = tf32_kernel_for(cpg);
     int ctas = 0;
-    st = kernel_occupancy(dev, fn, 128, best_smem, facts.smem_optin, ctas);
+    st = kernel_occupancy(dev, fn, gcb::kTf32Threads, best_smem, facts.smem_optin, ctas);
     if (st != GC_OK) return st;
     if (ctas < 1) return gc_error(GC_UNSUPPORTED, "3xTF32 path: kernel does not fit on an SM");
     out.P = best;
@@ -681,12 +701,16 @@ int launch_tf32(const gc_shape *p, const float *x, const float *w, float *y, int
     std::memset(&map, 0, sizeof(map));
     st = encode_nchw_map(map, x, p->n, p->cin, p->h, p->w, plan.P.raw_pitch, plan.P.raw_rows, 8);
     if (st != GC_OK) return st;
-    void *args[] = {&plan.P, &map};
-    cudaError_t e = cudaLaunchKernel(plan.fn, dim3(plan.grid), dim3(128), args, plan.smem, stream);
+    CUtensorMap wmap;
+    std::memset(&wmap, 0, sizeof(wmap));
+    st = encode_rows_map(wmap, w, p->cout, (p->cin / p->groups) * 9, 72, plan.P.cpg);
+    if (st != GC_OK) return st;
+    void *args[] = {&plan.P, &map, &wmap};
+    cudaError_t e = cudaLaunchKernel(plan.fn, dim3(plan.grid), dim3(gcb::kTf32Threads), args, plan.smem, stream);
     if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
     char buf[256];
     std::snprintf(buf, sizeof(buf),
-                  "kernel=tf32x3 engine=tcgen05 n_cta=%d block=128 smem=%zu T=%d strips=%d items=%d chunks=%d "
+                  "kernel=tf32x3 engine=tcgen05 n_cta=%d block=320 smem=%zu T=%d strips=%d items=%d chunks=%d "
                   "rows_a=%d raw_rows=%d tmem_cols=%u",
                   plan.grid, plan.smem, plan.P.T, plan.P.strips, plan.P.items, plan.P.chunks, plan.P.rows_a,
                   plan.P.raw_rows, plan.P.tmem_cols);
@@ -811,8 +835,12 @@ int run_kernel(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_ten
     return e == cudaSuccess ? gc_error(GC_OK, "") : gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
 }
 
-// Production choice for B geometry.
-int auto_kernel(const gc_shape *p, const gc_tensor *x) {
+// Production choice for B geometry: the tensor-core path for wide groups
+// (16-64 channels; for 8 the FFMA engine is faster), else the direct engine
+// with TMA staging where the layout allows it.
+int auto_kernel(const gc_shape *p, const gc_tensor *x, const gc_tensor *w) {
+    const long long cpg = p->cin / p->groups;
+    if (cpg >= 16 && tf32_eligible(p, x->data, w->data)) return GC_B200_TF32X3;
     return tma_eligible(p, x->data) ? GC_B200_DIRECT_TMA : GC_B200_DIRECT_LDG;
 }
 
@@ -856,7 +884,7 @@ int gc_cuda_conv(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_t
     if (implementation == 1) kernel = GC_B200_DIRECT_LDG;
     if (implementation == 2)
         kernel = tma_eligible(p, x->data) ? GC_B200_DIRECT_TMA : GC_B200_DIRECT_LDG;
-    if (implementation == 3) kernel = auto_kernel(p, x);
+    if (implementation == 3) kernel = auto_kernel(p, x, w);
     return run_kernel(p, x, w, y, kernel, dev, stream, true);
 }
 
@@ -872,14 +900,14 @@ int gc_b200_conv(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_t
     if (kernel == GC_B200_DIRECT_TMA && !tma_eligible(p, x->data))
         return gc_error(GC_UNSUPPORTED,
                         "TMA staging needs width % 4 == 0, width <= 248 and a 16-byte aligned input");
-    if (kernel == GC_B200_TF32X3 && !tf32_eligible(p, x->data))
+    if (kernel == GC_B200_TF32X3 && !tf32_eligible(p, x->data, w->data))
         return gc_error(GC_UNSUPPORTED,
                         "3xTF32 path needs 8, 16, 32 or 64 channels per group, width % 4 == 0, "
-                        "width <= 256 and a 16-byte aligned input");
+                        "width <= 256 and 16-byte aligned input and weights");
     int dev = -1;
     st = device_and_stream_checks(x, w, y, stream, dev);
     if (st != GC_OK) return st;
-    if (kernel == GC_B200_AUTO) kernel = b ? auto_kernel(p, x) : GC_B200_GENERAL;
+    if (kernel == GC_B200_AUTO) kernel = b ? auto_kernel(p, x, w) : GC_B200_GENERAL;
     return run_kernel(p, x, w, y, kernel, dev, stream);
 }
 

@@ -48,8 +48,8 @@ struct Tf32Params {
     unsigned raw_bytes;  // bytes of one staged step: 8 * raw_rows * raw_pitch * 4
     unsigned a_bytes;    // bytes of one A tile (hi or lo): rows_a * 32
     unsigned b_bytes;    // bytes of one B tile set (hi or lo): 9 taps * cpg * 32
+    unsigned wraw_bytes; // bytes of one staged weight chunk: cpg * 72 * 4
     unsigned tmem_cols;  // allocated TMEM columns (power of two)
-    int vec_ok;          // unused (stores are per element)
 };
 
 // ---- tcgen05 helpers -----------------------------------------------------------------
@@ -128,6 +128,16 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, float (&v)[4]) {
+    uint32_t r[4];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr)
+                 : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 4; ++i) v[i] = __uint_as_float(r[i]);
+}
 __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
     uint32_t r[8];
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
@@ -140,9 +150,52 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
     for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// ---- the kernel ---------------------------------------------------------------------------
+// ---- warp-specialized kernel -------------------------------------------------------------
+// Roles (320 threads): warps 0-7 convert staged rows and weights to hi/lo
+// TF32 tiles and run the epilogues; warp 8 (one lane) issues the MMAs;
+// warp 9 (one lane) issues the TMA loads.  Stages are handed over through
+// full/empty mbarriers:
+//   raw_full  (TMA -> converters)  raw_empty (converters -> TMA)
+//   ab_full   (converters -> MMA)  ab_empty  (MMA commit -> converters)
+//   acc_full  (MMA commit -> epilogue)  acc_empty (epilogue -> MMA)
+// Step k uses stage k % 2 for the k/2-th time, so every wait is on parity
+// (k/2) & 1 of that stage's barrier.  Every wait is bounded and also gives up
+// as soon as another role has recorded a failure in the shared abort word.
+constexpr int kConvWarps = 8;
+constexpr int kMmaWarp = 8;
+constexpr int kTmaWarp = 9;
+constexpr int kTf32Threads = 320;
+
+__device__ __forceinline__ bool role_wait(uint64_t *bar, uint32_t parity, volatile int *abort, unsigned status) {
+    const uint32_t a = smem_addr(bar);
+    if (mbar_try_wait(a, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (true) {
+        if (mbar_try_wait(a, parity)) return true;
+        if (*abort) return false;
+        if (global_ns() - t0 > kWaitLimitNs) {
+            *abort = 1;
+            raise_status(status);
+            return false;
+        }
+    }
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// 2-D tiled load (weights viewed as [C rows][cpg*9 columns]).
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int c0, int c1, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_addr(bar))
+        : "memory");
+}
+
 // Item order: group slowest, so consecutive items of one CTA mostly share the
-// group's weights in L1/L2.
+// group's weights in L2.
 __device__ __forceinline__ void tf32_decode(const Tf32Params &P, int item, int &g, int &n, int &strip) {
     const unsigned u = static_cast<unsigned>(item);
     const unsigned t = u / static_cast<unsigned>(P.strips);
@@ -151,103 +204,98 @@ __device__ __forceinline__ void tf32_decode(const Tf32Params &P, int item, int &
     n = static_cast<int>(t - static_cast<unsigned>(g) * static_cast<unsigned>(P.n));
 }
 
-// First padded input row of a strip (the raw tile's row 0 is image row hp0-1).
+// First padded input row of a strip (the staged tile's row 0 is image row hp0-1).
 __device__ __forceinline__ int strip_hp0(const Tf32Params &P, int strip) {
     return (strip * P.T * 128) / P.wp;
 }
 
-__device__ __forceinline__ void tf32_issue_tma(const Tf32Params &P, const CUtensorMap *xmap, float *raw,
-                                               uint64_t *bar, int item, int chunk) {
+// Converter warps: epilogue of one item.  Warp w reads TMEM lanes
+// 32*(w%4).. (32 consecutive pixels of each M-tile) and output channels
+// [w/4 * NCO/2, (w/4+1) * NCO/2); one coalesced store per channel.
+template <int NCO>
+__device__ __forceinline__ void tf32_epilogue(const Tf32Params &P, uint32_t acc, int item, int warp, int lane) {
+    constexpr int HALF = NCO / 2;
     int g, n, strip;
     tf32_decode(P, item, g, n, strip);
-    mbar_arrive_expect_tx(bar, P.raw_bytes);
-    tma_load_4d(raw, xmap, 0, strip_hp0(P, strip) - 1, g * P.cpg + chunk * 8, n, bar);
-}
-
-// Epilogue of one item: wait for the MMAs of its last step, then every warp
-// moves its 32 TMEM lanes (32 consecutive output pixels) of every M-tile to
-// global memory, one output channel per store instruction (coalesced along
-// the row).  Returns false when the wait gave up.
-template <int NCO>
-__device__ __forceinline__ bool tf32_epilogue(const Tf32Params &P, uint32_t tmem_base, int first, int stride,
-                                              int item_k, uint64_t *mma_bar, int last_step) {
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    bool done = true;
-    if (tid == 0) {
-        done = mbar_wait_bounded(&mma_bar[last_step & 1], static_cast<uint32_t>((last_step >> 1) & 1));
-        if (!done) raise_status(kStatusMmaTimeout);
-    }
-    if (!__syncthreads_and(done)) return false;
-    tc_fence_after();
-    int g, n, strip;
-    tf32_decode(P, first + item_k * stride, g, n, strip);
     const int o0 = strip * P.T * 128;
-    const uint32_t acc = tmem_base + static_cast<uint32_t>((item_k & 1) * P.T * NCO);
+    const int quad = warp & 3, half = warp >> 2;
     const long long plane_out = static_cast<long long>(P.h) * P.wd;
-    float *yg = P.y + (static_cast<long long>(n) * P.c + static_cast<long long>(g) * P.cpg) * plane_out;
+    float *yg = P.y + (static_cast<long long>(n) * P.c + static_cast<long long>(g) * P.cpg + half * HALF) * plane_out;
     for (int t = 0; t < P.T; ++t) {
         if (strip * P.T + t >= P.tiles) break;
-        const int o = o0 + t * 128 + warp * 32 + lane;
+        const int o = o0 + t * 128 + quad * 32 + lane;
         const int oh = o / P.wp, ow = o - oh * P.wp;
         const bool store = oh < P.h && ow < P.wd;
         float *yp = yg + static_cast<long long>(oh) * P.wd + ow;
-        const uint32_t taddr = acc + t * NCO + (static_cast<uint32_t>(warp * 32) << 16);
-        if (NCO % 16 == 0) {
+        const uint32_t taddr = acc + t * NCO + half * HALF + (static_cast<uint32_t>(quad * 32) << 16);
+        if (HALF % 16 == 0) {
 #pragma unroll
-            for (int c16 = 0; c16 < NCO; c16 += 16) {
+            for (int c = 0; c < HALF; c += 16) {
                 float v[16];
-                tmem_ld16(taddr + c16, v);
+                tmem_ld16(taddr + c, v);
                 if (store) {
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) st_stream(yp + (c16 + i) * plane_out, v[i]);
+                    for (int i = 0; i < 16; ++i) st_stream(yp + (c + i) * plane_out, v[i]);
+                }
+            }
+        } else if (HALF % 8 == 0) {
+#pragma unroll
+            for (int c = 0; c < HALF; c += 8) {
+                float v[8];
+                tmem_ld8(taddr + c, v);
+                if (store) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) st_stream(yp + (c + i) * plane_out, v[i]);
                 }
             }
         } else {
 #pragma unroll
-            for (int c8 = 0; c8 < NCO; c8 += 8) {
-                float v[8];
-                tmem_ld8(taddr + c8, v);
+            for (int c = 0; c < HALF; c += 4) {
+                float v[4];
+                tmem_ld4(taddr + c, v);
                 if (store) {
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) st_stream(yp + (c8 + i) * plane_out, v[i]);
+                    for (int i = 0; i < 4; ++i) st_stream(yp + (c + i) * plane_out, v[i]);
                 }
             }
         }
     }
-    tc_fence_before();
-    return true;
 }
 
 template <int NCO>
-__global__ void __launch_bounds__(128, 1) tf32x3_conv_kernel(const __grid_constant__ Tf32Params P,
-                                                             const __grid_constant__ CUtensorMap xmap) {
+__global__ void __launch_bounds__(kTf32Threads, 1)
+    tf32x3_conv_kernel(const __grid_constant__ Tf32Params P, const __grid_constant__ CUtensorMap xmap,
+                       const __grid_constant__ CUtensorMap wmap) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    // layout: raw[2] | a_hi[2] | a_lo[2] | b_hi[2] | b_lo[2] | barriers | tmem address
-    unsigned char *const raw0 = smem_raw;
-    unsigned char *const ahi0 = raw0 + 2 * P.raw_bytes;
+    // layout: xraw[2] | wraw[2] | a_hi[2] | a_lo[2] | b_hi[2] | b_lo[2] | barriers | words
+    unsigned char *const xraw0 = smem_raw;
+    unsigned char *const wraw0 = xraw0 + 2 * P.raw_bytes;
+    unsigned char *const ahi0 = wraw0 + 2 * P.wraw_bytes;
     unsigned char *const alo0 = ahi0 + 2 * P.a_bytes;
     unsigned char *const bhi0 = alo0 + 2 * P.a_bytes;
     unsigned char *const blo0 = bhi0 + 2 * P.b_bytes;
-    unsigned char *const q = blo0 + 2 * P.b_bytes;
-    uint64_t *tma_bar = reinterpret_cast<uint64_t *>(q);  // [2]
-    uint64_t *mma_bar = tma_bar + 2;                       // [2]
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(mma_bar + 2);
+    uint64_t *const bars = reinterpret_cast<uint64_t *>(blo0 + 2 * P.b_bytes);
+    uint64_t *const raw_full = bars, *const raw_empty = bars + 2, *const ab_full = bars + 4,
+                    *const ab_empty = bars + 6, *const acc_full = bars + 8, *const acc_empty = bars + 10;
+    uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(bars + 12);
+    volatile int *const abort_word = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int first = blockIdx.x, stride = gridDim.x;
     const int my_items = first < P.items ? (P.items - 1 - first) / stride + 1 : 0;
     const int steps = my_items * P.chunks;
-    constexpr uint32_t kIdesc = umma_idesc_tf32(NCO);
-    const uint32_t lbo_a = P.rows_a * 16u;  // between the two 4-channel halves of A
-    const uint32_t lbo_b = NCO * 16u;       // between the two 4-channel halves of B
 
     if (tid == 0) {
         for (int s = 0; s < 2; ++s) {
-            mbar_init(&tma_bar[s], 1);
-            mbar_init(&mma_bar[s], 1);
+            mbar_init(&raw_full[s], 1);
+            mbar_init(&raw_empty[s], kConvWarps);
+            mbar_init(&ab_full[s], kConvWarps);
+            mbar_init(&ab_empty[s], 1);
+            mbar_init(&acc_full[s], 1);
+            mbar_init(&acc_empty[s], kConvWarps);
         }
+        *abort_word = 0;
         fence_barrier_init();
-        prefetch_tensormap(&xmap);
     }
     if (warp == 0) tmem_alloc(tmem_slot, P.tmem_cols);
     tc_fence_before();
@@ -255,147 +303,186 @@ __global__ void __launch_bounds__(128, 1) tf32x3_conv_kernel(const __grid_consta
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
-    if (tid == 0)
-        for (int k = 0; k < 2 && k < steps; ++k)
-            tf32_issue_tma(P, &xmap, reinterpret_cast<float *>(raw0 + k * P.raw_bytes), &tma_bar[k], first + (k / P.chunks) * stride, k % P.chunks);
-
-    bool failed = false;
-    int waited = -1;     // last step whose staged rows were consumed
-    int issued = min(steps, 2) - 1;  // last step whose TMA load was issued
-    int committed = -1;  // last step whose MMAs were committed
-    int pending_item = -1;  // item index (per CTA) whose epilogue is still due
-    for (int k = 0; k < steps; ++k) {
-        const int s = k & 1;
-        const int item_k = k / P.chunks;
-        const int chunk = k - item_k * P.chunks;
-        const int item = first + item_k * stride;
-        int g, n, strip;
-        tf32_decode(P, item, g, n, strip);
-        const int o0 = strip * P.T * 128;
-        const int hp0 = strip_hp0(P, strip);
-
-        // Raw rows of step k landed, and the MMAs of step k-2 (the last reader
-        // of stage s) are done.
-        bool ok = true;
-        if (tid == 0) {
-            ok = mbar_wait_bounded(&tma_bar[s], static_cast<uint32_t>((k >> 1) & 1));
-            if (!ok) raise_status(kStatusTmaTimeout);
-            if (ok && k >= 2) {
-                ok = mbar_wait_bounded(&mma_bar[s], static_cast<uint32_t>(((k - 2) >> 1) & 1));
-                if (!ok) raise_status(kStatusMmaTimeout);
+    if (warp == kTmaWarp) {
+        if (lane == 0) {
+            prefetch_tensormap(&xmap);
+            prefetch_tensormap(&wmap);
+            int issued = -1, released = -1;
+            for (int k = 0; k < steps; ++k) {
+                const int s = k & 1;
+                if (k >= 2) {
+                    if (!role_wait(&raw_empty[s], static_cast<uint32_t>(((k - 2) >> 1) & 1), abort_word,
+                                   kStatusTmaTimeout))
+                        break;
+                    released = k - 2;
+                }
+                const int item_k = k / P.chunks, chunk = k - item_k * P.chunks;
+                int g, n, strip;
+                tf32_decode(P, first + item_k * stride, g, n, strip);
+                mbar_arrive_expect_tx(&raw_full[s], P.raw_bytes + P.wraw_bytes);
+                tma_load_4d(xraw0 + s * P.raw_bytes, &xmap, 0, strip_hp0(P, strip) - 1, g * P.cpg + chunk * 8, n,
+                            &raw_full[s]);
+                tma_load_2d(wraw0 + s * P.wraw_bytes, &wmap, chunk * 72, g * P.cpg, &raw_full[s]);
+                issued = k;
             }
+            // Loads still in flight must land before the CTA's shared memory
+            // is released: wait (bounded) for each issued stage not yet seen
+            // complete by this warp.
+            for (int j = released + 1; j <= issued; ++j)
+                mbar_wait_bounded(&raw_full[j & 1], static_cast<uint32_t>((j >> 1) & 1), 100000000ull);
         }
-        if (!__syncthreads_and(ok)) {
-            failed = true;
-            break;
-        }
-        waited = k;
-
-        unsigned char *const a_hi = ahi0 + s * P.a_bytes, *const a_lo = alo0 + s * P.a_bytes;
-        unsigned char *const b_hi = bhi0 + s * P.b_bytes, *const b_lo = blo0 + s * P.b_bytes;
-        // Weights of this chunk: thread -> (co, tap), 8 input channels each.
-        const float *wg = P.w + (static_cast<long long>(g) * P.cpg) * P.cpg * 9 + chunk * 8 * 9;
-        for (int p = tid; p < 9 * NCO; p += 128) {
-            const int co = p / 9, tap = p - co * 9;
-            const float *src = wg + co * P.cpg * 9 + tap;
-            float v[8];
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            constexpr uint32_t kIdesc = umma_idesc_tf32(NCO);
+            const uint32_t lbo_a = P.rows_a * 16u, lbo_b = NCO * 16u;
+            int committed = -1;
+            for (int k = 0; k < steps; ++k) {
+                const int s = k & 1;
+                const int item_k = k / P.chunks, chunk = k - item_k * P.chunks;
+                if (!role_wait(&ab_full[s], static_cast<uint32_t>((k >> 1) & 1), abort_word, kStatusMmaTimeout))
+                    break;
+                if (chunk == 0 && item_k >= 2 &&
+                    !role_wait(&acc_empty[item_k & 1], static_cast<uint32_t>(((item_k - 2) >> 1) & 1), abort_word,
+                               kStatusMmaTimeout))
+                    break;
+                tc_fence_after();
+                int g, n, strip;
+                tf32_decode(P, first + item_k * stride, g, n, strip);
+                const uint32_t acc = tmem_base + static_cast<uint32_t>((item_k & 1) * P.T * NCO);
+                const uint32_t ahi = smem_addr(ahi0 + s * P.a_bytes), alo = smem_addr(alo0 + s * P.a_bytes);
+                const uint32_t bhi = smem_addr(bhi0 + s * P.b_bytes), blo = smem_addr(blo0 + s * P.b_bytes);
+                for (int t = 0; t < P.T; ++t) {
+                    if (strip * P.T + t >= P.tiles) break;
+                    const uint32_t d = acc + t * NCO;
 #pragma unroll
-            for (int ci = 0; ci < 8; ++ci) v[ci] = __ldg(src + ci * 9);
-            uint32_t hi[8], lo[8];
-#pragma unroll
-            for (int ci = 0; ci < 8; ++ci) {
-                hi[ci] = tf32_rna(v[ci]);
-                lo[ci] = tf32_rna(v[ci] - __uint_as_float(hi[ci]));
+                    for (int tap = 0; tap < 9; ++tap) {
+                        const int r = tap / 3, sx = tap - r * 3;
+                        const uint32_t aoff = (t * 128 + r * P.wp + sx) * 16u;
+                        const uint32_t boff = tap * NCO * 32u;
+                        const uint64_t dah = umma_desc(ahi + aoff, lbo_a, 128), dal = umma_desc(alo + aoff, lbo_a, 128);
+                        const uint64_t dbh = umma_desc(bhi + boff, lbo_b, 128), dbl = umma_desc(blo + boff, lbo_b, 128);
+                        umma_tf32(d, dah, dbh, kIdesc, !(chunk == 0 && tap == 0));
+                        umma_tf32(d, dah, dbl, kIdesc, true);
+                        umma_tf32(d, dal, dbh, kIdesc, true);
+                    }
+                }
+                umma_commit(&ab_empty[s]);
+                if (chunk == P.chunks - 1) umma_commit(&acc_full[item_k & 1]);
+                committed = k;
             }
-            const uint32_t off = tap * NCO * 32u + co * 16u;
-            *reinterpret_cast<uint4 *>(b_hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-            *reinterpret_cast<uint4 *>(b_hi + off + lbo_b) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
-            *reinterpret_cast<uint4 *>(b_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-            *reinterpret_cast<uint4 *>(b_lo + off + lbo_b) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+            if (committed >= 0)
+                mbar_wait_bounded(&ab_empty[committed & 1], static_cast<uint32_t>((committed >> 1) & 1),
+                                  100000000ull);
         }
-        // Input rows: A[o - o0] = Xpad[o] for the 8 channels of this chunk.
-        const float *rw = reinterpret_cast<const float *>(raw0 + s * P.raw_bytes);
-        const int plane = P.raw_rows * P.raw_pitch;
-        for (int i = tid; i < P.rows_a; i += 128) {
-            const int o = o0 + i;
-            const int hp = o / P.wp;
-            const int ih = hp - 1, iw = o - hp * P.wp - 1;
-            const bool valid = ih >= 0 && ih < P.h && iw >= 0 && iw < P.wd;
-            const float *src = rw + (hp - hp0) * P.raw_pitch + iw;
-            float v[8];
-#pragma unroll
-            for (int ci = 0; ci < 8; ++ci) v[ci] = valid ? src[ci * plane] : 0.0f;
-            uint32_t hi[8], lo[8];
-#pragma unroll
-            for (int ci = 0; ci < 8; ++ci) {
-                hi[ci] = tf32_rna(v[ci]);
-                lo[ci] = tf32_rna(v[ci] - __uint_as_float(hi[ci]));
+    } else {
+        // Converter / epilogue warps.
+        const int ctid = tid;  // 0 .. 255
+        const uint32_t lbo_a = P.rows_a * 16u, lbo_b = NCO * 16u;
+        int pending = -1;  // per-CTA item index whose epilogue is due
+        for (int k = 0; k < steps; ++k) {
+            const int s = k & 1;
+            const int item_k = k / P.chunks, chunk = k - item_k * P.chunks;
+            // Lane 0 polls; the other lanes wait in __syncwarp.
+            bool ok = true;
+            if (lane == 0) {
+                ok = role_wait(&raw_full[s], static_cast<uint32_t>((k >> 1) & 1), abort_word, kStatusTmaTimeout);
+                if (ok && k >= 2)
+                    ok = role_wait(&ab_empty[s], static_cast<uint32_t>(((k - 2) >> 1) & 1), abort_word,
+                                   kStatusMmaTimeout);
             }
-            const uint32_t off = i * 16u;
-            *reinterpret_cast<uint4 *>(a_hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-            *reinterpret_cast<uint4 *>(a_hi + off + lbo_a) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
-            *reinterpret_cast<uint4 *>(a_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-            *reinterpret_cast<uint4 *>(a_lo + off + lbo_a) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
-        }
-        fence_async_smem();
-        tc_fence_before();
-        __syncthreads();
-        tc_fence_after();
-
-        if (tid == 0) {
-            // Raw stage s is free again: stage step k+2.
-            if (k + 2 < steps) {
-                tf32_issue_tma(P, &xmap, reinterpret_cast<float *>(raw0 + s * P.raw_bytes), &tma_bar[s], first + ((k + 2) / P.chunks) * stride,
-                               (k + 2) % P.chunks);
-            }
-            const uint32_t acc = tmem_base + static_cast<uint32_t>((item_k & 1) * P.T * NCO);
-            const uint32_t ahi = smem_addr(a_hi), alo = smem_addr(a_lo);
-            const uint32_t bhi = smem_addr(b_hi), blo = smem_addr(b_lo);
-            for (int t = 0; t < P.T; ++t) {
-                if (strip * P.T + t >= P.tiles) break;
-                const uint32_t d = acc + t * NCO;
+            if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+            int g, n, strip;
+            tf32_decode(P, first + item_k * stride, g, n, strip);
+            const int o0 = strip * P.T * 128;
+            const int hp0 = strip_hp0(P, strip);
+            unsigned char *const a_hi = ahi0 + s * P.a_bytes, *const a_lo = alo0 + s * P.a_bytes;
+            unsigned char *const b_hi = bhi0 + s * P.b_bytes, *const b_lo = blo0 + s * P.b_bytes;
+            // Weights: thread -> (co, 4-channel half); the 36 staged floats
+            // [co][kg*4 .. kg*4+3][tap] are contiguous.
+            const float *wr = reinterpret_cast<const float *>(wraw0 + s * P.wraw_bytes);
+            for (int u = ctid; u < 2 * NCO; u += kConvWarps * 32) {
+                const int co = u % NCO, kg = u / NCO;
+                const float4 *src = reinterpret_cast<const float4 *>(wr + co * 72 + kg * 36);
+                float v[36];
+#pragma unroll
+                for (int i = 0; i < 9; ++i) {
+                    const float4 m = src[i];
+                    v[4 * i] = m.x;
+                    v[4 * i + 1] = m.y;
+                    v[4 * i + 2] = m.z;
+                    v[4 * i + 3] = m.w;
+                }
 #pragma unroll
                 for (int tap = 0; tap < 9; ++tap) {
-                    const int r = tap / 3, sx = tap - r * 3;
-                    const uint32_t aoff = (t * 128 + r * P.wp + sx) * 16u;
-                    const uint32_t boff = tap * NCO * 32u;
-                    const bool first_mma = chunk == 0 && tap == 0;
-                    umma_tf32(d, umma_desc(ahi + aoff, lbo_a, 128), umma_desc(bhi + boff, lbo_b, 128), kIdesc,
-                              !first_mma);
-                    umma_tf32(d, umma_desc(ahi + aoff, lbo_a, 128), umma_desc(blo + boff, lbo_b, 128), kIdesc,
-                              true);
-                    umma_tf32(d, umma_desc(alo + aoff, lbo_a, 128), umma_desc(bhi + boff, lbo_b, 128), kIdesc,
-                              true);
+                    uint32_t hi[4], lo[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float x = v[j * 9 + tap];
+                        hi[j] = tf32_rna(x);
+                        lo[j] = tf32_rna(x - __uint_as_float(hi[j]));
+                    }
+                    const uint32_t off = tap * NCO * 32u + kg * lbo_b + co * 16u;
+                    *reinterpret_cast<uint4 *>(b_hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                    *reinterpret_cast<uint4 *>(b_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
                 }
             }
-            umma_commit(&mma_bar[s]);
-        }
-        if (k + 2 < steps) issued = k + 2;
-        committed = k;
-
-        // The previous item's epilogue runs while this step's MMAs execute
-        // (its accumulator is the other TMEM buffer).
-        if (chunk == 0 && pending_item >= 0) {
-            if (!tf32_epilogue<NCO>(P, tmem_base, first, stride, pending_item, mma_bar, k - 1)) {
-                failed = true;
-                break;
+            // Input rows: A[o - o0] = Xpad[o] for the 8 channels of this chunk.
+            const float *rw = reinterpret_cast<const float *>(xraw0 + s * P.raw_bytes);
+            const int plane = P.raw_rows * P.raw_pitch;
+            for (int i = ctid; i < P.rows_a; i += kConvWarps * 32) {
+                const int o = o0 + i;
+                const int hp = o / P.wp;
+                const int ih = hp - 1, iw = o - hp * P.wp - 1;
+                const bool valid = ih >= 0 && ih < P.h && iw >= 0 && iw < P.wd;
+                const float *src = rw + (hp - hp0) * P.raw_pitch + iw;
+                float v[8];
+#pragma unroll
+                for (int ci = 0; ci < 8; ++ci) v[ci] = valid ? src[ci * plane] : 0.0f;
+                uint32_t hi[8], lo[8];
+#pragma unroll
+                for (int ci = 0; ci < 8; ++ci) {
+                    hi[ci] = tf32_rna(v[ci]);
+                    lo[ci] = tf32_rna(v[ci] - __uint_as_float(hi[ci]));
+                }
+                const uint32_t off = i * 16u;
+                *reinterpret_cast<uint4 *>(a_hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<uint4 *>(a_hi + off + lbo_a) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+                *reinterpret_cast<uint4 *>(a_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                *reinterpret_cast<uint4 *>(a_lo + off + lbo_a) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
             }
-            pending_item = -1;
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&ab_full[s]);
+                mbar_arrive(&raw_empty[s]);
+            }
+            // Epilogue of the previous item while this step's MMAs run.
+            if (chunk == 0 && pending >= 0) {
+                bool done = true;
+                if (lane == 0)
+                    done = role_wait(&acc_full[pending & 1], static_cast<uint32_t>((pending >> 1) & 1), abort_word,
+                                     kStatusMmaTimeout);
+                if (!__shfl_sync(0xffffffffu, done ? 1 : 0, 0)) break;
+                tc_fence_after();
+                tf32_epilogue<NCO>(P, tmem_base + static_cast<uint32_t>((pending & 1) * P.T * NCO),
+                                   first + pending * stride, warp, lane);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[pending & 1]);
+                pending = -1;
+            }
+            if (chunk == P.chunks - 1) pending = item_k;
         }
-        if (chunk == P.chunks - 1) pending_item = item_k;
-    }
-    if (!failed && pending_item >= 0)
-        failed = !tf32_epilogue<NCO>(P, tmem_base, first, stride, pending_item, mma_bar, steps - 1);
-
-    if (failed && tid == 0) {
-        // Drain what this CTA issued (bounded) before its shared memory and
-        // TMEM are released: staged loads not yet consumed, and the MMAs of
-        // the last committed step (a commit covers all earlier MMAs).
-        for (int j = waited + 1; j <= issued; ++j)
-            mbar_wait_bounded(&tma_bar[j & 1], static_cast<uint32_t>((j >> 1) & 1), 100000000ull);
-        if (committed >= 0)
-            mbar_wait_bounded(&mma_bar[committed & 1], static_cast<uint32_t>((committed >> 1) & 1),
-                              100000000ull);
+        bool last_ok = pending >= 0;
+        if (last_ok && lane == 0)
+            last_ok = role_wait(&acc_full[pending & 1], static_cast<uint32_t>((pending >> 1) & 1), abort_word,
+                                kStatusMmaTimeout);
+        if (__shfl_sync(0xffffffffu, last_ok ? 1 : 0, 0)) {
+            tc_fence_after();
+            tf32_epilogue<NCO>(P, tmem_base + static_cast<uint32_t>((pending & 1) * P.T * NCO),
+                               first + pending * stride, warp, lane);
+            tc_fence_before();
+        }
     }
     tc_fence_before();
     __syncthreads();
