@@ -98,6 +98,23 @@ int kernel_occupancy(int dev, const void *fn, int threads, size_t smem, int smem
     return GC_OK;
 }
 
+// Launch on the caller's stream with programmatic stream serialization: the
+// kernel may start its prologue while the previous kernel in the stream
+// drains, and waits (griddepcontrol.wait) before touching global memory.
+cudaError_t launch_pdl(const void *fn, dim3 grid, dim3 block, void **args, size_t smem, cudaStream_t stream) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
 // ---- TMA descriptor encoding ---------------------------------------------------
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::once_flag g_encode_once;
@@ -590,7 +607,7 @@ int launch_direct(const gc_shape *p, const float *x, const float *w, float *y, b
     }
     args[1] = &map;
     const void *fn = tma ? plan.var->fn_tma : plan.var->fn_ldg;
-    cudaError_t e = cudaLaunchKernel(fn, dim3(plan.grid), dim3(plan.threads), args, plan.smem, stream);
+    cudaError_t e = launch_pdl(fn, dim3(plan.grid), dim3(plan.threads), args, plan.smem, stream);
     if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
     g_plan = buf;
     return GC_OK;
@@ -706,7 +723,7 @@ int launch_tf32(const gc_shape *p, const float *x, const float *w, float *y, int
     st = encode_rows_map(wmap, w, p->cout, (p->cin / p->groups) * 9, 72, plan.P.cpg);
     if (st != GC_OK) return st;
     void *args[] = {&plan.P, &map, &wmap};
-    cudaError_t e = cudaLaunchKernel(plan.fn, dim3(plan.grid), dim3(gcb::kTf32Threads), args, plan.smem, stream);
+    cudaError_t e = launch_pdl(plan.fn, dim3(plan.grid), dim3(gcb::kTf32Threads), args, plan.smem, stream);
     if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
     char buf[256];
     std::snprintf(buf, sizeof(buf),
@@ -751,8 +768,9 @@ int launch_general(const gc_shape *p, int64_t ho, int64_t wo, const float *x, co
     const int threads = 256;
     const long long blocks = std::min<long long>(ceil_div(P.total_runs, threads),
                                                  static_cast<long long>(facts.sms) * 8);
-    gcb::general_conv_kernel<kGeneralRun><<<static_cast<unsigned>(blocks), threads, 0, stream>>>(P);
-    cudaError_t e = cudaGetLastError();
+    void *args[] = {&P};
+    cudaError_t e = launch_pdl(reinterpret_cast<const void *>(&gcb::general_conv_kernel<kGeneralRun>),
+                               dim3(static_cast<unsigned>(blocks)), dim3(threads), args, 0, stream);
     if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
     char buf[160];
     std::snprintf(buf, sizeof(buf), "kernel=general grid=%lld block=%d run=%d runs=%lld", blocks,

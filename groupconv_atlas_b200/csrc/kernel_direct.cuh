@@ -174,12 +174,17 @@ __global__ void __launch_bounds__(256) direct_conv_kernel(const __grid_constant_
     const int chan_floats = P.rows * P.pitch;
     const int xoff = (g * cpg) * chan_floats + row0 * P.pitch + col0 + 4;
 
+    if (TMA && tid == 0) {
+        for (int s = 0; s < STAGES; ++s) mbar_init(&bars[s], 1);
+        fence_barrier_init();
+        prefetch_tensormap(&xmap);
+    }
+    // Everything above touches only shared memory and parameters; global
+    // memory is read and written after the previous launch in the stream has
+    // completed.
+    griddep_wait();
+    griddep_launch_dependents();
     if (TMA) {
-        if (tid == 0) {
-            for (int s = 0; s < STAGES; ++s) mbar_init(&bars[s], 1);
-            fence_barrier_init();
-            prefetch_tensormap(&xmap);
-        }
         __syncthreads();
         if (tid == 0)
             for (int s = 0; s < STAGES && s < count; ++s)

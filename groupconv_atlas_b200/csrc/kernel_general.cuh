@@ -8,6 +8,8 @@
 #pragma once
 #include <cstdint>
 
+#include "device_util.cuh"
+
 namespace gcb {
 
 struct GeneralParams {
@@ -22,6 +24,8 @@ struct GeneralParams {
 
 template <int RUN>
 __global__ void __launch_bounds__(256) general_conv_kernel(const __grid_constant__ GeneralParams P) {
+    griddep_wait();
+    griddep_launch_dependents();
     const long long cpg = P.cin / P.groups;
     const long long opg = P.cout / P.groups;
     for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;

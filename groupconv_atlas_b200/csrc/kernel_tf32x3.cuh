@@ -302,6 +302,8 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    griddep_wait();  // global memory only after the previous launch completed
+    griddep_launch_dependents();
 
     if (warp == kTmaWarp) {
         if (lane == 0) {

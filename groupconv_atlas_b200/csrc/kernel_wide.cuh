@@ -92,12 +92,14 @@ __global__ void __launch_bounds__(256) wide_conv_kernel(const __grid_constant__ 
     const int cob = tid / (P.qcols * P.rblocks);
     const int col0 = q * 4, row0 = rb * VR;
 
+    if (TMA && tid == 0) {
+        for (int s = 0; s < STAGES; ++s) mbar_init(&bars[s], 1);
+        fence_barrier_init();
+        prefetch_tensormap(&xmap);
+    }
+    griddep_wait();
+    griddep_launch_dependents();
     if (TMA) {
-        if (tid == 0) {
-            for (int s = 0; s < STAGES; ++s) mbar_init(&bars[s], 1);
-            fence_barrier_init();
-            prefetch_tensormap(&xmap);
-        }
         __syncthreads();
         if (tid == 0)
             for (int s = 0; s < STAGES && s < count; ++s)
