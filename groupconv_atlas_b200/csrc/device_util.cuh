@@ -1,6 +1,6 @@
 // Device-side building blocks shared by the kernels: the status word, bounded
 // mbarrier waits, TMA tensor/bulk loads and cp.async copies, as inline PTX for
-// sm_100a.  No TMA load here uses cluster multicast: every copy reads this
+// sm_100a.  Every TMA load here is a plain per-CTA copy: it reads this
 // GPU's own global memory into the issuing CTA's shared memory.
 #pragma once
 #include <cstdint>
