@@ -51,7 +51,8 @@ def parse_args(argv=None):
     ap.add_argument('--warmup', type=int, default=20)
     ap.add_argument('--impl', choices=['ours', 'reference'], default='ours')
     ap.add_argument('--workload', default='config2',
-                    choices=['config1', 'config2', 'config4_leaf', 'config5_g32', 'config5_g4'])
+                    choices=['config1', 'config2', 'config4_leaf', 'config5_g32', 'config5_g4', 'config4_block',
+                             'config3'])
     ap.add_argument('--scaling', choices=['weak', 'strong'], default=None,
                     help='weak: each rank runs the full workload batch; strong: the batch is sharded')
     ap.add_argument('--batch', type=int, default=None,
@@ -587,10 +588,173 @@ def cudnn_baseline(args, torch, shape, xs, dw, sets, our_step_ms):
             'cudnn_version': torch.backends.cudnn.version()}
 
 
+def set_fp32_precision(torch):
+    """TF32 off everywhere (cuDNN and matmul), read back."""
+    if hasattr(torch.backends, 'fp32_precision'):
+        for target in (torch.backends, torch.backends.cuda.matmul, torch.backends.cudnn,
+                       torch.backends.cudnn.conv):
+            target.fp32_precision = 'ieee'
+        if torch.backends.cudnn.conv.fp32_precision != 'ieee':
+            raise SystemExit('could not disable TF32')
+    else:
+        torch.backends.cuda.matmul.allow_tf32 = False
+        torch.backends.cudnn.allow_tf32 = False
+
+
+def run_block(args):
+    """Config 4: torchvision MobileNetV2 features[3] (random Kaiming-normal
+    init, seed 2, eval), N4 input N(0,1); the reference block runs every conv
+    on cuDNN, the candidate replaces only the depthwise 3x3 by gc_cuda_conv
+    (implementation 3), as the reference's bench/module_run.py:215-235 does.
+    Reports block latency from CUDA-graph replay (device) and synchronized
+    per-call wall time (API), both blocks, same inputs."""
+    import copy
+    import torch
+    import torchvision
+    from groupconv_atlas_b200 import api, torch_module
+    from oracle import oracle as orc
+    rank, world, local = dist_setup()
+    if rank != 0:
+        return 0
+    torch.cuda.set_device(local)
+    set_fp32_precision(torch)
+    torch.backends.cudnn.benchmark = True
+    torch.manual_seed(2)
+    block = torchvision.models.mobilenet_v2(weights=None).features[3].eval().cuda()
+    cand = copy.deepcopy(block)
+    native = api.Native()
+    replaced = torch_module.substitute(cand, torch_module.is_depthwise_3x3, native)
+    x = torch.randn((4, 24, 56, 56), generator=torch.Generator().manual_seed(2)).cuda()
+    stream = torch.cuda.Stream()
+    with torch.inference_mode(), torch.cuda.stream(stream):
+        ref = block(x)
+        out = cand(x)
+        stream.synchronize()
+        check = orc.error_metrics(out.cpu().numpy(), ref.cpu().numpy())
+        if not check['passed']:
+            raise SystemExit(f'substituted block does not match the cuDNN block: {check}')
+        plan = native.last_plan()
+        results = {}
+        for name, mod in (('ours', cand), ('cudnn', block)):
+            for _ in range(20):
+                mod(x)
+            results[name + '_graph_us'] = graph_step_ms(torch, stream, lambda k, m=mod: m(x), 50) * 1e3
+            stream.synchronize()
+            t0 = time.perf_counter()
+            for _ in range(args.steps):
+                mod(x)
+                stream.synchronize()
+            results[name + '_api_us'] = (time.perf_counter() - t0) / args.steps * 1e6
+        # end to end: pinned host input -> block -> pinned host output
+        xh = x.cpu().pin_memory()
+        yh = torch.empty(tuple(out.shape), pin_memory=True)
+        xd = torch.empty_like(x)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(args.e2e_steps):
+            xd.copy_(xh, non_blocking=True)
+            yh.copy_(cand(xd), non_blocking=True)
+        b.record(stream)
+        stream.synchronize()
+        e2e_us = a.elapsed_time(b) / args.e2e_steps * 1e3
+    line = {'metric': 'MobileNetV2 features[3] block latency, depthwise 3x3 on gc_cuda_conv (config 4)',
+            'value': results['ours_graph_us'], 'unit': 'us', 'n_gpus': 1, 'steps': args.steps,
+            'warmup': 20, 'ms_per_step': results['ours_graph_us'] / 1e3, 'higher_is_better': False,
+            'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic N(0,1) input, seed 2',
+            'config': {'workload': 'config4_block', 'replaced': replaced, 'kernel_plan': plan,
+                       'input': [4, 24, 56, 56]},
+            'block': results, 'speedup_graph': results['cudnn_graph_us'] / results['ours_graph_us'],
+            'speedup_api': results['cudnn_api_us'] / results['ours_api_us'], 'check': check,
+            'e2e': {'value': e2e_us, 'unit': 'us', 'h2d_bytes_per_step': x.numel() * 4,
+                    'd2h_bytes_per_step': out.numel() * 4},
+            'gpu_launches': None}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_sweep(args):
+    """Config 3: the 80-shape sweep.  Per shape: device time of gc_cuda_conv
+    (implementation 3) and of torch.nn.functional.conv2d (TF32 off, benchmark
+    mode), both by CUDA-graph replay over rotating buffers larger than L2 where
+    the shape allows; a 64-point FP64 check of our output; the roofline
+    fraction of the bound that applies to the chosen kernel."""
+    import torch
+    import torch.nn.functional as F
+    from groupconv_atlas_b200 import api, workloads
+    from oracle import oracle as orc
+    rank, world, local = dist_setup()
+    if rank != 0:
+        return 0
+    torch.cuda.set_device(local)
+    set_fp32_precision(torch)
+    torch.backends.cudnn.benchmark = True
+    native = api.Native()
+    peaks, peak_kind = measured_peaks()
+    props = torch.cuda.get_device_properties(local)
+    ffma_peak = props.multi_processor_count * 128 * 2 * 1.965e9 / 1e12  # TFLOP/s at max SM clock
+    tensor_peak = peaks['bf16_tflops'] / 6
+    stream = torch.cuda.Stream()
+    rows = []
+    for s in workloads.sweep_shapes():
+        x_host, w_host = workloads.sweep_inputs(s, 0, 1)
+        nbytes = 4 * (2 * math.prod(s.input) + math.prod(s.weight))
+        sets = int(max(1, min(8, math.ceil(3 * L2_BYTES / nbytes))))
+        g = torch.Generator(device='cuda').manual_seed(int(s.id[3:11], 16))
+        with torch.cuda.stream(stream):
+            xs = [torch.rand(s.input, device='cuda', generator=g) * 2 - 1 for _ in range(sets)]
+            ys = [torch.empty(s.output, device='cuda') for _ in range(sets)]
+            w = torch.from_numpy(w_host).cuda()
+            native.cuda(s, xs[0], w, ys[0], 3, stream.cuda_stream)
+            plan = native.last_plan()
+            stream.synchronize()
+            check = orc.check_points(s, xs[0].cpu().numpy(), w_host, ys[0].cpu().numpy())
+            reps = 20
+            ours = graph_step_ms(torch, stream, lambda k: native.cuda(s, xs[k % sets], w, ys[k % sets], 3,
+                                                                      stream.cuda_stream), reps)
+            with torch.inference_mode():
+                for k in range(3):
+                    F.conv2d(xs[k % sets], w, padding=1, groups=s.groups)
+                theirs = graph_step_ms(torch, stream,
+                                       lambda k: F.conv2d(xs[k % sets], w, padding=1, groups=s.groups), reps)
+        flops = 2 * math.prod(s.output) * s.cpg * 9
+        gbs = nbytes / (ours / 1e3) / 1e9
+        tflops = flops / (ours / 1e3) / 1e12
+        if plan.startswith('kernel=tf32x3'):
+            bound, frac = 'tensor', tflops / tensor_peak
+        elif s.cpg >= 4:
+            bound, frac = 'fp32', max(tflops / ffma_peak, gbs / peaks['hbm_gbs'])
+        else:
+            bound, frac = 'hbm', gbs / peaks['hbm_gbs']
+        rows.append({'shape': [s.n, s.cin, s.h, s.w, s.cpg], 'us': ours * 1e3, 'cudnn_us': theirs * 1e3,
+                     'speedup_vs_cudnn': theirs / ours, 'gbs': gbs, 'tflops': tflops, 'bound': bound,
+                     'frac': frac, 'points_ok': check['passed'], 'kernel': plan.split()[0].split('=')[1]})
+        del xs, ys
+        torch.cuda.empty_cache()
+    geo = lambda v: math.exp(statistics.fmean(math.log(max(x, 1e-12)) for x in v))
+    line = {'metric': 'config-3 sweep: geomean speedup of gc_cuda_conv over torch/cuDNN (TF32 off), 80 shapes',
+            'value': geo(r['speedup_vs_cudnn'] for r in rows), 'unit': 'x', 'n_gpus': 1, 'steps': 20,
+            'warmup': 3, 'higher_is_better': True, 'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32',
+            'data': 'synthetic uniform[-1,1) inputs, weights uniform[-1,1)/sqrt(9 cpg)',
+            'config': {'workload': 'config3', 'shapes': len(rows), 'timing': 'CUDA-graph replay, both sides'},
+            'wins': sum(r['speedup_vs_cudnn'] > 1.05 for r in rows),
+            'losses': sum(r['speedup_vs_cudnn'] < 1 / 1.05 for r in rows),
+            'all_points_ok': all(r['points_ok'] for r in rows),
+            'geomean_roofline_frac': geo(r['frac'] for r in rows),
+            'peaks': {'hbm_gbs': peaks['hbm_gbs'], 'ffma_tflops': ffma_peak, 'tf32x3_tflops': tensor_peak,
+                      'source': peak_kind},
+            'rows': rows}
+    print(json.dumps(line), flush=True)
+    return 0 if line['all_points_ok'] else 1
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.impl == 'reference':
         return run_reference(args)
+    if args.workload == 'config4_block':
+        return run_block(args)
+    if args.workload == 'config3':
+        return run_sweep(args)
     return run_ours(args)
 
 

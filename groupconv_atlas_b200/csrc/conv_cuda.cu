@@ -28,6 +28,7 @@
 #include "kernel_general.cuh"
 #include "kernel_wide.cuh"
 #include "kernel_tf32x3.cuh"
+#include "kernel_small.cuh"
 
 namespace {
 
@@ -619,9 +620,14 @@ bool tf32_cpg_supported(long long cpg) { return cpg == 8 || cpg == 16 || cpg == 
 // Whether the tensor-core path can serve this shape and input pointer: a
 // supported group width, a TMA-stageable row (width % 4 == 0, <= 256
 // floats, 16-byte aligned input) and 32-bit pixel indices.
+// Images small enough to stage 8 whole planes per step with one bulk copy.
+constexpr long long kTf32BulkMaxPixels = 1024;
+
 bool tf32_eligible(const gc_shape *p, const void *x, const void *w) {
     const long long cpg = p->cin / p->groups;
-    return tf32_cpg_supported(cpg) && p->w % 4 == 0 && p->w <= 256 && aligned16(x) && aligned16(w) &&
+    const bool rows_by_tma = p->w % 4 == 0 && p->w <= 256;
+    const bool planes_by_bulk = p->h * p->w <= kTf32BulkMaxPixels;
+    return tf32_cpg_supported(cpg) && (rows_by_tma || planes_by_bulk) && aligned16(x) && aligned16(w) &&
            p->h * (p->w + 2) < (1LL << 30) && p->n < (1LL << 30) && p->cin < (1LL << 30);
 }
 
@@ -651,19 +657,22 @@ int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
     const long long N = p->n, C = p->cin, H = p->h, W = p->w, cpg = C / p->groups;
     const long long wp = W + 2;
     const long long tiles = ceil_div(H * wp, 128);
+    const bool bulk = !(W % 4 == 0 && W <= 256);  // rows not TMA-stageable: whole planes
     int best_t = 0;
+    double best_cost = 0.0;
     gcb::Tf32Params best{};
     size_t best_smem = 0;
     for (long long T = 1; T <= tiles && 2 * T * cpg <= 512; ++T) {
         const long long rows_a = round_up(T * 128 + 2 * wp + 2, 8);
-        const long long raw_rows = (rows_a - 1) / wp + 2;
+        const long long raw_rows = bulk ? H : (rows_a - 1) / wp + 2;
         if (raw_rows > 256) break;
         const long long raw_bytes = 8 * raw_rows * W * 4;
         const long long wraw_bytes = cpg * 72 * 4;
         const long long a_bytes = rows_a * 32;
         const long long b_bytes = 9 * cpg * 32;
+        const long long raw_stride = round_up(raw_bytes, 128);
         const size_t smem =
-            static_cast<size_t>(2 * raw_bytes + 2 * wraw_bytes + 4 * a_bytes + 4 * b_bytes + 128);
+            static_cast<size_t>(2 * raw_stride + 2 * wraw_bytes + 4 * a_bytes + 4 * b_bytes + 128);
         if (smem > static_cast<size_t>(facts.smem_optin)) break;
         long long cols = 32;
         while (cols < 2 * T * cpg) cols *= 2;
@@ -686,10 +695,18 @@ int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
         P.raw_rows = static_cast<int>(raw_rows);
         P.raw_pitch = static_cast<int>(W);
         P.raw_bytes = static_cast<unsigned>(raw_bytes);
+        P.raw_stride = static_cast<unsigned>(raw_stride);
         P.a_bytes = static_cast<unsigned>(a_bytes);
         P.b_bytes = static_cast<unsigned>(b_bytes);
         P.wraw_bytes = static_cast<unsigned>(wraw_bytes);
         P.tmem_cols = static_cast<unsigned>(cols);
+        P.bulk = bulk ? 1 : 0;
+        // Time model: waves of items over the SMs (one CTA each) times the
+        // work of one item, which grows with the rows it converts (T M-tiles
+        // plus the 2*Wp+2 halo rows shared by a strip).
+        const double cost = static_cast<double>(ceil_div(items, facts.sms)) * static_cast<double>(rows_a);
+        if (best_t > 0 && cost >= best_cost) continue;
+        best_cost = cost;
         best = P;
         best_t = static_cast<int>(T);
         best_smem = smem;
@@ -716,8 +733,10 @@ int launch_tf32(const gc_shape *p, const float *x, const float *w, float *y, int
     plan.P.y = y;
     CUtensorMap map;
     std::memset(&map, 0, sizeof(map));
-    st = encode_nchw_map(map, x, p->n, p->cin, p->h, p->w, plan.P.raw_pitch, plan.P.raw_rows, 8);
-    if (st != GC_OK) return st;
+    if (!plan.P.bulk) {
+        st = encode_nchw_map(map, x, p->n, p->cin, p->h, p->w, plan.P.raw_pitch, plan.P.raw_rows, 8);
+        if (st != GC_OK) return st;
+    }
     CUtensorMap wmap;
     std::memset(&wmap, 0, sizeof(wmap));
     st = encode_rows_map(wmap, w, p->cout, (p->cin / p->groups) * 9, 72, plan.P.cpg);
@@ -728,9 +747,82 @@ int launch_tf32(const gc_shape *p, const float *x, const float *w, float *y, int
     char buf[256];
     std::snprintf(buf, sizeof(buf),
                   "kernel=tf32x3 engine=tcgen05 n_cta=%d block=320 smem=%zu T=%d strips=%d items=%d chunks=%d "
-                  "rows_a=%d raw_rows=%d tmem_cols=%u",
+                  "rows_a=%d raw_rows=%d tmem_cols=%u staging=%s",
                   plan.grid, plan.smem, plan.P.T, plan.P.strips, plan.P.items, plan.P.chunks, plan.P.rows_a,
-                  plan.P.raw_rows, plan.P.tmem_cols);
+                  plan.P.raw_rows, plan.P.tmem_cols, plan.P.bulk ? "bulk" : "tma");
+    g_plan = buf;
+    return GC_OK;
+}
+
+// ---- small-image kernel ----------------------------------------------------------------------
+constexpr long long kSmallMaxPixels = 1024;
+
+bool small_eligible(const gc_shape *p) {
+    return p->h * p->w <= kSmallMaxPixels && p->n < (1LL << 30) && p->cin < (1LL << 20);
+}
+
+const void *small_kernel_for(int cob) {
+    switch (cob) {
+    case 8: return reinterpret_cast<const void *>(&gcb::small_conv_kernel<8>);
+    case 4: return reinterpret_cast<const void *>(&gcb::small_conv_kernel<4>);
+    case 2: return reinterpret_cast<const void *>(&gcb::small_conv_kernel<2>);
+    default: return reinterpret_cast<const void *>(&gcb::small_conv_kernel<1>);
+    }
+}
+
+// Channels per item: the largest block of whole groups that still leaves at
+// least two items per SM and fits 48 KB of shared memory (several CTAs per
+// SM), else the smallest (one group).
+int launch_small(const gc_shape *p, const float *x, const float *w, float *y, int dev, cudaStream_t stream) {
+    DeviceFacts facts;
+    int st = device_facts(dev, facts);
+    if (st != GC_OK) return st;
+    const long long N = p->n, C = p->cin, cpg = C / p->groups, hw = p->h * p->w;
+    const int cob = cpg % 8 == 0 ? 8 : cpg % 4 == 0 ? 4 : cpg % 2 == 0 ? 2 : 1;
+    long long best_cb = 0;
+    for (long long gpi = 1; gpi <= p->groups; ++gpi) {
+        if (p->groups % gpi) continue;
+        const long long cb = gpi * cpg;
+        const long long smem = (round_up(cb * hw, 4) + cb * cpg * 9) * 4;
+        if (smem > 48 * 1024 && best_cb != 0) break;
+        if (smem > facts.smem_optin) break;
+        const long long items = N * (C / cb);
+        if (best_cb == 0 || items >= 2LL * facts.sms) best_cb = cb;
+        if (items < 2LL * facts.sms) break;
+    }
+    if (best_cb == 0) return gc_error(GC_UNSUPPORTED, "small-image kernel: one group does not fit in shared memory");
+    gcb::SmallParams P{};
+    P.x = x;
+    P.w = w;
+    P.y = y;
+    P.n = static_cast<int>(N);
+    P.c = static_cast<int>(C);
+    P.h = static_cast<int>(p->h);
+    P.wd = static_cast<int>(p->w);
+    P.cpg = static_cast<int>(cpg);
+    P.cb = static_cast<int>(best_cb);
+    P.cblocks = static_cast<int>(C / best_cb);
+    const long long items = N * P.cblocks;
+    if (items >= (1LL << 31)) return gc_error(GC_UNSUPPORTED, "small-image kernel: too many items");
+    P.items = static_cast<int>(items);
+    P.hw = static_cast<int>(hw);
+    P.cells = static_cast<int>(best_cb / cob * hw);
+    P.x_floats = static_cast<int>(round_up(best_cb * hw, 4));
+    P.vec = (aligned16(x) && (C * hw) % 4 == 0 && (best_cb * hw) % 4 == 0) ? 1 : 0;
+    const size_t smem = static_cast<size_t>((P.x_floats + best_cb * cpg * 9) * 4);
+    const int threads = static_cast<int>(std::min<long long>(256, round_up(P.cells, 32)));
+    const void *fn = small_kernel_for(cob);
+    int ctas = 0;
+    st = kernel_occupancy(dev, fn, threads, smem, facts.smem_optin, ctas);
+    if (st != GC_OK) return st;
+    if (ctas < 1) return gc_error(GC_UNSUPPORTED, "small-image kernel: does not fit on an SM");
+    const int grid = static_cast<int>(std::min<long long>(items, static_cast<long long>(facts.sms) * ctas));
+    void *args[] = {&P};
+    cudaError_t e = launch_pdl(fn, dim3(grid), dim3(threads), args, smem, stream);
+    if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+    char buf[200];
+    std::snprintf(buf, sizeof(buf), "kernel=small grid=%d block=%d smem=%zu ctas_per_sm=%d cob=%d cb=%d items=%d vec=%d",
+                  grid, threads, smem, ctas, cob, P.cb, P.items, P.vec);
     g_plan = buf;
     return GC_OK;
 }
@@ -843,6 +935,9 @@ int run_kernel(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_ten
     case GC_B200_TF32X3:
         st = launch_tf32(p, xp, wp, yp, dev, s);
         break;
+    case GC_B200_SMALL:
+        st = launch_small(p, xp, wp, yp, dev, s);
+        break;
     default:
         return gc_error(GC_UNSUPPORTED, "unknown B200 kernel family");
     }
@@ -859,6 +954,9 @@ int run_kernel(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_ten
 int auto_kernel(const gc_shape *p, const gc_tensor *x, const gc_tensor *w) {
     const long long cpg = p->cin / p->groups;
     if (cpg >= 16 && tf32_eligible(p, x->data, w->data)) return GC_B200_TF32X3;
+    // Small planes that the TMA tiles cannot stage (or that are narrower than
+    // a TMA tile's halo) run whole planes per CTA.
+    if (small_eligible(p) && (!tma_eligible(p, x->data) || p->w <= 16)) return GC_B200_SMALL;
     return tma_eligible(p, x->data) ? GC_B200_DIRECT_TMA : GC_B200_DIRECT_LDG;
 }
 
@@ -900,8 +998,7 @@ int gc_cuda_conv(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_t
     if (st != GC_OK) return st;
     int kernel = GC_B200_GENERAL;
     if (implementation == 1) kernel = GC_B200_DIRECT_LDG;
-    if (implementation == 2)
-        kernel = tma_eligible(p, x->data) ? GC_B200_DIRECT_TMA : GC_B200_DIRECT_LDG;
+    if (implementation == 2) kernel = auto_kernel(p, x, w);  // cpg <= 4: never the tensor-core path
     if (implementation == 3) kernel = auto_kernel(p, x, w);
     return run_kernel(p, x, w, y, kernel, dev, stream, true);
 }
@@ -910,7 +1007,7 @@ int gc_b200_conv(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_t
                  int kernel, void *stream) {
     int st = gc_validate_tensors(p, x, w, y, GC_CUDA, GC_F32);
     if (st != GC_OK) return st;
-    if (kernel < GC_B200_AUTO || kernel > GC_B200_TF32X3)
+    if (kernel < GC_B200_AUTO || kernel > GC_B200_SMALL)
         return gc_error(GC_UNSUPPORTED, "unknown B200 kernel family");
     const bool b = b_geometry(p);
     if (kernel != GC_B200_GENERAL && kernel != GC_B200_AUTO && !b)
@@ -918,6 +1015,8 @@ int gc_b200_conv(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_t
     if (kernel == GC_B200_DIRECT_TMA && !tma_eligible(p, x->data))
         return gc_error(GC_UNSUPPORTED,
                         "TMA staging needs width % 4 == 0, width <= 248 and a 16-byte aligned input");
+    if (kernel == GC_B200_SMALL && !small_eligible(p))
+        return gc_error(GC_UNSUPPORTED, "small-image kernel needs at most 1024 pixels per plane");
     if (kernel == GC_B200_TF32X3 && !tf32_eligible(p, x->data, w->data))
         return gc_error(GC_UNSUPPORTED,
                         "3xTF32 path needs 8, 16, 32 or 64 channels per group, width % 4 == 0, "

@@ -1,0 +1,95 @@
+// Grouped 3x3 convolution (stride 1, pad 1, Cin == Cout) for small images
+// (a few hundred pixels per plane, e.g. 7x7 and 14x14), where whole planes
+// are the natural unit and the row-band machinery of the direct engine costs
+// more than the work.  Any width, any alignment.
+//
+// Work item = (image n, block of `cb` channels made of whole groups).  The
+// item's input planes are one contiguous block of cb*H*W floats in global
+// memory (NCHW), and so are its output planes: the CTA copies the input block
+// into shared memory with coalesced 16-byte loads (4-byte when unaligned),
+// the weights beside it, and every thread then owns one output pixel of COB
+// consecutive output channels.  The nine tap offsets and their in-image
+// predicates depend only on the pixel, so they are computed once per thread
+// and reused for every input channel and output channel; each input value
+// read from shared memory feeds COB FMAs; weights are warp-broadcast reads.
+// Output stores are coalesced (consecutive threads, consecutive pixels).
+#pragma once
+#include "device_util.cuh"
+
+namespace gcb {
+
+struct SmallParams {
+    const float *x;
+    const float *w;
+    float *y;
+    int n, c, h, wd, cpg;
+    int cb;          // channels per item (whole groups)
+    int cblocks;     // c / cb
+    int items;       // n * cblocks
+    int hw;          // h * wd
+    int cells;       // (cb / COB) * hw
+    int x_floats;    // cb * hw rounded up to 4
+    int vec;         // 16-byte loads allowed for the input block
+};
+
+template <int COB>
+__global__ void __launch_bounds__(256) small_conv_kernel(const __grid_constant__ SmallParams P) {
+    extern __shared__ __align__(16) float smem[];
+    float *xs = smem;
+    float *ws = smem + P.x_floats;
+    const int cpg = P.cpg;
+    const int wcount = P.cb * cpg * 9;
+    griddep_wait();
+    griddep_launch_dependents();
+    for (int item = blockIdx.x; item < P.items; item += gridDim.x) {
+        const int nn = item / P.cblocks;
+        const int c0 = (item - nn * P.cblocks) * P.cb;
+        const long long base = (static_cast<long long>(nn) * P.c + c0) * P.hw;
+        __syncthreads();  // the previous item's readers are done
+        const int total = P.cb * P.hw;
+        if (P.vec) {
+            const float4 *src = reinterpret_cast<const float4 *>(P.x + base);
+            float4 *dst = reinterpret_cast<float4 *>(xs);
+            for (int e = threadIdx.x; e < total / 4; e += blockDim.x) dst[e] = __ldg(src + e);
+        } else {
+            for (int e = threadIdx.x; e < total; e += blockDim.x) xs[e] = __ldg(P.x + base + e);
+        }
+        const float *wsrc = P.w + static_cast<long long>(c0) * cpg * 9;
+        for (int e = threadIdx.x; e < wcount; e += blockDim.x) ws[e] = __ldg(wsrc + e);
+        __syncthreads();
+        for (int cell = threadIdx.x; cell < P.cells; cell += blockDim.x) {
+            const int cob = cell / P.hw;
+            const int p = cell - cob * P.hw;
+            const int oh = p / P.wd, ow = p - oh * P.wd;
+            const int co0 = cob * COB;      // item-local first output channel
+            const int g = co0 / cpg;        // item-local group
+            int off[9];
+            bool ok[9];
+#pragma unroll
+            for (int tap = 0; tap < 9; ++tap) {
+                const int ih = oh + tap / 3 - 1, iw = ow + tap % 3 - 1;
+                ok[tap] = ih >= 0 && ih < P.h && iw >= 0 && iw < P.wd;
+                off[tap] = ok[tap] ? ih * P.wd + iw : 0;
+            }
+            float acc[COB];
+#pragma unroll
+            for (int j = 0; j < COB; ++j) acc[j] = 0.0f;
+            const float *xg = xs + g * cpg * P.hw;
+            const float *wg = ws + co0 * cpg * 9;
+            for (int ci = 0; ci < cpg; ++ci) {
+                const float *xc = xg + ci * P.hw;
+#pragma unroll
+                for (int tap = 0; tap < 9; ++tap) {
+                    const float xv = ok[tap] ? xc[off[tap]] : 0.0f;
+#pragma unroll
+                    for (int j = 0; j < COB; ++j) acc[j] = fmaf(xv, wg[(j * cpg + ci) * 9 + tap], acc[j]);
+                }
+            }
+            float *yp = P.y + base + static_cast<long long>(co0) * P.hw + p;
+#pragma unroll
+            for (int j = 0; j < COB; ++j) st_stream(yp + static_cast<long long>(j) * P.hw, acc[j]);
+        }
+    }
+}
+
+}  // namespace gcb

@@ -46,10 +46,14 @@ struct Tf32Params {
     int raw_rows;        // image rows staged per step
     int raw_pitch;       // floats per staged row (the TMA box width)
     unsigned raw_bytes;  // bytes of one staged step: 8 * raw_rows * raw_pitch * 4
+    unsigned raw_stride; // shared-memory bytes reserved per staged step (raw_bytes rounded to 128)
     unsigned a_bytes;    // bytes of one A tile (hi or lo): rows_a * 32
     unsigned b_bytes;    // bytes of one B tile set (hi or lo): 9 taps * cpg * 32
     unsigned wraw_bytes; // bytes of one staged weight chunk: cpg * 72 * 4
     unsigned tmem_cols;  // allocated TMEM columns (power of two)
+    int bulk;            // 1: stage the 8 channels' whole planes with one contiguous
+                         //    bulk copy (rows start at image row 0); 0: TMA box from
+                         //    image row hp0-1 (zero-filled outside the image)
 };
 
 // ---- tcgen05 helpers -----------------------------------------------------------------
@@ -269,7 +273,7 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     // layout: xraw[2] | wraw[2] | a_hi[2] | a_lo[2] | b_hi[2] | b_lo[2] | barriers | words
     unsigned char *const xraw0 = smem_raw;
-    unsigned char *const wraw0 = xraw0 + 2 * P.raw_bytes;
+    unsigned char *const wraw0 = xraw0 + 2 * P.raw_stride;
     unsigned char *const ahi0 = wraw0 + 2 * P.wraw_bytes;
     unsigned char *const alo0 = ahi0 + 2 * P.a_bytes;
     unsigned char *const bhi0 = alo0 + 2 * P.a_bytes;
@@ -322,8 +326,13 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
                 int g, n, strip;
                 tf32_decode(P, first + item_k * stride, g, n, strip);
                 mbar_arrive_expect_tx(&raw_full[s], P.raw_bytes + P.wraw_bytes);
-                tma_load_4d(xraw0 + s * P.raw_bytes, &xmap, 0, strip_hp0(P, strip) - 1, g * P.cpg + chunk * 8, n,
-                            &raw_full[s]);
+                if (P.bulk) {
+                    const long long plane0 = static_cast<long long>(n) * P.c + g * P.cpg + chunk * 8;
+                    bulk_load(xraw0 + s * P.raw_stride, P.x + plane0 * P.h * P.wd, P.raw_bytes, &raw_full[s]);
+                } else {
+                    tma_load_4d(xraw0 + s * P.raw_stride, &xmap, 0, strip_hp0(P, strip) - 1, g * P.cpg + chunk * 8,
+                                n, &raw_full[s]);
+                }
                 tma_load_2d(wraw0 + s * P.wraw_bytes, &wmap, chunk * 72, g * P.cpg, &raw_full[s]);
                 issued = k;
             }
@@ -396,7 +405,8 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
             int g, n, strip;
             tf32_decode(P, first + item_k * stride, g, n, strip);
             const int o0 = strip * P.T * 128;
-            const int hp0 = strip_hp0(P, strip);
+            // image row held by staged row 0
+            const int row0 = P.bulk ? 0 : strip_hp0(P, strip) - 1;
             unsigned char *const a_hi = ahi0 + s * P.a_bytes, *const a_lo = alo0 + s * P.a_bytes;
             unsigned char *const b_hi = bhi0 + s * P.b_bytes, *const b_lo = blo0 + s * P.b_bytes;
             // Weights: thread -> (co, 4-channel half); the 36 staged floats
@@ -429,14 +439,14 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
                 }
             }
             // Input rows: A[o - o0] = Xpad[o] for the 8 channels of this chunk.
-            const float *rw = reinterpret_cast<const float *>(xraw0 + s * P.raw_bytes);
+            const float *rw = reinterpret_cast<const float *>(xraw0 + s * P.raw_stride);
             const int plane = P.raw_rows * P.raw_pitch;
             for (int i = ctid; i < P.rows_a; i += kConvWarps * 32) {
                 const int o = o0 + i;
                 const int hp = o / P.wp;
                 const int ih = hp - 1, iw = o - hp * P.wp - 1;
                 const bool valid = ih >= 0 && ih < P.h && iw >= 0 && iw < P.wd;
-                const float *src = rw + (hp - hp0) * P.raw_pitch + iw;
+                const float *src = rw + (ih - row0) * P.raw_pitch + iw;
                 float v[8];
 #pragma unroll
                 for (int ci = 0; ci < 8; ++ci) v[ci] = valid ? src[ci * plane] : 0.0f;

@@ -35,10 +35,11 @@ def test_golden_all_implementations(native, torch_cuda, golden_cases):
 
 
 def tf32_eligible(s):
-    return s.b_geometry and s.cpg in (8, 16, 32, 64) and s.w % 4 == 0 and s.w <= 256
+    rows_by_tma = s.w % 4 == 0 and s.w <= 256
+    return s.b_geometry and s.cpg in (8, 16, 32, 64) and (rows_by_tma or s.h * s.w <= 1024)
 
 
-@pytest.mark.parametrize('kernel', ['general', 'direct_ldg', 'direct_tma', 'tf32x3'])
+@pytest.mark.parametrize('kernel', ['general', 'direct_ldg', 'direct_tma', 'tf32x3', 'small'])
 def test_golden_kernel_families(native, torch_cuda, golden_cases, kernel):
     """Each kernel family on every golden case it serves; the others must be
     refused with GC_UNSUPPORTED, never silently rerouted."""
@@ -49,6 +50,8 @@ def test_golden_kernel_families(native, torch_cuda, golden_cases, kernel):
             eligible = eligible and c.shape.w % 4 == 0
         if kernel == 'tf32x3':
             eligible = tf32_eligible(c.shape)
+        if kernel == 'small':
+            eligible = c.shape.b_geometry and c.shape.h * c.shape.w <= 1024
         if not eligible:
             with pytest.raises(NativeError) as err:
                 run(native, torch_cuda, c.shape, c.x, c.w, kernel=kernel)
@@ -71,7 +74,7 @@ SMALL_B = [
 
 
 @pytest.mark.parametrize('n,c,h,w,cpg', SMALL_B)
-@pytest.mark.parametrize('kernel', ['direct_ldg', 'direct_tma', 'auto'])
+@pytest.mark.parametrize('kernel', ['direct_ldg', 'direct_tma', 'small', 'auto'])
 def test_b_geometry_shapes(native, torch_cuda, n, c, h, w, cpg, kernel):
     s = Shape(n=n, cin=c, cout=c, h=h, w=w, groups=c // cpg)
     x, wt = inputs(s, 7)
@@ -79,6 +82,8 @@ def test_b_geometry_shapes(native, torch_cuda, n, c, h, w, cpg, kernel):
         pytest.skip('TMA staging needs width % 4 == 0')
     if kernel == 'direct_tma' and w + 8 > 256:
         pytest.skip('TMA box is at most 256 columns')
+    if kernel == 'small' and h * w > 1024:
+        pytest.skip('small-image kernel serves at most 1024 pixels per plane')
     y, plan = run(native, torch_cuda, s, x, wt, kernel=kernel)
     assert_matches(s, x, wt, y, label=f'{s} {plan}')
 
@@ -132,6 +137,8 @@ TF32_SHAPES = [
     (1, 16, 8, 16, 8), (2, 32, 12, 20, 16), (1, 64, 9, 12, 32), (1, 128, 9, 12, 64),
     (3, 64, 30, 28, 32), (2, 128, 56, 56, 64), (1, 256, 14, 16, 8), (4, 96, 7, 8, 16),
     (1, 64, 112, 112, 16), (2, 64, 33, 44, 64),
+    # whole-plane bulk staging (width not TMA-stageable)
+    (3, 128, 7, 7, 64), (2, 64, 14, 14, 32), (1, 32, 13, 11, 16), (4, 16, 9, 5, 8), (1, 64, 30, 30, 64),
 ]
 
 
