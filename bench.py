@@ -55,6 +55,8 @@ def parse_args(argv=None):
                              'config3'])
     ap.add_argument('--scaling', choices=['weak', 'strong'], default=None,
                     help='weak: each rank runs the full workload batch; strong: the batch is sharded')
+    ap.add_argument('--shape', default=None,
+                    help='N,C,H,W,CPG: a custom 3x3/s1/p1 shape (uniform inputs) instead of --workload')
     ap.add_argument('--batch', type=int, default=None,
                     help='override the workload batch (small cases for profiling)')
     ap.add_argument('--e2e-steps', type=int, default=20)
@@ -65,6 +67,8 @@ def parse_args(argv=None):
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error('--warmup must be at least 3')
+    if args.shape:
+        args.workload = 'custom:' + args.shape
     if args.scaling is None:
         args.scaling = 'strong' if args.workload.startswith('config5') else 'weak'
     return args

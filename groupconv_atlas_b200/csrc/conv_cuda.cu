@@ -755,7 +755,7 @@ int launch_tf32(const gc_shape *p, const float *x, const float *w, float *y, int
 }
 
 // ---- small-image kernel ----------------------------------------------------------------------
-constexpr long long kSmallMaxPixels = 1024;
+constexpr long long kSmallMaxPixels = 512;  // one thread per pixel: at most 512 threads
 
 bool small_eligible(const gc_shape *p) {
     return p->h * p->w <= kSmallMaxPixels && p->n < (1LL << 30) && p->cin < (1LL << 20);
@@ -806,11 +806,13 @@ int launch_small(const gc_shape *p, const float *x, const float *w, float *y, in
     if (items >= (1LL << 31)) return gc_error(GC_UNSUPPORTED, "small-image kernel: too many items");
     P.items = static_cast<int>(items);
     P.hw = static_cast<int>(hw);
-    P.cells = static_cast<int>(best_cb / cob * hw);
+    P.hwp = static_cast<int>(round_up(hw, 32));
     P.x_floats = static_cast<int>(round_up(best_cb * hw, 4));
     P.vec = (aligned16(x) && (C * hw) % 4 == 0 && (best_cb * hw) % 4 == 0) ? 1 : 0;
     const size_t smem = static_cast<size_t>((P.x_floats + best_cb * cpg * 9) * 4);
-    const int threads = static_cast<int>(std::min<long long>(256, round_up(P.cells, 32)));
+    // pixel slots per CTA: up to 256 threads, never more slots than channel blocks
+    const long long slots = std::max<long long>(1, std::min<long long>(256 / P.hwp, best_cb / cob));
+    const int threads = static_cast<int>(slots * P.hwp);
     const void *fn = small_kernel_for(cob);
     int ctas = 0;
     st = kernel_occupancy(dev, fn, threads, smem, facts.smem_optin, ctas);
@@ -1016,7 +1018,7 @@ int gc_b200_conv(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_t
         return gc_error(GC_UNSUPPORTED,
                         "TMA staging needs width % 4 == 0, width <= 248 and a 16-byte aligned input");
     if (kernel == GC_B200_SMALL && !small_eligible(p))
-        return gc_error(GC_UNSUPPORTED, "small-image kernel needs at most 1024 pixels per plane");
+        return gc_error(GC_UNSUPPORTED, "small-image kernel needs at most 512 pixels per plane");
     if (kernel == GC_B200_TF32X3 && !tf32_eligible(p, x->data, w->data))
         return gc_error(GC_UNSUPPORTED,
                         "3xTF32 path needs 8, 16, 32 or 64 channels per group, width % 4 == 0, "

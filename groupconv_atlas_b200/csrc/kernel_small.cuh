@@ -27,18 +27,35 @@ struct SmallParams {
     int cblocks;     // c / cb
     int items;       // n * cblocks
     int hw;          // h * wd
-    int cells;       // (cb / COB) * hw
+    int hwp;         // hw rounded up to a whole warp: threads per pixel slot
     int x_floats;    // cb * hw rounded up to 4
     int vec;         // 16-byte loads allowed for the input block
 };
 
+// Threads are laid out as blockDim.x / hwp slots of hwp threads; thread
+// (slot, p) owns pixel p for the whole kernel (tap offsets and in-image
+// predicates computed once) and walks the item's output-channel blocks
+// slot, slot + slots, ...
 template <int COB>
-__global__ void __launch_bounds__(256) small_conv_kernel(const __grid_constant__ SmallParams P) {
+__global__ void __launch_bounds__(512) small_conv_kernel(const __grid_constant__ SmallParams P) {
     extern __shared__ __align__(16) float smem[];
     float *xs = smem;
     float *ws = smem + P.x_floats;
     const int cpg = P.cpg;
     const int wcount = P.cb * cpg * 9;
+    const int slots = blockDim.x / P.hwp;
+    const int p = threadIdx.x % P.hwp, slot = threadIdx.x / P.hwp;
+    const bool active = p < P.hw && slot < slots;
+    const int oh = p / P.wd, ow = p - oh * P.wd;
+    int off[9];
+    bool ok[9];
+#pragma unroll
+    for (int tap = 0; tap < 9; ++tap) {
+        const int ih = oh + tap / 3 - 1, iw = ow + tap % 3 - 1;
+        ok[tap] = active && ih >= 0 && ih < P.h && iw >= 0 && iw < P.wd;
+        off[tap] = ok[tap] ? ih * P.wd + iw : 0;
+    }
+    const int ncob = P.cb / COB;
     griddep_wait();
     griddep_launch_dependents();
     for (int item = blockIdx.x; item < P.items; item += gridDim.x) {
@@ -57,20 +74,11 @@ __global__ void __launch_bounds__(256) small_conv_kernel(const __grid_constant__
         const float *wsrc = P.w + static_cast<long long>(c0) * cpg * 9;
         for (int e = threadIdx.x; e < wcount; e += blockDim.x) ws[e] = __ldg(wsrc + e);
         __syncthreads();
-        for (int cell = threadIdx.x; cell < P.cells; cell += blockDim.x) {
-            const int cob = cell / P.hw;
-            const int p = cell - cob * P.hw;
-            const int oh = p / P.wd, ow = p - oh * P.wd;
-            const int co0 = cob * COB;      // item-local first output channel
-            const int g = co0 / cpg;        // item-local group
-            int off[9];
-            bool ok[9];
-#pragma unroll
-            for (int tap = 0; tap < 9; ++tap) {
-                const int ih = oh + tap / 3 - 1, iw = ow + tap % 3 - 1;
-                ok[tap] = ih >= 0 && ih < P.h && iw >= 0 && iw < P.wd;
-                off[tap] = ok[tap] ? ih * P.wd + iw : 0;
-            }
+        if (!active) continue;
+        float *yp0 = P.y + base + p;
+        for (int cob = slot; cob < ncob; cob += slots) {
+            const int co0 = cob * COB;  // item-local first output channel
+            const int g = co0 / cpg;    // item-local group
             float acc[COB];
 #pragma unroll
             for (int j = 0; j < COB; ++j) acc[j] = 0.0f;
@@ -78,16 +86,16 @@ __global__ void __launch_bounds__(256) small_conv_kernel(const __grid_constant__
             const float *wg = ws + co0 * cpg * 9;
             for (int ci = 0; ci < cpg; ++ci) {
                 const float *xc = xg + ci * P.hw;
+                const float *wc = wg + ci * 9;
 #pragma unroll
                 for (int tap = 0; tap < 9; ++tap) {
                     const float xv = ok[tap] ? xc[off[tap]] : 0.0f;
 #pragma unroll
-                    for (int j = 0; j < COB; ++j) acc[j] = fmaf(xv, wg[(j * cpg + ci) * 9 + tap], acc[j]);
+                    for (int j = 0; j < COB; ++j) acc[j] = fmaf(xv, wc[j * cpg * 9 + tap], acc[j]);
                 }
             }
-            float *yp = P.y + base + static_cast<long long>(co0) * P.hw + p;
 #pragma unroll
-            for (int j = 0; j < COB; ++j) st_stream(yp + static_cast<long long>(j) * P.hw, acc[j]);
+            for (int j = 0; j < COB; ++j) st_stream(yp0 + static_cast<long long>(co0 + j) * P.hw, acc[j]);
         }
     }
 }

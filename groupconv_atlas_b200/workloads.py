@@ -95,7 +95,16 @@ def config5(groups=32, batch=None, with_x=True):
                  'uniform', batch, with_x)
 
 
+def custom(spec, batch=None, with_x=True):
+    """'N,C,H,W,CPG' -> a 3x3/s1/p1 shape with uniform inputs (seed from its id)."""
+    n, c, h, w, cpg = (int(v) for v in spec.split(','))
+    shape = Shape(n=n, cin=c, cout=c, h=h, w=w, groups=c // cpg)
+    return _make('custom:' + spec, shape, int(shape.id[3:11], 16), 'uniform', batch, with_x)
+
+
 def by_name(name, batch=None, with_x=True):
+    if name.startswith('custom:'):
+        return custom(name.split(':', 1)[1], batch, with_x)
     if name == 'config1':
         return config1(batch, with_x)
     if name == 'config2':

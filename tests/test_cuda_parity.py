@@ -51,7 +51,7 @@ def test_golden_kernel_families(native, torch_cuda, golden_cases, kernel):
         if kernel == 'tf32x3':
             eligible = tf32_eligible(c.shape)
         if kernel == 'small':
-            eligible = c.shape.b_geometry and c.shape.h * c.shape.w <= 1024
+            eligible = c.shape.b_geometry and c.shape.h * c.shape.w <= 512
         if not eligible:
             with pytest.raises(NativeError) as err:
                 run(native, torch_cuda, c.shape, c.x, c.w, kernel=kernel)
@@ -82,8 +82,8 @@ def test_b_geometry_shapes(native, torch_cuda, n, c, h, w, cpg, kernel):
         pytest.skip('TMA staging needs width % 4 == 0')
     if kernel == 'direct_tma' and w + 8 > 256:
         pytest.skip('TMA box is at most 256 columns')
-    if kernel == 'small' and h * w > 1024:
-        pytest.skip('small-image kernel serves at most 1024 pixels per plane')
+    if kernel == 'small' and h * w > 512:
+        pytest.skip('small-image kernel serves at most 512 pixels per plane')
     y, plan = run(native, torch_cuda, s, x, wt, kernel=kernel)
     assert_matches(s, x, wt, y, label=f'{s} {plan}')
 
