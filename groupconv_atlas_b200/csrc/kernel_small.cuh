@@ -37,7 +37,7 @@ struct SmallParams {
 // predicates computed once) and walks the item's output-channel blocks
 // slot, slot + slots, ...
 template <int COB>
-__global__ void __launch_bounds__(512) small_conv_kernel(const __grid_constant__ SmallParams P) {
+__global__ void __launch_bounds__(512, 1) small_conv_kernel(const __grid_constant__ SmallParams P) {
     extern __shared__ __align__(16) float smem[];
     float *xs = smem;
     float *ws = smem + P.x_floats;
@@ -47,13 +47,15 @@ __global__ void __launch_bounds__(512) small_conv_kernel(const __grid_constant__
     const int p = threadIdx.x % P.hwp, slot = threadIdx.x / P.hwp;
     const bool active = p < P.hw && slot < slots;
     const int oh = p / P.wd, ow = p - oh * P.wd;
+    // Tap offsets (0 for taps outside the image) and a 9-bit in-image mask.
     int off[9];
-    bool ok[9];
+    unsigned okmask = 0;
 #pragma unroll
     for (int tap = 0; tap < 9; ++tap) {
         const int ih = oh + tap / 3 - 1, iw = ow + tap % 3 - 1;
-        ok[tap] = active && ih >= 0 && ih < P.h && iw >= 0 && iw < P.wd;
-        off[tap] = ok[tap] ? ih * P.wd + iw : 0;
+        const bool in = active && ih >= 0 && ih < P.h && iw >= 0 && iw < P.wd;
+        okmask |= in ? (1u << tap) : 0u;
+        off[tap] = in ? ih * P.wd + iw : 0;
     }
     const int ncob = P.cb / COB;
     griddep_wait();
@@ -89,7 +91,7 @@ __global__ void __launch_bounds__(512) small_conv_kernel(const __grid_constant__
                 const float *wc = wg + ci * 9;
 #pragma unroll
                 for (int tap = 0; tap < 9; ++tap) {
-                    const float xv = ok[tap] ? xc[off[tap]] : 0.0f;
+                    const float xv = (okmask >> tap) & 1u ? xc[off[tap]] : 0.0f;
 #pragma unroll
                     for (int j = 0; j < COB; ++j) acc[j] = fmaf(xv, wc[j * cpg * 9 + tap], acc[j]);
                 }
