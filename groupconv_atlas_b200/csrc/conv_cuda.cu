@@ -184,20 +184,27 @@ struct Variant {
     int cob, vr;
     const void *fn_tma;
     const void *fn_ldg;
+    bool ws;  // TMA staging runs the warp-specialized kernel (else CTA-synchronous)
 };
 
+// TMA staging: depthwise layers run the CTA-synchronous kernel (measured
+// faster on HBM-bound shapes), grouped layers the warp-specialized one.
 template <int CPG, int COB, int VR>
 Variant make_variant(const char *name) {
-    return Variant{name, COB, VR,
-                   reinterpret_cast<const void *>(&gcb::direct_conv_kernel<CPG, COB, VR, true>),
-                   reinterpret_cast<const void *>(&gcb::direct_conv_kernel<CPG, COB, VR, false>)};
+    const void *tma_fn;
+    if constexpr (CPG == 1)
+        tma_fn = reinterpret_cast<const void *>(&gcb::direct_conv_kernel<CPG, COB, VR, true>);
+    else
+        tma_fn = reinterpret_cast<const void *>(&gcb::direct_ws_kernel<CPG, COB, VR>);
+    return Variant{name, COB, VR, tma_fn,
+                   reinterpret_cast<const void *>(&gcb::direct_conv_kernel<CPG, COB, VR, false>), CPG != 1};
 }
 
 template <int COB, int VR>
 Variant make_wide(const char *name) {
     return Variant{name, COB, VR,
                    reinterpret_cast<const void *>(&gcb::wide_conv_kernel<COB, VR, true, kStages>),
-                   reinterpret_cast<const void *>(&gcb::wide_conv_kernel<COB, VR, false, kStages>)};
+                   reinterpret_cast<const void *>(&gcb::wide_conv_kernel<COB, VR, false, kStages>), false};
 }
 
 // Full-group kernel variants that can serve a group width (first = preferred).
@@ -368,7 +375,13 @@ int plan_small(const gc_shape *p, bool tma, bool w_aligned, bool y_aligned, int 
                 const long long bands = ceil_div(H, bh);
                 const long long items = N * (C / cb) * bands;
                 if (items >= (1LL << 31)) continue;
-                const int threads = static_cast<int>(round_up(cells, 32));
+                const int bulk_w = (tma && w_aligned && (cb * cpg) % 4 == 0) ? 1 : 0;
+                const bool ws = tma && var.ws;
+                // the warp-specialized kernel adds the copy warp and, when
+                // weights need work, the weight warp
+                const int threads = static_cast<int>(round_up(cells, 32)) +
+                                    (ws ? 32 * gcb::direct_ws_producer_warps(static_cast<int>(cpg), bulk_w) : 0);
+                if (threads > (ws ? gcb::kWsMaxThreads : 256)) continue;
                 const int pitch = choose_pitch(static_cast<int>(W), static_cast<int>(qcols),
                                                static_cast<int>(rblocks), vr, static_cast<int>(rows),
                                                static_cast<int>(cells), var.cob, static_cast<int>(cpg), tma);
@@ -376,9 +389,15 @@ int plan_small(const gc_shape *p, bool tma, bool w_aligned, bool y_aligned, int 
                 const long long xf = round_up(cb * rows * pitch, 32);
                 const long long wf = round_up(cb * cpg * 9, 32);
                 const long long wtf = cpg == 1 ? 0 : wf;  // transposed copy
+                // warp-specialized: x, raw and transposed weights per stage,
+                // then full / ready / empty barriers and the abort word;
+                // CTA-synchronous: x and raw weights per stage, one
+                // transposed copy, one barrier per stage.
+                const long long stage_floats = ws ? xf + wf + wtf : xf + wf;
                 for (int stages = 2; stages <= gcb::kMaxStages; ++stages) {
                     const size_t smem =
-                        static_cast<size_t>((stages * (xf + wf) + wtf) * 4 + 8 * gcb::kMaxStages);
+                        ws ? static_cast<size_t>(stages * stage_floats * 4 + 3 * 8 * gcb::kMaxStages + 16)
+                           : static_cast<size_t>((stages * stage_floats + wtf) * 4 + 8 * gcb::kMaxStages);
                     if (smem > static_cast<size_t>(facts.smem_optin)) break;
                     int ctas = 0;
                     int st = kernel_occupancy(dev, tma ? var.fn_tma : var.fn_ldg, threads, smem,
@@ -387,7 +406,7 @@ int plan_small(const gc_shape *p, bool tma, bool w_aligned, bool y_aligned, int 
                     if (ctas < 1) continue;
                     const long long slots = static_cast<long long>(facts.sms) * ctas;
                     const double balance = grid_balance(items, slots, facts.sms);
-                    const double cell_eff = static_cast<double>(cells) / threads;
+                    const double cell_eff = static_cast<double>(cells) / round_up(cells, 32);
                     // A CTA overlaps the staging of its next items with compute
                     // only when it owns several items.
                     const double per_cta = static_cast<double>(items) / std::min(items, slots);
@@ -424,14 +443,14 @@ int plan_small(const gc_shape *p, bool tma, bool w_aligned, bool y_aligned, int 
                     P.rows = static_cast<int>(rows);
                     P.x_floats = static_cast<int>(xf);
                     P.wraw_floats = static_cast<int>(wf);
-                    P.stage_floats = static_cast<int>(xf + wf);
+                    P.stage_floats = static_cast<int>(stage_floats);
                     P.wt_floats = static_cast<int>(wtf);
                     P.qcols = static_cast<int>(qcols);
                     P.rblocks = static_cast<int>(rblocks);
                     P.cells = static_cast<int>(cells);
                     P.stages = stages;
                     P.vec_store = (W % 4 == 0 && y_aligned) ? 1 : 0;
-                    P.bulk_w = (tma && w_aligned && (cb * cpg) % 4 == 0) ? 1 : 0;
+                    P.bulk_w = bulk_w;
                     P.x_bytes = static_cast<unsigned>(pitch * rows * cb * 4);
                     P.w_bytes = static_cast<unsigned>(cb * cpg * 9 * 4);
                     out.wide = false;

@@ -83,6 +83,28 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
     }
 }
 
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// Bounded wait of one role of a warp-specialized kernel: gives up when the
+// phase does not complete within the limit (sets the abort word and a status
+// bit) or when another role has already given up (abort word set).
+__device__ __forceinline__ bool role_wait(uint64_t *bar, uint32_t parity, volatile int *abort, unsigned status) {
+    const uint32_t a = smem_addr(bar);
+    if (mbar_try_wait(a, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (true) {
+        if (mbar_try_wait(a, parity)) return true;
+        if (*abort) return false;
+        if (global_ns() - t0 > kWaitLimitNs) {
+            *abort = 1;
+            raise_status(status);
+            return false;
+        }
+    }
+}
+
 // ---- TMA ----------------------------------------------------------------------
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
@@ -135,14 +157,13 @@ __device__ __forceinline__ void cp_async_wait_dynamic(int pending) {
 }
 
 // ---- shared-memory loads ------------------------------------------------------------
-// Predicated 4-byte shared load: returns the value at p when pred, else 0.0f,
-// without a branch (no warp divergence around rare edge loads).
-__device__ __forceinline__ float lds_if(const float *p, bool pred) {
-    float v;
+// Predicated 4-byte shared load: the value at p when pred, else v, as one
+// predicated instruction (no branch, so no warp divergence around rare edge
+// loads).
+__device__ __forceinline__ float lds_over(const float *p, bool pred, float v) {
     asm volatile(
-        "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\tmov.b32 %0, 0f00000000;\n\t"
-        "@q ld.shared.f32 %0, [%1];\n\t}"
-        : "=f"(v)
+        "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %2, 0;\n\t@q ld.shared.f32 %0, [%1];\n\t}"
+        : "+f"(v)
         : "r"(smem_addr(p)), "r"(pred ? 1 : 0));
     return v;
 }

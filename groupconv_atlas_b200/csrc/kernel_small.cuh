@@ -38,7 +38,7 @@ struct SmallParams {
 // slot, slot + slots, ...
 template <int COB>
 __global__ void __launch_bounds__(512, 1) small_conv_kernel(const __grid_constant__ SmallParams P) {
-    extern __shared__ __align__(16) float smem[];
+    extern __shared__ __align__(128) float smem[];
     float *xs = smem;
     float *ws = smem + P.x_floats;
     const int cpg = P.cpg;

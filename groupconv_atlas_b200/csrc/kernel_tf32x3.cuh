@@ -170,25 +170,6 @@ constexpr int kMmaWarp = 8;
 constexpr int kTmaWarp = 9;
 constexpr int kTf32Threads = 320;
 
-__device__ __forceinline__ bool role_wait(uint64_t *bar, uint32_t parity, volatile int *abort, unsigned status) {
-    const uint32_t a = smem_addr(bar);
-    if (mbar_try_wait(a, parity)) return true;
-    const uint64_t t0 = global_ns();
-    while (true) {
-        if (mbar_try_wait(a, parity)) return true;
-        if (*abort) return false;
-        if (global_ns() - t0 > kWaitLimitNs) {
-            *abort = 1;
-            raise_status(status);
-            return false;
-        }
-    }
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-
 // 2-D tiled load (weights viewed as [C rows][cpg*9 columns]).
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int c0, int c1, uint64_t *bar) {
     asm volatile(
