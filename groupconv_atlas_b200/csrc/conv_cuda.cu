@@ -182,6 +182,7 @@ int encode_rows_map(CUtensorMap &map, const float *base, long long rows, long lo
 struct Variant {
     const char *name;
     int cob, vr;
+    int cw;  // columns per thread (direct kernels)
     const void *fn_tma;
     const void *fn_ldg;
     bool ws;  // TMA staging runs the warp-specialized kernel (else CTA-synchronous)
@@ -189,37 +190,42 @@ struct Variant {
 
 // TMA staging: depthwise layers run the CTA-synchronous kernel (measured
 // faster on HBM-bound shapes), grouped layers the warp-specialized one.
-template <int CPG, int COB, int VR>
+template <int CPG, int COB, int VR, int CW>
 Variant make_variant(const char *name) {
     const void *tma_fn;
     if constexpr (CPG == 1)
-        tma_fn = reinterpret_cast<const void *>(&gcb::direct_conv_kernel<CPG, COB, VR, true>);
+        tma_fn = reinterpret_cast<const void *>(&gcb::direct_conv_kernel<CPG, COB, VR, CW, true>);
     else
-        tma_fn = reinterpret_cast<const void *>(&gcb::direct_ws_kernel<CPG, COB, VR>);
-    return Variant{name, COB, VR, tma_fn,
-                   reinterpret_cast<const void *>(&gcb::direct_conv_kernel<CPG, COB, VR, false>), CPG != 1};
+        tma_fn = reinterpret_cast<const void *>(&gcb::direct_ws_kernel<CPG, COB, VR, CW>);
+    return Variant{name, COB, VR, CW, tma_fn,
+                   reinterpret_cast<const void *>(&gcb::direct_conv_kernel<CPG, COB, VR, CW, false>), CPG != 1};
 }
 
 template <int COB, int VR>
 Variant make_wide(const char *name) {
-    return Variant{name, COB, VR,
+    return Variant{name, COB, VR, 4,
                    reinterpret_cast<const void *>(&gcb::wide_conv_kernel<COB, VR, true, kStages>),
                    reinterpret_cast<const void *>(&gcb::wide_conv_kernel<COB, VR, false, kStages>), false};
 }
 
 // Full-group kernel variants that can serve a group width (first = preferred).
 std::vector<const Variant *> small_variants(long long cpg) {
-    static const Variant d1 = make_variant<1, 1, 4>("d1");
-    static const Variant d1r8 = make_variant<1, 1, 8>("d1r8");
-    static const Variant d2 = make_variant<2, 2, 4>("d2");
-    static const Variant d4 = make_variant<4, 4, 2>("d4");
-    static const Variant d8 = make_variant<8, 8, 2>("d8");
-    static const Variant d8h = make_variant<8, 4, 2>("d8h");
-    static const Variant gen = make_variant<0, 1, 4>("g1");
+    // name: d<cpg> + cell shape (out-channels COB x rows VR x columns CW)
+    static const Variant d1 = make_variant<1, 1, 4, 4>("d1");
+    static const Variant d1r8 = make_variant<1, 1, 8, 4>("d1r8");
+    static const Variant d2 = make_variant<2, 2, 4, 4>("d2");
+    static const Variant d4 = make_variant<4, 4, 2, 4>("d4");
+    static const Variant d4q = make_variant<4, 2, 4, 4>("d4q");
+    static const Variant d4o1 = make_variant<4, 4, 1, 8>("d4o1");
+    static const Variant d8h = make_variant<8, 4, 2, 4>("d8h");
+    static const Variant d8v4 = make_variant<8, 4, 4, 4>("d8v4");
+    static const Variant d8q = make_variant<8, 2, 4, 4>("d8q");
+    static const Variant d8o41 = make_variant<8, 4, 1, 8>("d8o41");
+    static const Variant gen = make_variant<0, 1, 4, 4>("g1");
     if (cpg == 1) return {&d1r8, &d1};
     if (cpg == 2) return {&d2};
-    if (cpg == 4) return {&d4};
-    if (cpg == 8) return {&d8, &d8h};
+    if (cpg == 4) return {&d4, &d4q, &d4o1};
+    if (cpg == 8) return {&d8h, &d8v4, &d8q, &d8o41};
     return {&gen};
 }
 
@@ -287,16 +293,16 @@ const std::vector<long long> band_candidates(long long H) {
 }
 
 // Estimated fraction of a direct-kernel thread's instructions that are FFMA:
-// per input channel a cell loads VR+2 row segments (one 16-byte load, two
+// per input channel a cell loads VR+2 row segments (CW/4 16-byte loads, two
 // shuffles, two predicated edge loads, two selects each) and its weights, and
 // per item it pays a fixed cost (item decode, barriers, output addresses) plus
 // its stores.
 double issue_efficiency(const Variant &var, long long cpg) {
-    const double vr = var.vr, cob = var.cob;
-    const double ffma = cob * vr * 36.0 * cpg;
-    const double rows = (vr + 2) * 7.0 * cpg;
+    const double vr = var.vr, cob = var.cob, cw = var.cw;
+    const double ffma = cob * vr * 9.0 * cw * cpg;
+    const double rows = (vr + 2) * (6.0 + cw / 4.0) * cpg;
     const double weights = cpg == 1 ? 9.0 : 9.0 * std::ceil(cob / 4.0) * cpg;
-    const double fixed = 40.0 + vr * cob * 3.0;
+    const double fixed = 40.0 + vr * cob * 0.75 * cw;
     return ffma / (ffma + rows + weights + fixed);
 }
 
@@ -305,9 +311,9 @@ double issue_efficiency(const Variant &var, long long cpg) {
 // shared-memory wavefronts, found by replaying the lane -> address map of
 // the first warps (8 lanes of 16 bytes fill the 32 banks once; distinct
 // addresses in the same 16-byte bank group serialize).
-int choose_pitch(int W, int qcols, int rblocks, int vr, int rows, int cells, int cob, int cpg,
+int choose_pitch(int W, int qcols, int cw, int rblocks, int vr, int rows, int cells, int cob, int cpg,
                  bool tma) {
-    const int base = static_cast<int>(round_up(4LL * qcols + 8, 4));
+    const int base = static_cast<int>(round_up(static_cast<long long>(cw) * qcols + 8, 4));
     int best = base, best_cost = 1 << 30;
     for (int p = base; p <= base + 60; p += 4) {
         if (tma && p > 256) break;
@@ -321,7 +327,7 @@ int choose_pitch(int W, int qcols, int rblocks, int vr, int rows, int cells, int
                 const int q = cell % qcols, rbc = cell / qcols;
                 const int rb = rbc % rblocks, cbk = rbc / rblocks;
                 const int g = cbk * cob / cpg;
-                addr[lane] = ((static_cast<long long>(g) * cpg * rows + rb * vr) * p + q * 4 + 4) * 4;
+                addr[lane] = ((static_cast<long long>(g) * cpg * rows + rb * vr) * p + q * cw + 4) * 4;
             }
             int worst = 0;
             for (int bank = 0; bank < 8; ++bank) {
@@ -353,13 +359,13 @@ int plan_small(const gc_shape *p, bool tma, bool w_aligned, bool y_aligned, int 
                const DeviceFacts &facts, EnginePlan &out, bool &found) {
     const long long N = p->n, C = p->cin, H = p->h, W = p->w, cpg = p->cin / p->groups;
     const long long groups = p->groups;
-    const long long qcols = ceil_div(W, 4);
     const bool compute_bound = cpg >= 4;
     double best = -1.0;
     found = false;
     for (const Variant *vp : small_variants(cpg)) {
         const Variant &var = *vp;
         const int vr = var.vr;
+        const long long qcols = ceil_div(W, var.cw);
         for (long long gpi = 1; gpi <= groups; ++gpi) {
             if (groups % gpi != 0) continue;
             const long long cb = gpi * cpg;
@@ -382,7 +388,7 @@ int plan_small(const gc_shape *p, bool tma, bool w_aligned, bool y_aligned, int 
                 const int threads = static_cast<int>(round_up(cells, 32)) +
                                     (ws ? 32 * gcb::direct_ws_producer_warps(static_cast<int>(cpg), bulk_w) : 0);
                 if (threads > (ws ? gcb::kWsMaxThreads : 256)) continue;
-                const int pitch = choose_pitch(static_cast<int>(W), static_cast<int>(qcols),
+                const int pitch = choose_pitch(static_cast<int>(W), static_cast<int>(qcols), var.cw,
                                                static_cast<int>(rblocks), vr, static_cast<int>(rows),
                                                static_cast<int>(cells), var.cob, static_cast<int>(cpg), tma);
                 if (tma && pitch > 256) continue;
@@ -412,9 +418,11 @@ int plan_small(const gc_shape *p, bool tma, bool w_aligned, bool y_aligned, int 
                     const double per_cta = static_cast<double>(items) / std::min(items, slots);
                     const double halo = static_cast<double>(rows) / bh;
                     const double warps = ctas * threads / 32.0;
+                    // rows computed past the image in the last band
+                    const double band_eff = static_cast<double>(H) / (bands * rblocks * vr);
                     double score = balance * issue_efficiency(var, cpg);
                     if (compute_bound) {
-                        score *= cell_eff / (1.0 + 0.05 * (halo - 1.0));
+                        score *= cell_eff * band_eff / (1.0 + 0.05 * (halo - 1.0));
                         score *= std::min(1.0, 0.55 + 0.45 * warps / 16.0);
                     } else {
                         score *= cell_eff;

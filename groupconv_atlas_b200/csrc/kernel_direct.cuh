@@ -27,9 +27,10 @@
 //                      TMA staging for depthwise layers.
 //
 // Compute: every thread owns one fixed cell for the whole kernel - COB output
-// channels x VR rows x 4 columns - decoded once.  Cells are numbered with the
-// column quad fastest, so the lanes of a warp hold neighbouring quads of a
-// row: each input row segment is one 16-byte shared load, and the two halo
+// channels x VR rows x CW (4 or 8) columns - decoded once.  Cells are
+// numbered with the column block fastest, so the lanes of a warp hold
+// neighbouring blocks of a row: each input row segment is CW/4 16-byte shared
+// loads, and the two halo
 // columns come from the neighbouring lanes by warp shuffle, replaced by a
 // predicated shared load for the first/last lane of the warp and at the
 // image edges (where the tile holds the zero padding).  Each loaded value is
@@ -53,13 +54,14 @@ struct DirectParams {
     int bh;              // output rows per item
     int bands, cblocks;  // ceil(h / bh), c / cb
     int items;           // n * cblocks * bands
-    int pitch;           // shared row pitch in floats, multiple of 4, >= 4*qcols + 8
+    int pitch;           // shared row pitch in floats, multiple of 4, >= CW*qcols + 8
+                         // (the last block's right neighbour quad lies inside the row)
     int rows;            // tile rows: round_up(bh, VR) + 2
     int x_floats;        // input tile floats per stage (multiple of 32)
     int wraw_floats;     // raw weight floats per stage (multiple of 32)
     int wt_floats;       // transposed weight floats (0 when cpg == 1)
     int stage_floats;    // TMA kernel: x + wraw + wt per stage; cp.async kernel: x + wraw
-    int qcols;           // ceil(wd / 4)
+    int qcols;           // column blocks per row: ceil(wd / CW)
     int rblocks;         // ceil(bh / VR)
     int cells;           // (cb / COB) * rblocks * qcols  (<= compute threads)
     int stages;          // shared-memory ring depth, 2..kMaxStages
@@ -160,41 +162,47 @@ __device__ __forceinline__ void store_quad(float *yp, const float (&a)[4], bool 
     }
 }
 
-// Six consecutive values x[col0-1 .. col0+4] of one tile row for a thread
-// whose 16-byte quad starts at p: the quad itself is one shared load and the
-// two halo values come from the neighbouring lanes by shuffle.  Where the
-// neighbour quad is not in the neighbouring lane (first/last lane of the
-// warp, or the quad sits at an image edge and the neighbouring lane holds
-// another row) a predicated shared load reads the tile instead: the
-// neighbour column, or the zero padding beside the image.  The shuffles and
-// the loads are independent (selected afterwards), so their latencies
-// overlap; branch-free, so the warp never diverges.
-__device__ __forceinline__ void load_row6(const float *p, bool left_smem, bool right_smem, float (&x)[6]) {
-    const float4 m = *reinterpret_cast<const float4 *>(p);
-    const float sl = __shfl_up_sync(0xffffffffu, m.w, 1);
-    const float sr = __shfl_down_sync(0xffffffffu, m.x, 1);
+// The CW + 2 consecutive values x[col0-1 .. col0+CW] of one tile row for a
+// thread whose CW columns start at p (16-byte aligned): the columns
+// themselves are CW/4 16-byte shared loads and the two halo values come from
+// the neighbouring lanes by shuffle.  Where the neighbour block is not in the
+// neighbouring lane (first/last lane of the warp, or the block sits at an
+// image edge and the neighbouring lane holds another row) a predicated shared
+// load reads the tile instead: the neighbour column, or the zero padding
+// beside the image.  The shuffles and the loads are independent (selected
+// afterwards), so their latencies overlap; branch-free, so the warp never
+// diverges.
+template <int CW>
+__device__ __forceinline__ void load_row(const float *p, bool left_smem, bool right_smem, float (&x)[CW + 2]) {
+#pragma unroll
+    for (int b = 0; b < CW / 4; ++b) {
+        const float4 m = *reinterpret_cast<const float4 *>(p + 4 * b);
+        x[1 + 4 * b] = m.x;
+        x[2 + 4 * b] = m.y;
+        x[3 + 4 * b] = m.z;
+        x[4 + 4 * b] = m.w;
+    }
+    const float sl = __shfl_up_sync(0xffffffffu, x[CW], 1);
+    const float sr = __shfl_down_sync(0xffffffffu, x[1], 1);
     const float ml = lds_over(p - 1, left_smem, 0.0f);
-    const float mr = lds_over(p + 4, right_smem, 0.0f);
+    const float mr = lds_over(p + CW, right_smem, 0.0f);
     x[0] = left_smem ? ml : sl;
-    x[1] = m.x;
-    x[2] = m.y;
-    x[3] = m.z;
-    x[4] = m.w;
-    x[5] = right_smem ? mr : sr;
+    x[CW + 1] = right_smem ? mr : sr;
 }
 
-// The fixed cell of one thread.  Threads past the last cell mirror the last
-// cell's loads, so that every lane takes part in the shuffles, and store
-// nothing.
+// The fixed cell of one thread: COB output channels x VR rows x CW columns.
+// Threads past the last cell mirror the last cell's loads, so that every
+// lane takes part in the shuffles, and store nothing.
 struct Cell {
     int col0, row0;
     int co_item;  // first output channel of the cell, item-local
     int g, cog;   // item-local group, channel within the group
     int xoff;     // offset of the cell's first input row segment in a stage
-    bool has_cell, left_smem, right_smem, vec_ok;
+    bool has_cell, left_smem, right_smem;
+    unsigned vec_mask;  // bit b: quad b of the cell may use a 16-byte store
 };
 
-template <int COB, int VR>
+template <int COB, int VR, int CW>
 __device__ __forceinline__ Cell make_cell(const DirectParams &P, int tid, int cpg) {
     Cell c;
     const int lane = tid & 31;
@@ -204,21 +212,55 @@ __device__ __forceinline__ Cell make_cell(const DirectParams &P, int tid, int cp
     const int rbc = cell / P.qcols;
     const int rb = rbc % P.rblocks;
     const int cob = rbc / P.rblocks;
-    c.col0 = q * 4;
+    c.col0 = q * CW;
     c.row0 = rb * VR;
     c.co_item = cob * COB;
     c.g = c.co_item / cpg;
     c.cog = c.co_item - c.g * cpg;
     c.left_smem = q == 0 || lane == 0;
     c.right_smem = q == P.qcols - 1 || lane == 31;
-    c.vec_ok = P.vec_store && c.col0 + 4 <= P.wd;
+    c.vec_mask = 0;
+#pragma unroll
+    for (int b = 0; b < CW / 4; ++b)
+        if (P.vec_store && c.col0 + 4 * b + 4 <= P.wd) c.vec_mask |= 1u << b;
     c.xoff = (c.g * cpg) * P.rows * P.pitch + c.row0 * P.pitch + c.col0 + 4;
     return c;
 }
 
+// Same values by three plain loads per quad row: the quads left and right of
+// the thread's own are loaded whole (16 bytes each, conflict-free like the
+// centre load) and only their inner columns kept.  Three load instructions
+// and no shuffles or selects: fewer issue slots, more shared-memory
+// wavefronts - the better trade where FFMA issue is the bound.
+template <int CW>
+__device__ __forceinline__ void load_row_wide(const float *p, float (&x)[CW + 2]) {
+    const float4 l = *reinterpret_cast<const float4 *>(p - 4);
+#pragma unroll
+    for (int b = 0; b < CW / 4; ++b) {
+        const float4 m = *reinterpret_cast<const float4 *>(p + 4 * b);
+        x[1 + 4 * b] = m.x;
+        x[2 + 4 * b] = m.y;
+        x[3 + 4 * b] = m.z;
+        x[4 + 4 * b] = m.w;
+    }
+    const float4 r = *reinterpret_cast<const float4 *>(p + CW);
+    x[0] = l.w;
+    x[CW + 1] = r.x;
+}
+
+// One output row segment of a cell: CW/4 quads.
+template <int CW>
+__device__ __forceinline__ void store_row(float *yp, const float (&a)[CW], const Cell &c, int width) {
+#pragma unroll
+    for (int b = 0; b < CW / 4; ++b) {
+        const float q[4] = {a[4 * b], a[4 * b + 1], a[4 * b + 2], a[4 * b + 3]};
+        store_quad(yp + 4 * b, q, (c.vec_mask >> b) & 1u, c.col0 + 4 * b, width);
+    }
+}
+
 // One item of one cell: xs is the stage's input tile, wk the weights (raw
 // [co][tap] for depthwise, transposed [group][ci][tap][co] otherwise).
-template <int CPG, int COB, int VR>
+template <int CPG, int COB, int VR, int CW>
 __device__ __forceinline__ void compute_item(const DirectParams &P, const Cell &c, const float *xs,
                                              const float *wk_base, int item) {
     const int cpg = CPG > 0 ? CPG : P.cpg;
@@ -237,41 +279,40 @@ __device__ __forceinline__ void compute_item(const DirectParams &P, const Cell &
         float wk[9];
 #pragma unroll
         for (int t = 0; t < 9; ++t) wk[t] = wk_base[c.co_item * 9 + t];
-        float acc[3][4];
+        float acc[3][CW];
 #pragma unroll
         for (int rr = 0; rr < VR + 2; ++rr) {
-            float xrow[6];
-            load_row6(xg + rr * P.pitch, c.left_smem, c.right_smem, xrow);
+            float xrow[CW + 2];
+            load_row<CW>(xg + rr * P.pitch, c.left_smem, c.right_smem, xrow);
 #pragma unroll
             for (int r = 0; r < 3; ++r) {
                 const int v = rr - r;  // output row this input row feeds with kernel row r
                 if (v < 0 || v >= VR) continue;
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
+                for (int u = 0; u < CW; ++u) {
                     float a = r == 0 ? 0.0f : acc[v % 3][u];
 #pragma unroll
                     for (int sx = 0; sx < 3; ++sx) a = fmaf(xrow[u + sx], wk[r * 3 + sx], a);
                     acc[v % 3][u] = a;
                 }
             }
-            if (rr >= 2 && rr - 2 < rows_valid)
-                store_quad(ybase + (rr - 2) * P.wd, acc[(rr - 2) % 3], c.vec_ok, c.col0, P.wd);
+            if (rr >= 2 && rr - 2 < rows_valid) store_row<CW>(ybase + (rr - 2) * P.wd, acc[(rr - 2) % 3], c, P.wd);
         }
     } else {
         const int chan_floats = P.rows * P.pitch;
-        float acc[COB][VR][4];
+        float acc[COB][VR][CW];
 #pragma unroll
         for (int j = 0; j < COB; ++j)
 #pragma unroll
             for (int v = 0; v < VR; ++v)
 #pragma unroll
-                for (int u = 0; u < 4; ++u) acc[j][v][u] = 0.0f;
+                for (int u = 0; u < CW; ++u) acc[j][v][u] = 0.0f;
 #pragma unroll(CPG == 2 ? 2 : 1)
         for (int ci = 0; ci < cpg; ++ci) {
             const float *xc = xg + ci * chan_floats;
-            float xr[VR + 2][6];
+            float xr[VR + 2][CW + 2];
 #pragma unroll
-            for (int rr = 0; rr < VR + 2; ++rr) load_row6(xc + rr * P.pitch, c.left_smem, c.right_smem, xr[rr]);
+            for (int rr = 0; rr < VR + 2; ++rr) load_row_wide<CW>(xc + rr * P.pitch, xr[rr]);
             const float *wp = wk_base + ((c.g * cpg + ci) * 9) * cpg + c.cog;
 #pragma unroll
             for (int tap = 0; tap < 9; ++tap) {
@@ -302,7 +343,7 @@ __device__ __forceinline__ void compute_item(const DirectParams &P, const Cell &
 #pragma unroll
                     for (int v = 0; v < VR; ++v)
 #pragma unroll
-                        for (int u = 0; u < 4; ++u)
+                        for (int u = 0; u < CW; ++u)
                             acc[j][v][u] = fmaf(xr[v + r][u + sx], wv[j], acc[j][v][u]);
             }
         }
@@ -310,8 +351,7 @@ __device__ __forceinline__ void compute_item(const DirectParams &P, const Cell &
         for (int j = 0; j < COB; ++j)
 #pragma unroll
             for (int v = 0; v < VR; ++v)
-                if (v < rows_valid)
-                    store_quad(ybase + j * plane_floats + v * P.wd, acc[j][v], c.vec_ok, c.col0, P.wd);
+                if (v < rows_valid) store_row<CW>(ybase + j * plane_floats + v * P.wd, acc[j][v], c, P.wd);
     }
 }
 
@@ -331,7 +371,7 @@ __host__ __device__ inline int direct_ws_producer_warps(int cpg, int bulk_w) {
     return (cpg != 1 || !bulk_w) ? 2 : 1;
 }
 
-template <int CPG, int COB, int VR>
+template <int CPG, int COB, int VR, int CW>
 __global__ void __launch_bounds__(kWsMaxThreads) direct_ws_kernel(const __grid_constant__ DirectParams P,
                                                          const __grid_constant__ CUtensorMap xmap) {
     extern __shared__ __align__(128) float smem[];
@@ -417,7 +457,7 @@ __global__ void __launch_bounds__(kWsMaxThreads) direct_ws_kernel(const __grid_c
     }
 
     // ---- compute warps ----
-    const Cell c = make_cell<COB, VR>(P, tid, cpg);
+    const Cell c = make_cell<COB, VR, CW>(P, tid, cpg);
     uint64_t *const publish = weight_warp ? ready : full;
     for (int k = 0; k < count; ++k) {
         const int s = k % STAGES;
@@ -426,7 +466,7 @@ __global__ void __launch_bounds__(kWsMaxThreads) direct_ws_kernel(const __grid_c
         if (!ok) return;
         const float *xs = xs_of(s);
         const float *wk = CPG == 1 ? xs + P.x_floats : xs + P.x_floats + P.wraw_floats;
-        compute_item<CPG, COB, VR>(P, c, xs, wk, first + k * step);
+        compute_item<CPG, COB, VR, CW>(P, c, xs, wk, first + k * step);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
     }
@@ -438,7 +478,7 @@ __global__ void __launch_bounds__(kWsMaxThreads) direct_ws_kernel(const __grid_c
 // the others wait in the hardware barrier (no issue slots spent spinning).
 // Used for cp.async staging, and for depthwise layers with TMA staging,
 // where a whole CTA moving in lockstep keeps the most bytes in flight.
-template <int CPG, int COB, int VR, bool TMA>
+template <int CPG, int COB, int VR, int CW, bool TMA>
 __global__ void __launch_bounds__(256) direct_conv_kernel(const __grid_constant__ DirectParams P,
                                                           const __grid_constant__ CUtensorMap xmap) {
     extern __shared__ __align__(128) float smem[];
@@ -449,7 +489,7 @@ __global__ void __launch_bounds__(256) direct_conv_kernel(const __grid_constant_
     const int first = blockIdx.x, step = gridDim.x;
     const int count = first < P.items ? (P.items - 1 - first) / step + 1 : 0;
     const int tid = threadIdx.x;
-    const Cell c = make_cell<COB, VR>(P, tid, cpg);
+    const Cell c = make_cell<COB, VR, CW>(P, tid, cpg);
 
     if (TMA && tid == 0) {
         for (int s = 0; s < STAGES; ++s) mbar_init(&bars[s], 1);
@@ -508,7 +548,7 @@ __global__ void __launch_bounds__(256) direct_conv_kernel(const __grid_constant_
             transpose_weights(wr, wt, P.cb, cpg, tid, blockDim.x);
             __syncthreads();
         }
-        compute_item<CPG, COB, VR>(P, c, xs, CPG == 1 ? wr : wt, first + k * step);
+        compute_item<CPG, COB, VR, CW>(P, c, xs, CPG == 1 ? wr : wt, first + k * step);
         __syncthreads();
         if (TMA && tid == 0 && k + STAGES < count)
             stage_with_tma(P, &xmap, xs, wr, &bars[s], first + (k + STAGES) * step);
