@@ -190,15 +190,18 @@ struct Variant {
 
 // TMA staging: depthwise layers run the CTA-synchronous kernel (measured
 // faster on HBM-bound shapes), grouped layers the warp-specialized one.
-template <int CPG, int COB, int VR, int CW>
+// LDG = false: TMA staging only (no cp.async instance; the planner skips the
+// variant for shapes TMA cannot stage).
+template <int CPG, int COB, int VR, int CW, bool LDG = true>
 Variant make_variant(const char *name) {
     const void *tma_fn;
     if constexpr (CPG == 1)
         tma_fn = reinterpret_cast<const void *>(&gcb::direct_conv_kernel<CPG, COB, VR, CW, true>);
     else
         tma_fn = reinterpret_cast<const void *>(&gcb::direct_ws_kernel<CPG, COB, VR, CW>);
-    return Variant{name, COB, VR, CW, tma_fn,
-                   reinterpret_cast<const void *>(&gcb::direct_conv_kernel<CPG, COB, VR, CW, false>), CPG != 1};
+    const void *ldg_fn = nullptr;
+    if constexpr (LDG) ldg_fn = reinterpret_cast<const void *>(&gcb::direct_conv_kernel<CPG, COB, VR, CW, false>);
+    return Variant{name, COB, VR, CW, tma_fn, ldg_fn, CPG != 1};
 }
 
 template <int COB, int VR>
@@ -216,11 +219,11 @@ std::vector<const Variant *> small_variants(long long cpg) {
     static const Variant d2 = make_variant<2, 2, 4, 4>("d2");
     static const Variant d4 = make_variant<4, 4, 2, 4>("d4");
     static const Variant d4q = make_variant<4, 2, 4, 4>("d4q");
-    static const Variant d4o1 = make_variant<4, 4, 1, 8>("d4o1");
+    static const Variant d4o1 = make_variant<4, 4, 1, 8, false>("d4o1");
     static const Variant d8h = make_variant<8, 4, 2, 4>("d8h");
     static const Variant d8v4 = make_variant<8, 4, 4, 4>("d8v4");
     static const Variant d8q = make_variant<8, 2, 4, 4>("d8q");
-    static const Variant d8o41 = make_variant<8, 4, 1, 8>("d8o41");
+    static const Variant d8o41 = make_variant<8, 4, 1, 8, false>("d8o41");
     static const Variant gen = make_variant<0, 1, 4, 4>("g1");
     if (cpg == 1) return {&d1r8, &d1};
     if (cpg == 2) return {&d2};
@@ -364,6 +367,7 @@ int plan_small(const gc_shape *p, bool tma, bool w_aligned, bool y_aligned, int 
     found = false;
     for (const Variant *vp : small_variants(cpg)) {
         const Variant &var = *vp;
+        if (!tma && var.fn_ldg == nullptr) continue;
         const int vr = var.vr;
         const long long qcols = ceil_div(W, var.cw);
         for (long long gpi = 1; gpi <= groups; ++gpi) {
@@ -644,17 +648,14 @@ int launch_direct(const gc_shape *p, const float *x, const float *w, float *y, b
 // ---- tcgen05 3xTF32 implicit GEMM ------------------------------------------------------
 bool tf32_cpg_supported(long long cpg) { return cpg == 8 || cpg == 16 || cpg == 32 || cpg == 64; }
 
-// Whether the tensor-core path can serve this shape and input pointer: a
-// supported group width, a TMA-stageable row (width % 4 == 0, <= 256
-// floats, 16-byte aligned input) and 32-bit pixel indices.
-// Images small enough to stage 8 whole planes per step with one bulk copy.
-constexpr long long kTf32BulkMaxPixels = 1024;
-
+// Whether the tensor-core path can serve this shape: a supported group width,
+// 16-byte aligned weights (TMA-staged), A rows of one M-tile plus its halo
+// within the converters' reach, and 32-bit pixel indices.  Inputs are read
+// with plain loads: any width, any alignment.
 bool tf32_eligible(const gc_shape *p, const void *x, const void *w) {
+    (void)x;
     const long long cpg = p->cin / p->groups;
-    const bool rows_by_tma = p->w % 4 == 0 && p->w <= 256;
-    const bool planes_by_bulk = p->h * p->w <= kTf32BulkMaxPixels;
-    return tf32_cpg_supported(cpg) && (rows_by_tma || planes_by_bulk) && aligned16(x) && aligned16(w) &&
+    return tf32_cpg_supported(cpg) && aligned16(w) && 128 + 2 * (p->w + 2) + 2 <= gcb::kTf32MaxRows &&
            p->h * (p->w + 2) < (1LL << 30) && p->n < (1LL << 30) && p->cin < (1LL << 30);
 }
 
@@ -684,22 +685,17 @@ int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
     const long long N = p->n, C = p->cin, H = p->h, W = p->w, cpg = C / p->groups;
     const long long wp = W + 2;
     const long long tiles = ceil_div(H * wp, 128);
-    const bool bulk = !(W % 4 == 0 && W <= 256);  // rows not TMA-stageable: whole planes
     int best_t = 0;
     double best_cost = 0.0;
     gcb::Tf32Params best{};
     size_t best_smem = 0;
     for (long long T = 1; T <= tiles && 2 * T * cpg <= 512; ++T) {
         const long long rows_a = round_up(T * 128 + 2 * wp + 2, 8);
-        const long long raw_rows = bulk ? H : (rows_a - 1) / wp + 2;
-        if (raw_rows > 256) break;
-        const long long raw_bytes = 8 * raw_rows * W * 4;
+        if (rows_a > gcb::kTf32MaxRows) break;
         const long long wraw_bytes = cpg * 72 * 4;
         const long long a_bytes = rows_a * 32;
         const long long b_bytes = 9 * cpg * 32;
-        const long long raw_stride = round_up(raw_bytes, 128);
-        const size_t smem =
-            static_cast<size_t>(2 * raw_stride + 2 * wraw_bytes + 4 * a_bytes + 4 * b_bytes + 128);
+        const size_t smem = static_cast<size_t>(2 * wraw_bytes + 4 * a_bytes + 4 * b_bytes + 128);
         if (smem > static_cast<size_t>(facts.smem_optin)) break;
         long long cols = 32;
         while (cols < 2 * T * cpg) cols *= 2;
@@ -719,19 +715,18 @@ int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
         P.items = static_cast<int>(items);
         P.chunks = static_cast<int>(cpg / 8);
         P.rows_a = static_cast<int>(rows_a);
-        P.raw_rows = static_cast<int>(raw_rows);
-        P.raw_pitch = static_cast<int>(W);
-        P.raw_bytes = static_cast<unsigned>(raw_bytes);
-        P.raw_stride = static_cast<unsigned>(raw_stride);
         P.a_bytes = static_cast<unsigned>(a_bytes);
         P.b_bytes = static_cast<unsigned>(b_bytes);
         P.wraw_bytes = static_cast<unsigned>(wraw_bytes);
         P.tmem_cols = static_cast<unsigned>(cols);
-        P.bulk = bulk ? 1 : 0;
-        // Time model: waves of items over the SMs (one CTA each) times the
-        // work of one item, which grows with the rows it converts (T M-tiles
-        // plus the 2*Wp+2 halo rows shared by a strip).
-        const double cost = static_cast<double>(ceil_div(items, facts.sms)) * static_cast<double>(rows_a);
+        // Time model per step (8 input channels) of an item, in shared-memory
+        // cycles: the tensor core reads A (4 KB) and B (cpg * 32 bytes) three
+        // times per tap and M-tile; the converters' work (A rows incl. the
+        // halo, and the chunk's weights) overlaps it; a fixed hand-off cost
+        // per step.  Items run in waves over the SMs.
+        const double mma = static_cast<double>(T) * 27.0 * (4096.0 + 32.0 * cpg) / 128.0;
+        const double conv = (static_cast<double>(rows_a) * 8.0 + 72.0 * cpg) * 12.0 / 256.0;
+        const double cost = static_cast<double>(ceil_div(items, facts.sms)) * (std::max(mma, conv) + 400.0);
         if (best_t > 0 && cost >= best_cost) continue;
         best_cost = cost;
         best = P;
@@ -758,25 +753,19 @@ int launch_tf32(const gc_shape *p, const float *x, const float *w, float *y, int
     plan.P.x = x;
     plan.P.w = w;
     plan.P.y = y;
-    CUtensorMap map;
-    std::memset(&map, 0, sizeof(map));
-    if (!plan.P.bulk) {
-        st = encode_nchw_map(map, x, p->n, p->cin, p->h, p->w, plan.P.raw_pitch, plan.P.raw_rows, 8);
-        if (st != GC_OK) return st;
-    }
     CUtensorMap wmap;
     std::memset(&wmap, 0, sizeof(wmap));
     st = encode_rows_map(wmap, w, p->cout, (p->cin / p->groups) * 9, 72, plan.P.cpg);
     if (st != GC_OK) return st;
-    void *args[] = {&plan.P, &map, &wmap};
+    void *args[] = {&plan.P, &wmap};
     cudaError_t e = launch_pdl(plan.fn, dim3(plan.grid), dim3(gcb::kTf32Threads), args, plan.smem, stream);
     if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
     char buf[256];
     std::snprintf(buf, sizeof(buf),
                   "kernel=tf32x3 engine=tcgen05 n_cta=%d block=320 smem=%zu T=%d strips=%d items=%d chunks=%d "
-                  "rows_a=%d raw_rows=%d tmem_cols=%u staging=%s",
+                  "rows_a=%d tmem_cols=%u",
                   plan.grid, plan.smem, plan.P.T, plan.P.strips, plan.P.items, plan.P.chunks, plan.P.rows_a,
-                  plan.P.raw_rows, plan.P.tmem_cols, plan.P.bulk ? "bulk" : "tma");
+                  plan.P.tmem_cols);
     g_plan = buf;
     return GC_OK;
 }

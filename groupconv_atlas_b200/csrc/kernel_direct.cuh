@@ -151,14 +151,15 @@ __device__ __forceinline__ void transpose_weights_global(const float *w, float *
 
 // Four outputs of one row: one streaming 16-byte store when the row is
 // 16-byte aligned and fully inside the image, else per-column stores.
-__device__ __forceinline__ void store_quad(float *yp, const float (&a)[4], bool vec_ok, int col0,
-                                           int width) {
+__device__ __forceinline__ void store_quad(float *yp, float a0, float a1, float a2, float a3, bool vec_ok,
+                                           int col0, int width) {
     if (vec_ok) {
-        st_stream_v4(yp, a[0], a[1], a[2], a[3]);
+        st_stream_v4(yp, a0, a1, a2, a3);
     } else {
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-            if (col0 + u < width) st_stream(yp + u, a[u]);
+        if (col0 < width) st_stream(yp, a0);
+        if (col0 + 1 < width) st_stream(yp + 1, a1);
+        if (col0 + 2 < width) st_stream(yp + 2, a2);
+        if (col0 + 3 < width) st_stream(yp + 3, a3);
     }
 }
 
@@ -252,10 +253,9 @@ __device__ __forceinline__ void load_row_wide(const float *p, float (&x)[CW + 2]
 template <int CW>
 __device__ __forceinline__ void store_row(float *yp, const float (&a)[CW], const Cell &c, int width) {
 #pragma unroll
-    for (int b = 0; b < CW / 4; ++b) {
-        const float q[4] = {a[4 * b], a[4 * b + 1], a[4 * b + 2], a[4 * b + 3]};
-        store_quad(yp + 4 * b, q, (c.vec_mask >> b) & 1u, c.col0 + 4 * b, width);
-    }
+    for (int b = 0; b < CW / 4; ++b)
+        store_quad(yp + 4 * b, a[4 * b], a[4 * b + 1], a[4 * b + 2], a[4 * b + 3], (c.vec_mask >> b) & 1u,
+                   c.col0 + 4 * b, width);
 }
 
 // One item of one cell: xs is the stage's input tile, wk the weights (raw
@@ -307,7 +307,7 @@ __device__ __forceinline__ void compute_item(const DirectParams &P, const Cell &
             for (int v = 0; v < VR; ++v)
 #pragma unroll
                 for (int u = 0; u < CW; ++u) acc[j][v][u] = 0.0f;
-#pragma unroll(CPG == 2 ? 2 : 1)
+#pragma unroll 1
         for (int ci = 0; ci < cpg; ++ci) {
             const float *xc = xg + ci * chan_floats;
             float xr[VR + 2][CW + 2];

@@ -10,22 +10,29 @@
 //         tap is therefore a pure row shift of one shared-memory tile;
 //   B_tap[ci, co] = w[g*cpg + co, ci, r, s].
 // tcgen05.mma.kind::tf32, M = 128 pixels, N = cpg output channels, K = 8 input
-// channels per instruction.  x = hi + lo with hi = tf32(x), lo = tf32(x - hi);
-// D += A_hi B_hi + A_hi B_lo + A_lo B_hi (the lo*lo term is below FP32
-// rounding of the sum).
+// channels per instruction.  x = hi + lo with hi = x rounded to TF32 (nearest,
+// ties away) and lo = x - hi (exact in FP32; the tensor core reads its top 19
+// bits); D += A_hi B_hi + A_hi B_lo + A_lo B_hi.  Per product the dropped terms
+// are below 2^-20 of |x*w|, far inside the 1e-5 * sum|x*w| acceptance bound.
 //
 // Work item = (group, image, strip of T consecutive 128-pixel M-tiles); pipeline
-// step = (item, chunk of 8 input channels).  Per step, one TMA box brings the
-// raw NCHW rows of the 8 channels (zero-filled outside the image) into a
-// double-buffered staging area; all threads split x and the chunk's weights into
-// hi/lo TF32 in the K-major no-swizzle canonical layout (core matrix = 8 rows x
-// 16 bytes; rows 16 bytes apart, the two 4-channel halves LBO apart), so a
-// shift by one pixel is +16 bytes of descriptor start address; one thread
-// issues 27*T MMAs and commits them to an mbarrier that frees the stage.  The
-// accumulator of item j lives in TMEM buffer j % 2, so the epilogue of item j
-// (tcgen05.ld -> coalesced streaming stores of whole output rows) overlaps the
-// MMAs of item j+1.  Every wait is bounded; on timeout the kernel records it in
-// the status word, drains what it issued, frees its TMEM and returns.
+// step = (item, chunk of 8 input channels).  Per step:
+//   - the converter warps read the step's input pixels straight from global
+//     memory (8 coalesced channel loads per A row, issued one step ahead into
+//     registers so their latency hides behind the current step), split them
+//     into hi/lo TF32 rows of the K-major no-swizzle canonical layout (core
+//     matrix = 8 rows x 16 bytes; rows 16 bytes apart, the two 4-channel halves
+//     LBO apart, so a shift by one pixel is +16 bytes of descriptor start
+//     address), and split the chunk's weights, which one lane of the weight
+//     warp stages by TMA (2-D box of the [C][cpg*9] weight matrix);
+//   - one lane of the MMA warp issues 27*T MMAs and commits them to the
+//     mbarrier that frees the A/B stage.
+// The accumulator of item j lives in TMEM buffer j % 2, so the epilogue of item
+// j (tcgen05.ld -> coalesced streaming stores of whole output rows) overlaps
+// the MMAs of item j+1.  Every wait is bounded; on timeout the kernel records
+// it in the status word, drains what it issued, frees its TMEM and returns.
+// Inputs are assumed finite: for an infinite input the split is undefined and
+// the outputs it reaches come out NaN.
 #pragma once
 #include "device_util.cuh"
 
@@ -42,27 +49,14 @@ struct Tf32Params {
     int strips;          // ceil(tiles / T)
     int items;           // groups * n * strips
     int chunks;          // cpg / 8
-    int rows_a;          // A rows per step: T*128 + 2*wp + 2, rounded up to 8
-    int raw_rows;        // image rows staged per step
-    int raw_pitch;       // floats per staged row (the TMA box width)
-    unsigned raw_bytes;  // bytes of one staged step: 8 * raw_rows * raw_pitch * 4
-    unsigned raw_stride; // shared-memory bytes reserved per staged step (raw_bytes rounded to 128)
+    int rows_a;          // A rows per step: T*128 + 2*wp + 2, rounded up to 8 (<= kTf32MaxRows)
     unsigned a_bytes;    // bytes of one A tile (hi or lo): rows_a * 32
     unsigned b_bytes;    // bytes of one B tile set (hi or lo): 9 taps * cpg * 32
     unsigned wraw_bytes; // bytes of one staged weight chunk: cpg * 72 * 4
     unsigned tmem_cols;  // allocated TMEM columns (power of two)
-    int bulk;            // 1: stage the 8 channels' whole planes with one contiguous
-                         //    bulk copy (rows start at image row 0); 0: TMA box from
-                         //    image row hp0-1 (zero-filled outside the image)
 };
 
 // ---- tcgen05 helpers -----------------------------------------------------------------
-__device__ __forceinline__ uint32_t tf32_rna(float x) {
-    uint32_t r;
-    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-    return r;
-}
-
 // Shared-memory matrix descriptor, K-major, no swizzle (canonical layout
 // ((8,m),2):((1,SBO),LBO) in 16-byte units), sm100 version bit set.
 __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
@@ -155,20 +149,23 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
 }
 
 // ---- warp-specialized kernel -------------------------------------------------------------
-// Roles (320 threads): warps 0-7 convert staged rows and weights to hi/lo
-// TF32 tiles and run the epilogues; warp 8 (one lane) issues the MMAs;
-// warp 9 (one lane) issues the TMA loads.  Stages are handed over through
-// full/empty mbarriers:
-//   raw_full  (TMA -> converters)  raw_empty (converters -> TMA)
-//   ab_full   (converters -> MMA)  ab_empty  (MMA commit -> converters)
-//   acc_full  (MMA commit -> epilogue)  acc_empty (epilogue -> MMA)
+// Roles (320 threads): warps 0-7 load and convert the A rows and the weights
+// to hi/lo TF32 tiles and run the epilogues; warp 8 (one lane) issues the
+// MMAs; warp 9 (one lane) issues the weight TMA loads.  Stages are handed
+// over through full/empty mbarriers:
+//   w_full   (TMA -> converters)     w_empty  (converters -> TMA)
+//   ab_full  (converters -> MMA)     ab_empty (MMA commit -> converters)
+//   acc_full (MMA commit -> epilogue)  acc_empty (epilogue -> MMA)
 // Step k uses stage k % 2 for the k/2-th time, so every wait is on parity
 // (k/2) & 1 of that stage's barrier.  Every wait is bounded and also gives up
 // as soon as another role has recorded a failure in the shared abort word.
 constexpr int kConvWarps = 8;
+constexpr int kConvThreads = kConvWarps * 32;
 constexpr int kMmaWarp = 8;
 constexpr int kTmaWarp = 9;
 constexpr int kTf32Threads = 320;
+constexpr int kTf32RowsPerThread = 4;
+constexpr int kTf32MaxRows = kTf32RowsPerThread * kConvThreads;
 
 // 2-D tiled load (weights viewed as [C rows][cpg*9 columns]).
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int c0, int c1, uint64_t *bar) {
@@ -189,9 +186,51 @@ __device__ __forceinline__ void tf32_decode(const Tf32Params &P, int item, int &
     n = static_cast<int>(t - static_cast<unsigned>(g) * static_cast<unsigned>(P.n));
 }
 
-// First padded input row of a strip (the staged tile's row 0 is image row hp0-1).
-__device__ __forceinline__ int strip_hp0(const Tf32Params &P, int strip) {
-    return (strip * P.T * 128) / P.wp;
+// x = hi + lo: hi rounded to TF32 (nearest, ties away from zero) by integer
+// arithmetic on the bit pattern, lo the exact FP32 remainder.
+__device__ __forceinline__ void tf32_split(float x, uint32_t &hi, uint32_t &lo) {
+    hi = (__float_as_uint(x) + 0x1000u) & 0xFFFFE000u;
+    lo = __float_as_uint(x - __uint_as_float(hi));
+}
+
+// Converter thread's A rows of one item: plane offset of each row's input
+// pixel and a bit per row that lies inside the image (else the row is zero
+// padding or past the strip's rows).
+struct RowGeom {
+    int off[kTf32RowsPerThread];
+    unsigned valid;
+};
+
+__device__ __forceinline__ RowGeom tf32_rows(const Tf32Params &P, int strip, int ctid) {
+    RowGeom gm;
+    gm.valid = 0;
+    const int o0 = strip * P.T * 128;
+#pragma unroll
+    for (int r = 0; r < kTf32RowsPerThread; ++r) {
+        const int i = ctid + r * kConvThreads;
+        const int o = o0 + i;
+        const int hp = o / P.wp;
+        const int ih = hp - 1, iw = o - hp * P.wp - 1;
+        const bool in = i < P.rows_a && ih >= 0 && ih < P.h && iw >= 0 && iw < P.wd;
+        gm.off[r] = in ? ih * P.wd + iw : 0;
+        gm.valid |= in ? (1u << r) : 0u;
+    }
+    return gm;
+}
+
+// The 8 channels of the chunk at every A row of this thread (0 outside the image).
+__device__ __forceinline__ void tf32_load_rows(const Tf32Params &P, int item, int chunk, const RowGeom &gm,
+                                               float (&v)[kTf32RowsPerThread][8]) {
+    int g, n, strip;
+    tf32_decode(P, item, g, n, strip);
+    const long long hw = static_cast<long long>(P.h) * P.wd;
+    const float *base = P.x + (static_cast<long long>(n) * P.c + g * P.cpg + chunk * 8) * hw;
+#pragma unroll
+    for (int r = 0; r < kTf32RowsPerThread; ++r) {
+        const bool in = (gm.valid >> r) & 1u;
+#pragma unroll
+        for (int ci = 0; ci < 8; ++ci) v[r][ci] = in ? __ldg(base + ci * hw + gm.off[r]) : 0.0f;
+    }
 }
 
 // Converter warps: epilogue of one item.  Warp w reads TMEM lanes
@@ -249,18 +288,16 @@ __device__ __forceinline__ void tf32_epilogue(const Tf32Params &P, uint32_t acc,
 
 template <int NCO>
 __global__ void __launch_bounds__(kTf32Threads, 1)
-    tf32x3_conv_kernel(const __grid_constant__ Tf32Params P, const __grid_constant__ CUtensorMap xmap,
-                       const __grid_constant__ CUtensorMap wmap) {
+    tf32x3_conv_kernel(const __grid_constant__ Tf32Params P, const __grid_constant__ CUtensorMap wmap) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    // layout: xraw[2] | wraw[2] | a_hi[2] | a_lo[2] | b_hi[2] | b_lo[2] | barriers | words
-    unsigned char *const xraw0 = smem_raw;
-    unsigned char *const wraw0 = xraw0 + 2 * P.raw_stride;
+    // layout: wraw[2] | a_hi[2] | a_lo[2] | b_hi[2] | b_lo[2] | barriers | words
+    unsigned char *const wraw0 = smem_raw;
     unsigned char *const ahi0 = wraw0 + 2 * P.wraw_bytes;
     unsigned char *const alo0 = ahi0 + 2 * P.a_bytes;
     unsigned char *const bhi0 = alo0 + 2 * P.a_bytes;
     unsigned char *const blo0 = bhi0 + 2 * P.b_bytes;
     uint64_t *const bars = reinterpret_cast<uint64_t *>(blo0 + 2 * P.b_bytes);
-    uint64_t *const raw_full = bars, *const raw_empty = bars + 2, *const ab_full = bars + 4,
+    uint64_t *const w_full = bars, *const w_empty = bars + 2, *const ab_full = bars + 4,
                     *const ab_empty = bars + 6, *const acc_full = bars + 8, *const acc_empty = bars + 10;
     uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(bars + 12);
     volatile int *const abort_word = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -272,8 +309,8 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
 
     if (tid == 0) {
         for (int s = 0; s < 2; ++s) {
-            mbar_init(&raw_full[s], 1);
-            mbar_init(&raw_empty[s], kConvWarps);
+            mbar_init(&w_full[s], 1);
+            mbar_init(&w_empty[s], kConvWarps);
             mbar_init(&ab_full[s], kConvWarps);
             mbar_init(&ab_empty[s], 1);
             mbar_init(&acc_full[s], 1);
@@ -292,13 +329,12 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
 
     if (warp == kTmaWarp) {
         if (lane == 0) {
-            prefetch_tensormap(&xmap);
             prefetch_tensormap(&wmap);
             int issued = -1, released = -1;
             for (int k = 0; k < steps; ++k) {
                 const int s = k & 1;
                 if (k >= 2) {
-                    if (!role_wait(&raw_empty[s], static_cast<uint32_t>(((k - 2) >> 1) & 1), abort_word,
+                    if (!role_wait(&w_empty[s], static_cast<uint32_t>(((k - 2) >> 1) & 1), abort_word,
                                    kStatusTmaTimeout))
                         break;
                     released = k - 2;
@@ -306,22 +342,15 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
                 const int item_k = k / P.chunks, chunk = k - item_k * P.chunks;
                 int g, n, strip;
                 tf32_decode(P, first + item_k * stride, g, n, strip);
-                mbar_arrive_expect_tx(&raw_full[s], P.raw_bytes + P.wraw_bytes);
-                if (P.bulk) {
-                    const long long plane0 = static_cast<long long>(n) * P.c + g * P.cpg + chunk * 8;
-                    bulk_load(xraw0 + s * P.raw_stride, P.x + plane0 * P.h * P.wd, P.raw_bytes, &raw_full[s]);
-                } else {
-                    tma_load_4d(xraw0 + s * P.raw_stride, &xmap, 0, strip_hp0(P, strip) - 1, g * P.cpg + chunk * 8,
-                                n, &raw_full[s]);
-                }
-                tma_load_2d(wraw0 + s * P.wraw_bytes, &wmap, chunk * 72, g * P.cpg, &raw_full[s]);
+                mbar_arrive_expect_tx(&w_full[s], P.wraw_bytes);
+                tma_load_2d(wraw0 + s * P.wraw_bytes, &wmap, chunk * 72, g * P.cpg, &w_full[s]);
                 issued = k;
             }
             // Loads still in flight must land before the CTA's shared memory
             // is released: wait (bounded) for each issued stage not yet seen
-            // complete by this warp.
+            // released by the converters.
             for (int j = released + 1; j <= issued; ++j)
-                mbar_wait_bounded(&raw_full[j & 1], static_cast<uint32_t>((j >> 1) & 1), 100000000ull);
+                mbar_wait_bounded(&w_full[j & 1], static_cast<uint32_t>((j >> 1) & 1), 100000000ull);
         }
     } else if (warp == kMmaWarp) {
         if (lane == 0) {
@@ -341,19 +370,30 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
                 int g, n, strip;
                 tf32_decode(P, first + item_k * stride, g, n, strip);
                 const uint32_t acc = tmem_base + static_cast<uint32_t>((item_k & 1) * P.T * NCO);
-                const uint32_t ahi = smem_addr(ahi0 + s * P.a_bytes), alo = smem_addr(alo0 + s * P.a_bytes);
-                const uint32_t bhi = smem_addr(bhi0 + s * P.b_bytes), blo = smem_addr(blo0 + s * P.b_bytes);
+                // Descriptors of the stage's tiles; a shift of the start
+                // address is an add on the descriptor's low field (16-byte
+                // units; every offset stays inside shared memory, so no carry
+                // leaves the field).
+                const uint64_t dah0 = umma_desc(smem_addr(ahi0 + s * P.a_bytes), lbo_a, 128);
+                const uint64_t dal0 = umma_desc(smem_addr(alo0 + s * P.a_bytes), lbo_a, 128);
+                const uint64_t dbh0 = umma_desc(smem_addr(bhi0 + s * P.b_bytes), lbo_b, 128);
+                const uint64_t dbl0 = umma_desc(smem_addr(blo0 + s * P.b_bytes), lbo_b, 128);
+                const uint32_t wp = static_cast<uint32_t>(P.wp);
                 for (int t = 0; t < P.T; ++t) {
                     if (strip * P.T + t >= P.tiles) break;
                     const uint32_t d = acc + t * NCO;
+                    const uint32_t a_t = static_cast<uint32_t>(t) * 128u;
 #pragma unroll
                     for (int tap = 0; tap < 9; ++tap) {
-                        const int r = tap / 3, sx = tap - r * 3;
-                        const uint32_t aoff = (t * 128 + r * P.wp + sx) * 16u;
-                        const uint32_t boff = tap * NCO * 32u;
-                        const uint64_t dah = umma_desc(ahi + aoff, lbo_a, 128), dal = umma_desc(alo + aoff, lbo_a, 128);
-                        const uint64_t dbh = umma_desc(bhi + boff, lbo_b, 128), dbl = umma_desc(blo + boff, lbo_b, 128);
-                        umma_tf32(d, dah, dbh, kIdesc, !(chunk == 0 && tap == 0));
+                        const uint32_t r = tap / 3, sx = tap % 3;
+                        const uint64_t aoff = a_t + r * wp + sx;              // rows of 16 bytes
+                        const uint64_t boff = static_cast<uint64_t>(tap) * NCO * 2u;  // 32 bytes per co
+                        const uint64_t dah = dah0 + aoff, dal = dal0 + aoff;
+                        const uint64_t dbh = dbh0 + boff, dbl = dbl0 + boff;
+                        if (tap == 0)
+                            umma_tf32(d, dah, dbh, kIdesc, chunk != 0);
+                        else
+                            umma_tf32(d, dah, dbh, kIdesc, true);
                         umma_tf32(d, dah, dbl, kIdesc, true);
                         umma_tf32(d, dal, dbh, kIdesc, true);
                     }
@@ -369,85 +409,84 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
     } else {
         // Converter / epilogue warps.
         const int ctid = tid;  // 0 .. 255
-        const uint32_t lbo_a = P.rows_a * 16u, lbo_b = NCO * 16u;
+        const uint32_t lbo_a = P.rows_a * 16u;
+        constexpr int kBVals = 72 * NCO;  // weight values per chunk (hi and lo each)
+        constexpr int kBPerThread = (kBVals + kConvThreads - 1) / kConvThreads;
         int pending = -1;  // per-CTA item index whose epilogue is due
+        RowGeom gm{};
+        float xv[kTf32RowsPerThread][8];
+        if (steps > 0) {
+            int g, n, strip;
+            tf32_decode(P, first, g, n, strip);
+            gm = tf32_rows(P, strip, ctid);
+            tf32_load_rows(P, first, 0, gm, xv);
+        }
         for (int k = 0; k < steps; ++k) {
             const int s = k & 1;
             const int item_k = k / P.chunks, chunk = k - item_k * P.chunks;
-            // Lane 0 polls; the other lanes wait in __syncwarp.
+            // Next step's rows, in flight while this step converts.
+            RowGeom gn = gm;
+            float xn[kTf32RowsPerThread][8];
+            if (k + 1 < steps) {
+                const int item_n = (k + 1) / P.chunks, chunk_n = (k + 1) - item_n * P.chunks;
+                if (chunk_n == 0) {
+                    int g, n, strip;
+                    tf32_decode(P, first + item_n * stride, g, n, strip);
+                    gn = tf32_rows(P, strip, ctid);
+                }
+                tf32_load_rows(P, first + item_n * stride, chunk_n, gn, xn);
+            }
+            // Lane 0 polls; the other lanes wait in the shuffle.
             bool ok = true;
             if (lane == 0) {
-                ok = role_wait(&raw_full[s], static_cast<uint32_t>((k >> 1) & 1), abort_word, kStatusTmaTimeout);
+                ok = role_wait(&w_full[s], static_cast<uint32_t>((k >> 1) & 1), abort_word, kStatusTmaTimeout);
                 if (ok && k >= 2)
                     ok = role_wait(&ab_empty[s], static_cast<uint32_t>(((k - 2) >> 1) & 1), abort_word,
                                    kStatusMmaTimeout);
             }
             if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
-            int g, n, strip;
-            tf32_decode(P, first + item_k * stride, g, n, strip);
-            const int o0 = strip * P.T * 128;
-            // image row held by staged row 0
-            const int row0 = P.bulk ? 0 : strip_hp0(P, strip) - 1;
-            unsigned char *const a_hi = ahi0 + s * P.a_bytes, *const a_lo = alo0 + s * P.a_bytes;
-            unsigned char *const b_hi = bhi0 + s * P.b_bytes, *const b_lo = blo0 + s * P.b_bytes;
-            // Weights: thread -> (co, 4-channel half); the 36 staged floats
-            // [co][kg*4 .. kg*4+3][tap] are contiguous.
-            const float *wr = reinterpret_cast<const float *>(wraw0 + s * P.wraw_bytes);
-            for (int u = ctid; u < 2 * NCO; u += kConvWarps * 32) {
-                const int co = u % NCO, kg = u / NCO;
-                const float4 *src = reinterpret_cast<const float4 *>(wr + co * 72 + kg * 36);
-                float v[36];
+            // Weights: value v of the B tile set is (tap, half, co, j) with j
+            // fastest, i.e. the canonical layout is contiguous in v.
+            {
+                const float *wr = reinterpret_cast<const float *>(wraw0 + s * P.wraw_bytes);
+                uint32_t *const bh = reinterpret_cast<uint32_t *>(bhi0 + s * P.b_bytes);
+                uint32_t *const bl = reinterpret_cast<uint32_t *>(blo0 + s * P.b_bytes);
 #pragma unroll
-                for (int i = 0; i < 9; ++i) {
-                    const float4 m = src[i];
-                    v[4 * i] = m.x;
-                    v[4 * i + 1] = m.y;
-                    v[4 * i + 2] = m.z;
-                    v[4 * i + 3] = m.w;
-                }
-#pragma unroll
-                for (int tap = 0; tap < 9; ++tap) {
-                    uint32_t hi[4], lo[4];
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float x = v[j * 9 + tap];
-                        hi[j] = tf32_rna(x);
-                        lo[j] = tf32_rna(x - __uint_as_float(hi[j]));
+                for (int q = 0; q < kBPerThread; ++q) {
+                    const int v = ctid + q * kConvThreads;
+                    if (kBVals % kConvThreads == 0 || v < kBVals) {
+                        const int j = v & 3, co = (v >> 2) & (NCO - 1), kt = v / (4 * NCO);
+                        const int kg = kt & 1, tap = kt >> 1;
+                        uint32_t hi, lo;
+                        tf32_split(wr[co * 72 + (kg * 4 + j) * 9 + tap], hi, lo);
+                        bh[v] = hi;
+                        bl[v] = lo;
                     }
-                    const uint32_t off = tap * NCO * 32u + kg * lbo_b + co * 16u;
-                    *reinterpret_cast<uint4 *>(b_hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                    *reinterpret_cast<uint4 *>(b_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
                 }
             }
-            // Input rows: A[o - o0] = Xpad[o] for the 8 channels of this chunk.
-            const float *rw = reinterpret_cast<const float *>(xraw0 + s * P.raw_stride);
-            const int plane = P.raw_rows * P.raw_pitch;
-            for (int i = ctid; i < P.rows_a; i += kConvWarps * 32) {
-                const int o = o0 + i;
-                const int hp = o / P.wp;
-                const int ih = hp - 1, iw = o - hp * P.wp - 1;
-                const bool valid = ih >= 0 && ih < P.h && iw >= 0 && iw < P.wd;
-                const float *src = rw + (ih - row0) * P.raw_pitch + iw;
-                float v[8];
+            // Input rows: A[i] = Xpad[o0 + i] for the 8 channels of this chunk.
+            {
+                unsigned char *const a_hi = ahi0 + s * P.a_bytes, *const a_lo = alo0 + s * P.a_bytes;
 #pragma unroll
-                for (int ci = 0; ci < 8; ++ci) v[ci] = valid ? src[ci * plane] : 0.0f;
-                uint32_t hi[8], lo[8];
+                for (int r = 0; r < kTf32RowsPerThread; ++r) {
+                    const int i = ctid + r * kConvThreads;
+                    if (i < P.rows_a) {
+                        uint32_t hi[8], lo[8];
 #pragma unroll
-                for (int ci = 0; ci < 8; ++ci) {
-                    hi[ci] = tf32_rna(v[ci]);
-                    lo[ci] = tf32_rna(v[ci] - __uint_as_float(hi[ci]));
+                        for (int ci = 0; ci < 8; ++ci) tf32_split(xv[r][ci], hi[ci], lo[ci]);
+                        const uint32_t off = i * 16u;
+                        *reinterpret_cast<uint4 *>(a_hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                        *reinterpret_cast<uint4 *>(a_hi + off + lbo_a) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+                        *reinterpret_cast<uint4 *>(a_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                        *reinterpret_cast<uint4 *>(a_lo + off + lbo_a) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+                    }
                 }
-                const uint32_t off = i * 16u;
-                *reinterpret_cast<uint4 *>(a_hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<uint4 *>(a_hi + off + lbo_a) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
-                *reinterpret_cast<uint4 *>(a_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-                *reinterpret_cast<uint4 *>(a_lo + off + lbo_a) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
             }
             fence_async_smem();
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&ab_full[s]);
-                mbar_arrive(&raw_empty[s]);
+                mbar_arrive(&w_empty[s]);
             }
             // Epilogue of the previous item while this step's MMAs run.
             if (chunk == 0 && pending >= 0) {
@@ -465,6 +504,11 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
                 pending = -1;
             }
             if (chunk == P.chunks - 1) pending = item_k;
+            gm = gn;
+#pragma unroll
+            for (int r = 0; r < kTf32RowsPerThread; ++r)
+#pragma unroll
+                for (int ci = 0; ci < 8; ++ci) xv[r][ci] = xn[r][ci];
         }
         bool last_ok = pending >= 0;
         if (last_ok && lane == 0)

@@ -35,8 +35,9 @@ def test_golden_all_implementations(native, torch_cuda, golden_cases):
 
 
 def tf32_eligible(s):
-    rows_by_tma = s.w % 4 == 0 and s.w <= 256
-    return s.b_geometry and s.cpg in (8, 16, 32, 64) and (rows_by_tma or s.h * s.w <= 1024)
+    """One M-tile of 128 pixels plus its 2 * (W + 2) + 2 halo rows must fit the
+    converters' 1024 rows."""
+    return s.b_geometry and s.cpg in (8, 16, 32, 64) and 128 + 2 * (s.w + 2) + 2 <= 1024
 
 
 @pytest.mark.parametrize('kernel', ['general', 'direct_ldg', 'direct_tma', 'tf32x3', 'small'])
@@ -137,9 +138,19 @@ TF32_SHAPES = [
     (1, 16, 8, 16, 8), (2, 32, 12, 20, 16), (1, 64, 9, 12, 32), (1, 128, 9, 12, 64),
     (3, 64, 30, 28, 32), (2, 128, 56, 56, 64), (1, 256, 14, 16, 8), (4, 96, 7, 8, 16),
     (1, 64, 112, 112, 16), (2, 64, 33, 44, 64),
-    # whole-plane bulk staging (width not TMA-stageable)
+    # widths that are not a multiple of 4, tiny planes
     (3, 128, 7, 7, 64), (2, 64, 14, 14, 32), (1, 32, 13, 11, 16), (4, 16, 9, 5, 8), (1, 64, 30, 30, 64),
+    # widest row the converters reach (A rows = 1024), and one tile per image row
+    (1, 16, 6, 445, 16), (2, 8, 3, 300, 8),
 ]
+
+
+def test_tf32x3_refuses_rows_beyond_reach(native, torch_cuda):
+    s = Shape(n=1, cin=16, cout=16, h=4, w=446, groups=1)
+    x, wt = inputs(s, 5)
+    with pytest.raises(NativeError) as err:
+        run(native, torch_cuda, s, x, wt, kernel='tf32x3')
+    assert err.value.status == GC_UNSUPPORTED
 
 
 @pytest.mark.parametrize('n,c,h,w,cpg', TF32_SHAPES)
