@@ -648,15 +648,28 @@ int launch_direct(const gc_shape *p, const float *x, const float *w, float *y, b
 // ---- tcgen05 3xTF32 implicit GEMM ------------------------------------------------------
 bool tf32_cpg_supported(long long cpg) { return cpg == 8 || cpg == 16 || cpg == 32 || cpg == 64; }
 
+// Pixel rows per step and shared memory of the tensor-core path for a shape:
+// weights staged twice, A tiles of max(64, 2 cpg) rows twice, hi/lo pixel
+// tiles twice, the epilogue buffers and the barrier block.
+constexpr size_t kTf32SmemLimit = 227 * 1024;  // B200 opt-in shared memory per block
+long long tf32_rows_b(long long w) { return round_up(gcb::kTf32N + 2 * (w + 2) + 2, 8); }
+size_t tf32_smem(long long cpg, long long w) {
+    const long long m = std::max(64LL, 2 * cpg);
+    return static_cast<size_t>(2 * cpg * 72 * 4 + 2 * 9 * m * 32 + 4 * tf32_rows_b(w) * 32 +
+                               gcb::kConvWarps * gcb::kTf32EpiFloats * 4 + 128);
+}
+
 // Whether the tensor-core path can serve this shape: a supported group width,
-// 16-byte aligned weights (TMA-staged), A rows of one M-tile plus its halo
-// within the converters' reach, and 32-bit pixel indices.  Inputs are read
-// with plain loads: any width, any alignment.
+// 16-byte aligned weights (TMA-staged), one 256-pixel strip plus its
+// 2*(W+2)+2 halo rows within the converters' reach and shared memory, and
+// 32-bit pixel indices.  Inputs are read with plain loads: any width, any
+// alignment.
 bool tf32_eligible(const gc_shape *p, const void *x, const void *w) {
     (void)x;
     const long long cpg = p->cin / p->groups;
-    return tf32_cpg_supported(cpg) && aligned16(w) && 128 + 2 * (p->w + 2) + 2 <= gcb::kTf32MaxRows &&
-           p->h * (p->w + 2) < (1LL << 30) && p->n < (1LL << 30) && p->cin < (1LL << 30);
+    return tf32_cpg_supported(cpg) && aligned16(w) && tf32_rows_b(p->w) <= gcb::kTf32MaxRows &&
+           tf32_smem(cpg, p->w) <= kTf32SmemLimit && (p->h + 2) * (p->w + 2) < (1LL << 30) &&
+           p->n < (1LL << 30) && p->cin < (1LL << 30);
 }
 
 struct Tf32Plan {
@@ -666,12 +679,19 @@ struct Tf32Plan {
     int grid = 0;
 };
 
-const void *tf32_kernel_for(long long cpg) {
+// Kernel instance for a group width and the pixel rows per step (two or
+// four rows per converter thread).
+const void *tf32_kernel_for(long long cpg, long long rows_b) {
+    const bool two = rows_b <= 2 * gcb::kConvThreads;
     switch (cpg) {
-    case 8: return reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<8>);
-    case 16: return reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<16>);
-    case 32: return reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<32>);
-    case 64: return reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<64>);
+    case 8: return two ? reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<8, 2>)
+                       : reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<8, 4>);
+    case 16: return two ? reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<16, 2>)
+                        : reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<16, 4>);
+    case 32: return two ? reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<32, 2>)
+                        : reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<32, 4>);
+    case 64: return two ? reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<64, 2>)
+                        : reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<64, 4>);
     default: return nullptr;
     }
 }
@@ -683,66 +703,59 @@ int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
     int st = device_facts(dev, facts);
     if (st != GC_OK) return st;
     const long long N = p->n, C = p->cin, H = p->h, W = p->w, cpg = C / p->groups;
-    const long long wp = W + 2;
-    const long long tiles = ceil_div(H * wp, 128);
-    int best_t = 0;
-    double best_cost = 0.0;
-    gcb::Tf32Params best{};
-    size_t best_smem = 0;
-    for (long long T = 1; T <= tiles && 2 * T * cpg <= 512; ++T) {
-        const long long rows_a = round_up(T * 128 + 2 * wp + 2, 8);
-        if (rows_a > gcb::kTf32MaxRows) break;
-        const long long wraw_bytes = cpg * 72 * 4;
-        const long long a_bytes = rows_a * 32;
-        const long long b_bytes = 9 * cpg * 32;
-        const size_t smem = static_cast<size_t>(2 * wraw_bytes + 4 * a_bytes + 4 * b_bytes + 128);
-        if (smem > static_cast<size_t>(facts.smem_optin)) break;
-        long long cols = 32;
-        while (cols < 2 * T * cpg) cols *= 2;
-        gcb::Tf32Params P{};
-        P.n = static_cast<int>(N);
-        P.c = static_cast<int>(C);
-        P.h = static_cast<int>(H);
-        P.wd = static_cast<int>(W);
-        P.cpg = static_cast<int>(cpg);
-        P.groups = static_cast<int>(p->groups);
-        P.wp = static_cast<int>(wp);
-        P.tiles = static_cast<int>(tiles);
-        P.T = static_cast<int>(T);
-        P.strips = static_cast<int>(ceil_div(tiles, T));
-        const long long items = static_cast<long long>(p->groups) * N * P.strips;
-        if (items >= (1LL << 31)) break;
-        P.items = static_cast<int>(items);
-        P.chunks = static_cast<int>(cpg / 8);
-        P.rows_a = static_cast<int>(rows_a);
-        P.a_bytes = static_cast<unsigned>(a_bytes);
-        P.b_bytes = static_cast<unsigned>(b_bytes);
-        P.wraw_bytes = static_cast<unsigned>(wraw_bytes);
-        P.tmem_cols = static_cast<unsigned>(cols);
-        // Time model per step (8 input channels) of an item, in shared-memory
-        // cycles: the tensor core reads A (4 KB) and B (cpg * 32 bytes) three
-        // times per tap and M-tile; the converters' work (A rows incl. the
-        // halo, and the chunk's weights) overlaps it; a fixed hand-off cost
-        // per step.  Items run in waves over the SMs.
-        const double mma = static_cast<double>(T) * 27.0 * (4096.0 + 32.0 * cpg) / 128.0;
-        const double conv = (static_cast<double>(rows_a) * 8.0 + 72.0 * cpg) * 12.0 / 256.0;
-        const double cost = static_cast<double>(ceil_div(items, facts.sms)) * (std::max(mma, conv) + 400.0);
-        if (best_t > 0 && cost >= best_cost) continue;
-        best_cost = cost;
-        best = P;
-        best_t = static_cast<int>(T);
-        best_smem = smem;
+    const long long wp = W + 2, hp2 = H + 2;
+    const long long rows_b = tf32_rows_b(W);
+    const size_t smem = tf32_smem(cpg, W);
+    if (rows_b > gcb::kTf32MaxRows || smem > std::min(kTf32SmemLimit, static_cast<size_t>(facts.smem_optin)))
+        return gc_error(GC_UNSUPPORTED, "3xTF32 path: pixel strip does not fit");
+    // Images per block: every item costs the same MMA time (one 256-pixel
+    // strip, all channel chunks), so pick the block that needs the fewest
+    // waves of items over the SMs; ties go to the smaller block.
+    long long best_nb = 1, best_waves = -1, best_items = 0, best_strips = 0;
+    for (long long nb = 1; nb <= N; ++nb) {
+        const long long out_rows = (nb - 1) * hp2 + H;
+        if (nb > 1 && out_rows * wp > 16 * gcb::kTf32N) break;  // stacking only pays for small planes
+        if (nb * hp2 * wp >= (1LL << 30)) break;
+        const long long strips = ceil_div(out_rows * wp, gcb::kTf32N);
+        const long long items = static_cast<long long>(p->groups) * ceil_div(N, nb) * strips;
+        if (items >= (1LL << 31)) continue;
+        const long long waves = ceil_div(items, facts.sms);
+        if (best_waves < 0 || waves < best_waves) {
+            best_waves = waves;
+            best_nb = nb;
+            best_items = items;
+            best_strips = strips;
+        }
     }
-    if (best_t == 0) return gc_error(GC_UNSUPPORTED, "3xTF32 path: no M-tile strip fits in shared memory");
-    const void *fn = tf32_kernel_for(cpg);
+    if (best_waves < 0) return gc_error(GC_UNSUPPORTED, "3xTF32 path: too many work items");
+    gcb::Tf32Params P{};
+    P.n = static_cast<int>(N);
+    P.c = static_cast<int>(C);
+    P.h = static_cast<int>(H);
+    P.wd = static_cast<int>(W);
+    P.cpg = static_cast<int>(cpg);
+    P.groups = static_cast<int>(p->groups);
+    P.wp = static_cast<int>(wp);
+    P.nb = static_cast<int>(best_nb);
+    P.blocks = static_cast<int>(ceil_div(N, best_nb));
+    P.out_rows = static_cast<int>((best_nb - 1) * hp2 + H);
+    P.strips = static_cast<int>(best_strips);
+    P.items = static_cast<int>(best_items);
+    P.chunks = static_cast<int>(cpg / 8);
+    P.m = static_cast<int>(std::max(64LL, 2 * cpg));
+    P.rows_b = static_cast<int>(rows_b);
+    P.a_bytes = static_cast<unsigned>(9 * P.m * 32);
+    P.b_bytes = static_cast<unsigned>(rows_b * 32);
+    P.wraw_bytes = static_cast<unsigned>(cpg * 72 * 4);
+    const void *fn = tf32_kernel_for(cpg, rows_b);
     int ctas = 0;
-    st = kernel_occupancy(dev, fn, gcb::kTf32Threads, best_smem, facts.smem_optin, ctas);
+    st = kernel_occupancy(dev, fn, gcb::kTf32Threads, smem, facts.smem_optin, ctas);
     if (st != GC_OK) return st;
     if (ctas < 1) return gc_error(GC_UNSUPPORTED, "3xTF32 path: kernel does not fit on an SM");
-    out.P = best;
+    out.P = P;
     out.fn = fn;
-    out.smem = best_smem;
-    out.grid = static_cast<int>(std::min<long long>(best.items, static_cast<long long>(facts.sms)));
+    out.smem = smem;
+    out.grid = static_cast<int>(std::min<long long>(P.items, static_cast<long long>(facts.sms)));
     return GC_OK;
 }
 
@@ -762,10 +775,10 @@ int launch_tf32(const gc_shape *p, const float *x, const float *w, float *y, int
     if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
     char buf[256];
     std::snprintf(buf, sizeof(buf),
-                  "kernel=tf32x3 engine=tcgen05 n_cta=%d block=320 smem=%zu T=%d strips=%d items=%d chunks=%d "
-                  "rows_a=%d tmem_cols=%u",
-                  plan.grid, plan.smem, plan.P.T, plan.P.strips, plan.P.items, plan.P.chunks, plan.P.rows_a,
-                  plan.P.tmem_cols);
+                  "kernel=tf32x3 engine=tcgen05 n_cta=%d block=320 smem=%zu M=%d N=%d nb=%d strips=%d items=%d "
+                  "chunks=%d rows_b=%d",
+                  plan.grid, plan.smem, plan.P.m, gcb::kTf32N, plan.P.nb, plan.P.strips, plan.P.items,
+                  plan.P.chunks, plan.P.rows_b);
     g_plan = buf;
     return GC_OK;
 }
@@ -1037,8 +1050,8 @@ int gc_b200_conv(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_t
         return gc_error(GC_UNSUPPORTED, "small-image kernel needs at most 512 pixels per plane");
     if (kernel == GC_B200_TF32X3 && !tf32_eligible(p, x->data, w->data))
         return gc_error(GC_UNSUPPORTED,
-                        "3xTF32 path needs 8, 16, 32 or 64 channels per group, width % 4 == 0, "
-                        "width <= 256 and 16-byte aligned input and weights");
+                        "3xTF32 path needs 8, 16, 32 or 64 channels per group, 16-byte aligned weights "
+                        "and a 256-pixel strip plus halo within 1024 rows and shared memory");
     int dev = -1;
     st = device_and_stream_checks(x, w, y, stream, dev);
     if (st != GC_OK) return st;

@@ -2,41 +2,57 @@
 // on the 5th-generation tensor cores (tcgen05, accumulators in TMEM), with
 // 3xTF32 split precision so the result stays within FP32 tolerance.
 //
-// GEMM view, per (image n, group g):  D[o, co] = sum_tap sum_ci A_tap[o, ci] * B_tap[ci, co]
-//   o   : output pixel in "padded" numbering o = h * Wp + w, Wp = W + 2 (the two
-//         extra columns per row are computed and discarded);
-//   A_tap[o, ci] = Xpad[o + r*Wp + s]  for tap (r, s), where Xpad is the input
-//         with one zero row/column on every side, numbered the same way.  Every
-//         tap is therefore a pure row shift of one shared-memory tile;
-//   B_tap[ci, co] = w[g*cpg + co, ci, r, s].
-// tcgen05.mma.kind::tf32, M = 128 pixels, N = cpg output channels, K = 8 input
-// channels per instruction.  x = hi + lo with hi = x rounded to TF32 (nearest,
-// ties away) and lo = x - hi (exact in FP32; the tensor core reads its top 19
-// bits); D += A_hi B_hi + A_hi B_lo + A_lo B_hi.  Per product the dropped terms
-// are below 2^-20 of |x*w|, far inside the 1e-5 * sum|x*w| acceptance bound.
+// GEMM view, per group g and a block of `nb` images stacked along H:
+//   D[m, o] = sum_tap sum_ci A_tap[m, ci] * X[o + r*Wp + s, ci]
+//   o   : output pixel of the block in "padded" numbering: image k's padded
+//         plane (H+2 rows of Wp = W+2 columns, zero border) occupies rows
+//         k*(H+2) .. k*(H+2)+H+1, and o = row*Wp + column.  The zero border
+//         separates stacked images, so every tap (r, s) is a pure shift of
+//         the pixel tile by r*Wp + s rows, and small images share one tile;
+//   X   : the padded input of the block, 8 channels per K step;
+//   A_tap = [w_hi; w_lo]: the tap's weights split x = hi + lo (hi = x rounded
+//         to TF32, ties away; lo the exact FP32 remainder, of which the tensor
+//         core reads the top 19 bits), stacked along M so one MMA applies both.
+// Two MMAs per tap and 8-channel step: D += A_tap X_hi, D += A_tap X_lo, i.e.
+// D_hi + D_lo = (w_hi + w_lo)(x_hi + x_lo) up to the truncation of the lo
+// parts (below 2^-20 of |x*w| per product, far inside the 1e-5 * sum|x*w|
+// acceptance bound).  tcgen05.mma.kind::tf32 with M = 128 (cpg 64) or 64
+// rows of weights and N = 256 pixels: at this shape the tensor core runs at
+// its full TF32 rate whatever the per-tap shift of the pixel operand.
 //
-// Work item = (group, image, strip of T consecutive 128-pixel M-tiles); pipeline
-// step = (item, chunk of 8 input channels).  Per step:
-//   - the converter warps read the step's input pixels straight from global
-//     memory (8 coalesced channel loads per A row, issued one step ahead into
-//     registers so their latency hides behind the current step), split them
-//     into hi/lo TF32 rows of the K-major no-swizzle canonical layout (core
-//     matrix = 8 rows x 16 bytes; rows 16 bytes apart, the two 4-channel halves
-//     LBO apart, so a shift by one pixel is +16 bytes of descriptor start
-//     address), and split the chunk's weights, which one lane of the weight
-//     warp stages by TMA (2-D box of the [C][cpg*9] weight matrix);
-//   - one lane of the MMA warp issues 27*T MMAs and commits them to the
-//     mbarrier that frees the A/B stage.
-// The accumulator of item j lives in TMEM buffer j % 2, so the epilogue of item
-// j (tcgen05.ld -> coalesced streaming stores of whole output rows) overlaps
-// the MMAs of item j+1.  Every wait is bounded; on timeout the kernel records
-// it in the status word, drains what it issued, frees its TMEM and returns.
-// Inputs are assumed finite: for an infinite input the split is undefined and
-// the outputs it reaches come out NaN.
+// Rows of A: the M rows are spread over the four TMEM lane quadrants (M = 128:
+// row m -> lane m; M = 64: rows 16q..16q+15 -> lanes 32q..32q+15), and within
+// a quadrant the first half holds w_hi of a block of output channels, the
+// second half w_lo of the same channels, so the epilogue adds the two parts
+// with one warp shuffle.
+//
+// Work item = (group, image block, strip of 256 pixels); pipeline step =
+// (item, chunk of 8 input channels).  Per step:
+//   - the converter warps load the step's pixels from global memory into
+//     registers (per thread its own pixel rows, 8 coalesced channel loads
+//     each; two register sets alternate between even and odd steps, and each
+//     set is refilled for step k+2 as soon as step k is converted, so the
+//     loads have a whole step to land), split them
+//     into the hi/lo pixel tiles (K-major no-swizzle canonical layout: core
+//     matrix = 8 rows x 16 bytes, rows 16 bytes apart, the two 4-channel halves
+//     LBO apart, so a shift by one pixel is +16 bytes of descriptor address),
+//     and split the chunk's weights, which one lane of the weight warp stages
+//     by TMA (2-D box of the [C][cpg*9] weight matrix), into the A tiles;
+//   - one lane of the MMA warp issues the 18 MMAs and commits them to the
+//     mbarrier that frees the stage.
+// The accumulator of item j lives in TMEM columns 256*(j % 2), so the epilogue
+// of item j (tcgen05.ld -> pair sum -> per-warp transpose in shared memory ->
+// coalesced streaming stores, consecutive lanes on consecutive pixels)
+// overlaps the MMAs of item j+1.  Every wait is bounded; on timeout the kernel
+// records it in the status word, drains what it issued, frees its TMEM and
+// returns.  Inputs are assumed finite: for an infinite input the split is
+// undefined and the outputs it reaches come out NaN.
 #pragma once
 #include "device_util.cuh"
 
 namespace gcb {
+
+constexpr int kTf32N = 256;  // pixels per item: the MMA's N
 
 struct Tf32Params {
     const float *x;
@@ -44,17 +60,20 @@ struct Tf32Params {
     float *y;
     int n, c, h, wd, cpg, groups;
     int wp;              // padded row pitch W + 2
-    int tiles;           // 128-pixel M-tiles per image: ceil(h * wp / 128)
-    int T;               // M-tiles per item
-    int strips;          // ceil(tiles / T)
-    int items;           // groups * n * strips
+    int nb;              // images stacked into one block
+    int blocks;          // ceil(n / nb)
+    int out_rows;        // padded rows holding the block's outputs: (nb - 1) * (h + 2) + h
+    int strips;          // ceil(out_rows * wp / 256)
+    int items;           // groups * blocks * strips
     int chunks;          // cpg / 8
-    int rows_a;          // A rows per step: T*128 + 2*wp + 2, rounded up to 8 (<= kTf32MaxRows)
-    unsigned a_bytes;    // bytes of one A tile (hi or lo): rows_a * 32
-    unsigned b_bytes;    // bytes of one B tile set (hi or lo): 9 taps * cpg * 32
-    unsigned wraw_bytes; // bytes of one staged weight chunk: cpg * 72 * 4
-    unsigned tmem_cols;  // allocated TMEM columns (power of two)
+    int m;               // MMA M: max(64, 2 * cpg)
+    int rows_b;          // pixel rows per step: 256 + 2*wp + 2, rounded up to 8 (<= kTf32MaxRows)
+    unsigned a_bytes;    // one step's weight tiles: 9 taps * m * 32
+    unsigned b_bytes;    // one pixel tile (hi or lo): rows_b * 32
+    unsigned wraw_bytes; // one staged weight chunk: cpg * 72 * 4
 };
+
+constexpr int kTf32EpiFloats = 16 * 33;  // per-warp epilogue transpose buffer (16 channels x 32 pixels, padded)
 
 // ---- tcgen05 helpers -----------------------------------------------------------------
 // Shared-memory matrix descriptor, K-major, no swizzle (canonical layout
@@ -68,9 +87,10 @@ __device__ __forceinline__ uint64_t umma_desc(uint32_t saddr, uint32_t lbo_bytes
     return d;         // base offset 0, absolute LBO mode 0, layout SWIZZLE_NONE (0)
 }
 
-// Instruction descriptor: D f32, A/B tf32, both K-major, M = 128, N = n.
-__host__ __device__ constexpr uint32_t umma_idesc_tf32(int n) {
-    return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(n >> 3) << 17) | (8u << 24);
+// Instruction descriptor: D f32, A/B tf32, both K-major, M = m (64 or 128), N = n.
+__host__ __device__ constexpr uint32_t umma_idesc_tf32(int m, int n) {
+    return (1u << 4) | (2u << 7) | (2u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+           (static_cast<uint32_t>(m >> 4) << 24);
 }
 
 __device__ __forceinline__ void umma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -111,6 +131,23 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t cols) {
                  : "memory");
 }
 
+// 32 consecutive accumulator columns of this warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // 16 consecutive accumulator columns of this warp's 32 TMEM lanes.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     uint32_t r[16];
@@ -149,10 +186,10 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
 }
 
 // ---- warp-specialized kernel -------------------------------------------------------------
-// Roles (320 threads): warps 0-7 load and convert the A rows and the weights
-// to hi/lo TF32 tiles and run the epilogues; warp 8 (one lane) issues the
-// MMAs; warp 9 (one lane) issues the weight TMA loads.  Stages are handed
-// over through full/empty mbarriers:
+// Roles (320 threads): warps 0-7 load and convert the pixel rows and the
+// weights and run the epilogues; warp 8 (one lane) issues the MMAs; warp 9
+// (one lane) issues the weight TMA loads.  Stages are handed over through
+// full/empty mbarriers:
 //   w_full   (TMA -> converters)     w_empty  (converters -> TMA)
 //   ab_full  (converters -> MMA)     ab_empty (MMA commit -> converters)
 //   acc_full (MMA commit -> epilogue)  acc_empty (epilogue -> MMA)
@@ -164,8 +201,7 @@ constexpr int kConvThreads = kConvWarps * 32;
 constexpr int kMmaWarp = 8;
 constexpr int kTmaWarp = 9;
 constexpr int kTf32Threads = 320;
-constexpr int kTf32RowsPerThread = 4;
-constexpr int kTf32MaxRows = kTf32RowsPerThread * kConvThreads;
+constexpr int kTf32MaxRows = 4 * kConvThreads;  // pixel rows per step the converters reach
 
 // 2-D tiled load (weights viewed as [C rows][cpg*9 columns]).
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int c0, int c1, uint64_t *bar) {
@@ -176,14 +212,14 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
-// Item order: group slowest, so consecutive items of one CTA mostly share the
-// group's weights in L2.
-__device__ __forceinline__ void tf32_decode(const Tf32Params &P, int item, int &g, int &n, int &strip) {
+// Item order: strip fastest, group slowest, so consecutive items of one CTA
+// mostly share the group's weights in L2.
+__device__ __forceinline__ void tf32_decode(const Tf32Params &P, int item, int &g, int &blk, int &strip) {
     const unsigned u = static_cast<unsigned>(item);
     const unsigned t = u / static_cast<unsigned>(P.strips);
     strip = static_cast<int>(u - t * static_cast<unsigned>(P.strips));
-    g = static_cast<int>(t / static_cast<unsigned>(P.n));
-    n = static_cast<int>(t - static_cast<unsigned>(g) * static_cast<unsigned>(P.n));
+    g = static_cast<int>(t / static_cast<unsigned>(P.blocks));
+    blk = static_cast<int>(t - static_cast<unsigned>(g) * static_cast<unsigned>(P.blocks));
 }
 
 // x = hi + lo: hi rounded to TF32 (nearest, ties away from zero) by integer
@@ -193,110 +229,114 @@ __device__ __forceinline__ void tf32_split(float x, uint32_t &hi, uint32_t &lo) 
     lo = __float_as_uint(x - __uint_as_float(hi));
 }
 
-// Converter thread's A rows of one item: plane offset of each row's input
-// pixel and a bit per row that lies inside the image (else the row is zero
-// padding or past the strip's rows).
+// Converter thread's pixel rows of one item: element offset (image and
+// in-plane position) of each row's input pixel, and a bit per row that lies
+// inside an image (else the row is zero border or past the block).
+template <int ROWS>
 struct RowGeom {
-    int off[kTf32RowsPerThread];
+    long long off[ROWS];
     unsigned valid;
 };
 
-__device__ __forceinline__ RowGeom tf32_rows(const Tf32Params &P, int strip, int ctid) {
-    RowGeom gm;
+template <int ROWS>
+__device__ __forceinline__ RowGeom<ROWS> tf32_rows(const Tf32Params &P, int blk, int strip, int ctid) {
+    RowGeom<ROWS> gm;
     gm.valid = 0;
-    const int o0 = strip * P.T * 128;
+    const int o0 = strip * kTf32N;
+    const int hp2 = P.h + 2;
+    const long long image_floats = static_cast<long long>(P.c) * P.h * P.wd;
 #pragma unroll
-    for (int r = 0; r < kTf32RowsPerThread; ++r) {
+    for (int r = 0; r < ROWS; ++r) {
         const int i = ctid + r * kConvThreads;
         const int o = o0 + i;
-        const int hp = o / P.wp;
-        const int ih = hp - 1, iw = o - hp * P.wp - 1;
-        const bool in = i < P.rows_a && ih >= 0 && ih < P.h && iw >= 0 && iw < P.wd;
-        gm.off[r] = in ? ih * P.wd + iw : 0;
+        const int vrow = o / P.wp;
+        const int k = vrow / hp2;
+        const int ih = vrow - k * hp2 - 1, iw = o - vrow * P.wp - 1;
+        const int img = blk * P.nb + k;
+        const bool in = i < P.rows_b && k < P.nb && img < P.n && ih >= 0 && ih < P.h && iw >= 0 && iw < P.wd;
+        gm.off[r] = in ? static_cast<long long>(img) * image_floats + ih * P.wd + iw : 0;
         gm.valid |= in ? (1u << r) : 0u;
     }
     return gm;
 }
 
-// The 8 channels of the chunk at every A row of this thread (0 outside the image).
-__device__ __forceinline__ void tf32_load_rows(const Tf32Params &P, int item, int chunk, const RowGeom &gm,
-                                               float (&v)[kTf32RowsPerThread][8]) {
-    int g, n, strip;
-    tf32_decode(P, item, g, n, strip);
+// The 8 channels of the chunk at every pixel row of this thread (0 outside images).
+template <int ROWS>
+__device__ __forceinline__ void tf32_load_rows(const Tf32Params &P, int g, int chunk, const RowGeom<ROWS> &gm,
+                                               float (&v)[ROWS][8]) {
     const long long hw = static_cast<long long>(P.h) * P.wd;
-    const float *base = P.x + (static_cast<long long>(n) * P.c + g * P.cpg + chunk * 8) * hw;
+    const float *base = P.x + (static_cast<long long>(g) * P.cpg + chunk * 8) * hw;
 #pragma unroll
-    for (int r = 0; r < kTf32RowsPerThread; ++r) {
+    for (int r = 0; r < ROWS; ++r) {
         const bool in = (gm.valid >> r) & 1u;
 #pragma unroll
-        for (int ci = 0; ci < 8; ++ci) v[r][ci] = in ? __ldg(base + ci * hw + gm.off[r]) : 0.0f;
+        for (int ci = 0; ci < 8; ++ci) v[r][ci] = in ? __ldg(base + gm.off[r] + ci * hw) : 0.0f;
     }
 }
 
-// Converter warps: epilogue of one item.  Warp w reads TMEM lanes
-// 32*(w%4).. (32 consecutive pixels of each M-tile) and output channels
-// [w/4 * NCO/2, (w/4+1) * NCO/2); one coalesced store per channel.
-template <int NCO>
-__device__ __forceinline__ void tf32_epilogue(const Tf32Params &P, uint32_t acc, int item, int warp, int lane) {
-    constexpr int HALF = NCO / 2;
-    int g, n, strip;
-    tf32_decode(P, item, g, n, strip);
-    const int o0 = strip * P.T * 128;
-    const int quad = warp & 3, half = warp >> 2;
-    const long long plane_out = static_cast<long long>(P.h) * P.wd;
-    float *yg = P.y + (static_cast<long long>(n) * P.c + static_cast<long long>(g) * P.cpg + half * HALF) * plane_out;
-    for (int t = 0; t < P.T; ++t) {
-        if (strip * P.T + t >= P.tiles) break;
-        const int o = o0 + t * 128 + quad * 32 + lane;
-        const int oh = o / P.wp, ow = o - oh * P.wp;
-        const bool store = oh < P.h && ow < P.wd;
-        float *yp = yg + static_cast<long long>(oh) * P.wd + ow;
-        const uint32_t taddr = acc + t * NCO + half * HALF + (static_cast<uint32_t>(quad * 32) << 16);
-        if (HALF % 16 == 0) {
+// Converter warps: epilogue of one item.  Warp w reads lane quadrant w % 4
+// and pixel columns [128*(w/4), 128*(w/4) + 128) in chunks of 32.  In the
+// quadrant, lane l (l < HALF) holds the w_hi rows and lane l + HALF the w_lo
+// rows of the same output channel: one shuffle adds them (lane l keeps
+// pixels 0-15 of the chunk, lane l + HALF pixels 16-31).  The sums go through
+// the warp's transpose buffer, so that the stores run with consecutive lanes
+// on consecutive pixels of one output channel.
+template <int M>
+__device__ __forceinline__ void tf32_epilogue(const Tf32Params &P, uint32_t acc, int item, int warp, int lane,
+                                              float *ep) {
+    constexpr int HALF = M / 8;  // output channels per lane quadrant
+    int g, blk, strip;
+    tf32_decode(P, item, g, blk, strip);
+    const int quad = warp & 3, colhalf = warp >> 2;
+    if (quad * HALF >= P.cpg) return;  // quadrant holds only zero rows (warp-uniform)
+    const int nco = min(HALF, P.cpg - quad * HALF);
+    const bool low = (lane & HALF) == 0;
+    const bool writer = lane < 2 * HALF && (lane & (HALF - 1)) < nco;
+    const int hp2 = P.h + 2;
+    const long long hw = static_cast<long long>(P.h) * P.wd;
+    const long long image_floats = static_cast<long long>(P.c) * hw;
+    const int out_px = P.out_rows * P.wp;
+    float *const ych = P.y + (static_cast<long long>(g) * P.cpg + quad * HALF) * hw;
+    float *const epw = ep + (lane & (HALF - 1)) * 33 + (low ? 0 : 16);
+#pragma unroll 1
+    for (int c32 = 0; c32 < 4; ++c32) {
+        const int col0 = colhalf * 128 + c32 * 32;
+        float v[32];
+        tmem_ld32(acc + col0 + (static_cast<uint32_t>(quad * 32) << 16), v);
 #pragma unroll
-            for (int c = 0; c < HALF; c += 16) {
-                float v[16];
-                tmem_ld16(taddr + c, v);
-                if (store) {
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) st_stream(yp + (c + i) * plane_out, v[i]);
-                }
-            }
-        } else if (HALF % 8 == 0) {
-#pragma unroll
-            for (int c = 0; c < HALF; c += 8) {
-                float v[8];
-                tmem_ld8(taddr + c, v);
-                if (store) {
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) st_stream(yp + (c + i) * plane_out, v[i]);
-                }
-            }
-        } else {
-#pragma unroll
-            for (int c = 0; c < HALF; c += 4) {
-                float v[4];
-                tmem_ld4(taddr + c, v);
-                if (store) {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) st_stream(yp + (c + i) * plane_out, v[i]);
-                }
-            }
+        for (int i = 0; i < 16; ++i) {
+            const float send = low ? v[16 + i] : v[i];
+            const float r = __shfl_xor_sync(0xffffffffu, send, HALF);
+            if (writer) epw[i] = (low ? v[i] : v[16 + i]) + r;
         }
+        __syncwarp();
+        // lane -> pixel o of the chunk
+        const int o = strip * kTf32N + col0 + lane;
+        const int vrow = o / P.wp, col = o - vrow * P.wp;
+        const int k = vrow / hp2, hh = vrow - k * hp2;
+        const int img = blk * P.nb + k;
+        if (o < out_px && hh < P.h && col < P.wd && img < P.n) {
+            float *yp = ych + img * image_floats + static_cast<long long>(hh) * P.wd + col;
+            for (int j = 0; j < nco; ++j) st_stream(yp + j * hw, ep[j * 33 + lane]);
+        }
+        __syncwarp();
     }
 }
 
-template <int NCO>
+template <int CPG, int ROWS>
 __global__ void __launch_bounds__(kTf32Threads, 1)
     tf32x3_conv_kernel(const __grid_constant__ Tf32Params P, const __grid_constant__ CUtensorMap wmap) {
+    constexpr int M = CPG * 2 > 64 ? CPG * 2 : 64;
+    constexpr int RQ = M / 4;      // A rows per lane quadrant
+    constexpr int HALF = RQ / 2;   // output channels per quadrant
     extern __shared__ __align__(1024) unsigned char smem_raw[];
-    // layout: wraw[2] | a_hi[2] | a_lo[2] | b_hi[2] | b_lo[2] | barriers | words
+    // layout: wraw[2] | a[2] | x_hi[2] | x_lo[2] | epilogue[8 warps] | barriers | words
     unsigned char *const wraw0 = smem_raw;
-    unsigned char *const ahi0 = wraw0 + 2 * P.wraw_bytes;
-    unsigned char *const alo0 = ahi0 + 2 * P.a_bytes;
-    unsigned char *const bhi0 = alo0 + 2 * P.a_bytes;
-    unsigned char *const blo0 = bhi0 + 2 * P.b_bytes;
-    uint64_t *const bars = reinterpret_cast<uint64_t *>(blo0 + 2 * P.b_bytes);
+    unsigned char *const a0 = wraw0 + 2 * P.wraw_bytes;
+    unsigned char *const xhi0 = a0 + 2 * P.a_bytes;
+    unsigned char *const xlo0 = xhi0 + 2 * P.b_bytes;
+    float *const ep0 = reinterpret_cast<float *>(xlo0 + 2 * P.b_bytes);
+    uint64_t *const bars = reinterpret_cast<uint64_t *>(ep0 + kConvWarps * kTf32EpiFloats);
     uint64_t *const w_full = bars, *const w_empty = bars + 2, *const ab_full = bars + 4,
                     *const ab_empty = bars + 6, *const acc_full = bars + 8, *const acc_empty = bars + 10;
     uint32_t *const tmem_slot = reinterpret_cast<uint32_t *>(bars + 12);
@@ -319,7 +359,11 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
         *abort_word = 0;
         fence_barrier_init();
     }
-    if (warp == 0) tmem_alloc(tmem_slot, P.tmem_cols);
+    // Rows of A no output channel uses (cpg < M / 2) stay zero for the whole kernel.
+    if (CPG * 2 < M)
+        for (unsigned e = tid; e < 2 * P.a_bytes / 16; e += blockDim.x)
+            reinterpret_cast<uint4 *>(a0)[e] = make_uint4(0u, 0u, 0u, 0u);
+    if (warp == 0) tmem_alloc(tmem_slot, 2 * kTf32N);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -340,8 +384,8 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
                     released = k - 2;
                 }
                 const int item_k = k / P.chunks, chunk = k - item_k * P.chunks;
-                int g, n, strip;
-                tf32_decode(P, first + item_k * stride, g, n, strip);
+                int g, blk, strip;
+                tf32_decode(P, first + item_k * stride, g, blk, strip);
                 mbar_arrive_expect_tx(&w_full[s], P.wraw_bytes);
                 tma_load_2d(wraw0 + s * P.wraw_bytes, &wmap, chunk * 72, g * P.cpg, &w_full[s]);
                 issued = k;
@@ -354,8 +398,7 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
         }
     } else if (warp == kMmaWarp) {
         if (lane == 0) {
-            constexpr uint32_t kIdesc = umma_idesc_tf32(NCO);
-            const uint32_t lbo_a = P.rows_a * 16u, lbo_b = NCO * 16u;
+            constexpr uint32_t kIdesc = umma_idesc_tf32(M, kTf32N);
             int committed = -1;
             for (int k = 0; k < steps; ++k) {
                 const int s = k & 1;
@@ -367,36 +410,25 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
                                kStatusMmaTimeout))
                     break;
                 tc_fence_after();
-                int g, n, strip;
-                tf32_decode(P, first + item_k * stride, g, n, strip);
-                const uint32_t acc = tmem_base + static_cast<uint32_t>((item_k & 1) * P.T * NCO);
+                const uint32_t d = tmem_base + static_cast<uint32_t>((item_k & 1) * kTf32N);
                 // Descriptors of the stage's tiles; a shift of the start
                 // address is an add on the descriptor's low field (16-byte
                 // units; every offset stays inside shared memory, so no carry
                 // leaves the field).
-                const uint64_t dah0 = umma_desc(smem_addr(ahi0 + s * P.a_bytes), lbo_a, 128);
-                const uint64_t dal0 = umma_desc(smem_addr(alo0 + s * P.a_bytes), lbo_a, 128);
-                const uint64_t dbh0 = umma_desc(smem_addr(bhi0 + s * P.b_bytes), lbo_b, 128);
-                const uint64_t dbl0 = umma_desc(smem_addr(blo0 + s * P.b_bytes), lbo_b, 128);
+                const uint64_t da0 = umma_desc(smem_addr(a0 + s * P.a_bytes), M * 16u, 128);
+                const uint64_t dxh0 = umma_desc(smem_addr(xhi0 + s * P.b_bytes), P.rows_b * 16u, 128);
+                const uint64_t dxl0 = umma_desc(smem_addr(xlo0 + s * P.b_bytes), P.rows_b * 16u, 128);
                 const uint32_t wp = static_cast<uint32_t>(P.wp);
-                for (int t = 0; t < P.T; ++t) {
-                    if (strip * P.T + t >= P.tiles) break;
-                    const uint32_t d = acc + t * NCO;
-                    const uint32_t a_t = static_cast<uint32_t>(t) * 128u;
 #pragma unroll
-                    for (int tap = 0; tap < 9; ++tap) {
-                        const uint32_t r = tap / 3, sx = tap % 3;
-                        const uint64_t aoff = a_t + r * wp + sx;              // rows of 16 bytes
-                        const uint64_t boff = static_cast<uint64_t>(tap) * NCO * 2u;  // 32 bytes per co
-                        const uint64_t dah = dah0 + aoff, dal = dal0 + aoff;
-                        const uint64_t dbh = dbh0 + boff, dbl = dbl0 + boff;
-                        if (tap == 0)
-                            umma_tf32(d, dah, dbh, kIdesc, chunk != 0);
-                        else
-                            umma_tf32(d, dah, dbh, kIdesc, true);
-                        umma_tf32(d, dah, dbl, kIdesc, true);
-                        umma_tf32(d, dal, dbh, kIdesc, true);
-                    }
+                for (int tap = 0; tap < 9; ++tap) {
+                    const uint32_t r = tap / 3, sx = tap % 3;
+                    const uint64_t aoff = static_cast<uint64_t>(tap) * M * 2u;  // M rows of 32 bytes
+                    const uint64_t xoff = r * wp + sx;                          // pixel rows of 16 bytes
+                    if (tap == 0)
+                        umma_tf32(d, da0 + aoff, dxh0 + xoff, kIdesc, chunk != 0);
+                    else
+                        umma_tf32(d, da0 + aoff, dxh0 + xoff, kIdesc, true);
+                    umma_tf32(d, da0 + aoff, dxl0 + xoff, kIdesc, true);
                 }
                 umma_commit(&ab_empty[s]);
                 if (chunk == P.chunks - 1) umma_commit(&acc_full[item_k & 1]);
@@ -409,33 +441,32 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
     } else {
         // Converter / epilogue warps.
         const int ctid = tid;  // 0 .. 255
-        const uint32_t lbo_a = P.rows_a * 16u;
-        constexpr int kBVals = 72 * NCO;  // weight values per chunk (hi and lo each)
-        constexpr int kBPerThread = (kBVals + kConvThreads - 1) / kConvThreads;
+        const uint32_t lbo_x = P.rows_b * 16u;
+        constexpr int kWVals = 72 * CPG;  // weights per chunk
+        constexpr int kWPerThread = (kWVals + kConvThreads - 1) / kConvThreads;
+        float *const ep = ep0 + warp * kTf32EpiFloats;
         int pending = -1;  // per-CTA item index whose epilogue is due
-        RowGeom gm{};
-        float xv[kTf32RowsPerThread][8];
-        if (steps > 0) {
-            int g, n, strip;
-            tf32_decode(P, first, g, n, strip);
-            gm = tf32_rows(P, strip, ctid);
-            tf32_load_rows(P, first, 0, gm, xv);
-        }
-        for (int k = 0; k < steps; ++k) {
+        bool failed = false;
+        // Load side: the item whose row geometry is cached.
+        int load_item = -1, load_g = 0;
+        RowGeom<ROWS> lgm{};
+        auto load = [&](int j, float (&buf)[ROWS][8]) {  // step j's pixel rows into buf
+            if (j >= steps) return;
+            const int item_j = j / P.chunks, chunk_j = j - item_j * P.chunks;
+            if (item_j != load_item) {
+                int blk, strip;
+                tf32_decode(P, first + item_j * stride, load_g, blk, strip);
+                lgm = tf32_rows<ROWS>(P, blk, strip, ctid);
+                load_item = item_j;
+            }
+            tf32_load_rows<ROWS>(P, load_g, chunk_j, lgm, buf);
+        };
+        // One pipeline step: wait for the stage, convert the weights and the
+        // rows held in buf, publish, refill buf with step k+2, and run a due
+        // epilogue.
+        auto step = [&](int k, float (&buf)[ROWS][8]) {
             const int s = k & 1;
             const int item_k = k / P.chunks, chunk = k - item_k * P.chunks;
-            // Next step's rows, in flight while this step converts.
-            RowGeom gn = gm;
-            float xn[kTf32RowsPerThread][8];
-            if (k + 1 < steps) {
-                const int item_n = (k + 1) / P.chunks, chunk_n = (k + 1) - item_n * P.chunks;
-                if (chunk_n == 0) {
-                    int g, n, strip;
-                    tf32_decode(P, first + item_n * stride, g, n, strip);
-                    gn = tf32_rows(P, strip, ctid);
-                }
-                tf32_load_rows(P, first + item_n * stride, chunk_n, gn, xn);
-            }
             // Lane 0 polls; the other lanes wait in the shuffle.
             bool ok = true;
             if (lane == 0) {
@@ -444,41 +475,46 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
                     ok = role_wait(&ab_empty[s], static_cast<uint32_t>(((k - 2) >> 1) & 1), abort_word,
                                    kStatusMmaTimeout);
             }
-            if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
-            // Weights: value v of the B tile set is (tap, half, co, j) with j
-            // fastest, i.e. the canonical layout is contiguous in v.
+            if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
+                failed = true;
+                return;
+            }
+            // Weights: v = ((tap*2 + half)*CPG + co)*4 + j enumerates the chunk's
+            // weights w[co][half*4 + j][tap]; hi goes to A row m_hi(co), lo to
+            // m_hi(co) + HALF, at byte tap*M*32 + half*M*16 + row*16 + j*4.
             {
                 const float *wr = reinterpret_cast<const float *>(wraw0 + s * P.wraw_bytes);
-                uint32_t *const bh = reinterpret_cast<uint32_t *>(bhi0 + s * P.b_bytes);
-                uint32_t *const bl = reinterpret_cast<uint32_t *>(blo0 + s * P.b_bytes);
+                unsigned char *const at = a0 + s * P.a_bytes;
 #pragma unroll
-                for (int q = 0; q < kBPerThread; ++q) {
+                for (int q = 0; q < kWPerThread; ++q) {
                     const int v = ctid + q * kConvThreads;
-                    if (kBVals % kConvThreads == 0 || v < kBVals) {
-                        const int j = v & 3, co = (v >> 2) & (NCO - 1), kt = v / (4 * NCO);
-                        const int kg = kt & 1, tap = kt >> 1;
+                    if (kWVals % kConvThreads == 0 || v < kWVals) {
+                        const int j = v & 3, co = (v >> 2) % CPG, th = (v >> 2) / CPG;
+                        const int half = th & 1, tap = th >> 1;
                         uint32_t hi, lo;
-                        tf32_split(wr[co * 72 + (kg * 4 + j) * 9 + tap], hi, lo);
-                        bh[v] = hi;
-                        bl[v] = lo;
+                        tf32_split(wr[co * 72 + (half * 4 + j) * 9 + tap], hi, lo);
+                        const int row = (co / HALF) * RQ + (co % HALF);
+                        const uint32_t off = tap * M * 32u + half * M * 16u + row * 16u + j * 4u;
+                        *reinterpret_cast<uint32_t *>(at + off) = hi;
+                        *reinterpret_cast<uint32_t *>(at + off + HALF * 16u) = lo;
                     }
                 }
             }
-            // Input rows: A[i] = Xpad[o0 + i] for the 8 channels of this chunk.
+            // Pixel rows: X[i] = Xpad[o0 + i] for the 8 channels of this chunk.
             {
-                unsigned char *const a_hi = ahi0 + s * P.a_bytes, *const a_lo = alo0 + s * P.a_bytes;
+                unsigned char *const x_hi = xhi0 + s * P.b_bytes, *const x_lo = xlo0 + s * P.b_bytes;
 #pragma unroll
-                for (int r = 0; r < kTf32RowsPerThread; ++r) {
+                for (int r = 0; r < ROWS; ++r) {
                     const int i = ctid + r * kConvThreads;
-                    if (i < P.rows_a) {
+                    if (i < P.rows_b) {
                         uint32_t hi[8], lo[8];
 #pragma unroll
-                        for (int ci = 0; ci < 8; ++ci) tf32_split(xv[r][ci], hi[ci], lo[ci]);
+                        for (int ci = 0; ci < 8; ++ci) tf32_split(buf[r][ci], hi[ci], lo[ci]);
                         const uint32_t off = i * 16u;
-                        *reinterpret_cast<uint4 *>(a_hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                        *reinterpret_cast<uint4 *>(a_hi + off + lbo_a) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
-                        *reinterpret_cast<uint4 *>(a_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-                        *reinterpret_cast<uint4 *>(a_lo + off + lbo_a) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
+                        *reinterpret_cast<uint4 *>(x_hi + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                        *reinterpret_cast<uint4 *>(x_hi + off + lbo_x) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
+                        *reinterpret_cast<uint4 *>(x_lo + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                        *reinterpret_cast<uint4 *>(x_lo + off + lbo_x) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
                     }
                 }
             }
@@ -488,43 +524,49 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
                 mbar_arrive(&ab_full[s]);
                 mbar_arrive(&w_empty[s]);
             }
+            load(k + 2, buf);
             // Epilogue of the previous item while this step's MMAs run.
             if (chunk == 0 && pending >= 0) {
                 bool done = true;
                 if (lane == 0)
                     done = role_wait(&acc_full[pending & 1], static_cast<uint32_t>((pending >> 1) & 1), abort_word,
                                      kStatusMmaTimeout);
-                if (!__shfl_sync(0xffffffffu, done ? 1 : 0, 0)) break;
+                if (!__shfl_sync(0xffffffffu, done ? 1 : 0, 0)) {
+                    failed = true;
+                    return;
+                }
                 tc_fence_after();
-                tf32_epilogue<NCO>(P, tmem_base + static_cast<uint32_t>((pending & 1) * P.T * NCO),
-                                   first + pending * stride, warp, lane);
+                tf32_epilogue<M>(P, tmem_base + static_cast<uint32_t>((pending & 1) * kTf32N),
+                                 first + pending * stride, warp, lane, ep);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&acc_empty[pending & 1]);
                 pending = -1;
             }
             if (chunk == P.chunks - 1) pending = item_k;
-            gm = gn;
-#pragma unroll
-            for (int r = 0; r < kTf32RowsPerThread; ++r)
-#pragma unroll
-                for (int ci = 0; ci < 8; ++ci) xv[r][ci] = xn[r][ci];
+        };
+        float xa[ROWS][8], xb[ROWS][8];
+        load(0, xa);
+        load(1, xb);
+        for (int k = 0; k < steps && !failed; k += 2) {
+            step(k, xa);
+            if (k + 1 < steps && !failed) step(k + 1, xb);
         }
-        bool last_ok = pending >= 0;
+        bool last_ok = !failed && pending >= 0;
         if (last_ok && lane == 0)
             last_ok = role_wait(&acc_full[pending & 1], static_cast<uint32_t>((pending >> 1) & 1), abort_word,
                                 kStatusMmaTimeout);
         if (__shfl_sync(0xffffffffu, last_ok ? 1 : 0, 0)) {
             tc_fence_after();
-            tf32_epilogue<NCO>(P, tmem_base + static_cast<uint32_t>((pending & 1) * P.T * NCO),
-                               first + pending * stride, warp, lane);
+            tf32_epilogue<M>(P, tmem_base + static_cast<uint32_t>((pending & 1) * kTf32N),
+                             first + pending * stride, warp, lane, ep);
             tc_fence_before();
         }
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == 0) tmem_dealloc(tmem_base, P.tmem_cols);
+    if (warp == 0) tmem_dealloc(tmem_base, 2 * kTf32N);
 }
 
 }  // namespace gcb

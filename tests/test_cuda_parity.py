@@ -34,10 +34,21 @@ def test_golden_all_implementations(native, torch_cuda, golden_cases):
             assert_matches(c.shape, c.x, c.w, y, c.y32, label=f'{c.name} impl{impl} [{plan}]')
 
 
+def tf32_fits(cpg, w):
+    """A 256-pixel strip plus its 2 * (W + 2) + 2 halo rows must fit the
+    converters' 1024 rows and the shared memory: weights staged twice, A tiles
+    of max(64, 2 cpg) rows twice, four pixel tiles, the epilogue buffers and
+    the barriers."""
+    rows_b = -(-(256 + 2 * (w + 2) + 2) // 8) * 8
+    smem = 2 * cpg * 288 + 2 * 9 * max(64, 2 * cpg) * 32 + 4 * rows_b * 32 + 8 * 16 * 33 * 4 + 128
+    return rows_b <= 1024 and smem <= 227 * 1024
+
+
 def tf32_eligible(s):
-    """One M-tile of 128 pixels plus its 2 * (W + 2) + 2 halo rows must fit the
-    converters' 1024 rows."""
-    return s.b_geometry and s.cpg in (8, 16, 32, 64) and 128 + 2 * (s.w + 2) + 2 <= 1024
+    return s.b_geometry and s.cpg in (8, 16, 32, 64) and tf32_fits(s.cpg, s.w)
+
+
+TF32_WIDEST_CPG16 = max(w for w in range(1, 1024) if tf32_fits(16, w))
 
 
 @pytest.mark.parametrize('kernel', ['general', 'direct_ldg', 'direct_tma', 'tf32x3', 'small'])
@@ -140,13 +151,15 @@ TF32_SHAPES = [
     (1, 64, 112, 112, 16), (2, 64, 33, 44, 64),
     # widths that are not a multiple of 4, tiny planes
     (3, 128, 7, 7, 64), (2, 64, 14, 14, 32), (1, 32, 13, 11, 16), (4, 16, 9, 5, 8), (1, 64, 30, 30, 64),
-    # widest row the converters reach (A rows = 1024), and one tile per image row
-    (1, 16, 6, 445, 16), (2, 8, 3, 300, 8),
+    # widest row that fits, several strips per row
+    (1, 16, 6, TF32_WIDEST_CPG16, 16), (2, 8, 3, 300, 8),
+    # images stacked into one strip: batch not a multiple of the block, 1x1 planes
+    (5, 64, 5, 6, 32), (7, 32, 3, 3, 16), (3, 64, 1, 1, 64), (9, 128, 10, 9, 64),
 ]
 
 
 def test_tf32x3_refuses_rows_beyond_reach(native, torch_cuda):
-    s = Shape(n=1, cin=16, cout=16, h=4, w=446, groups=1)
+    s = Shape(n=1, cin=16, cout=16, h=4, w=TF32_WIDEST_CPG16 + 1, groups=1)
     x, wt = inputs(s, 5)
     with pytest.raises(NativeError) as err:
         run(native, torch_cuda, s, x, wt, kernel='tf32x3')
