@@ -652,11 +652,14 @@ bool tf32_cpg_supported(long long cpg) { return cpg == 8 || cpg == 16 || cpg == 
 // weights staged twice, A tiles of max(64, 2 cpg) rows twice, hi/lo pixel
 // tiles twice, the epilogue buffers and the barrier block.
 constexpr size_t kTf32SmemLimit = 227 * 1024;  // B200 opt-in shared memory per block
-long long tf32_rows_b(long long w) { return round_up(gcb::kTf32N + 2 * (w + 2) + 2, 8); }
-size_t tf32_smem(long long cpg, long long w) {
+long long tf32_rows_b(long long w, int sp) { return round_up(sp * gcb::kTf32N + 2 * (w + 2) + 2, 8); }
+size_t tf32_smem(long long cpg, long long w, int sp) {
     const long long m = std::max(64LL, 2 * cpg);
-    return static_cast<size_t>(2 * cpg * 72 * 4 + 2 * 9 * m * 32 + 4 * tf32_rows_b(w) * 32 +
+    return static_cast<size_t>(2 * cpg * 72 * 4 + 2 * 9 * m * 32 + 4 * tf32_rows_b(w, sp) * 32 +
                                gcb::kConvWarps * gcb::kTf32EpiFloats * 4 + 128);
+}
+bool tf32_fits(long long cpg, long long w, int sp, size_t limit) {
+    return tf32_rows_b(w, sp) <= gcb::kTf32MaxRows && tf32_smem(cpg, w, sp) <= limit;
 }
 
 // Whether the tensor-core path can serve this shape: a supported group width,
@@ -667,8 +670,8 @@ size_t tf32_smem(long long cpg, long long w) {
 bool tf32_eligible(const gc_shape *p, const void *x, const void *w) {
     (void)x;
     const long long cpg = p->cin / p->groups;
-    return tf32_cpg_supported(cpg) && aligned16(w) && tf32_rows_b(p->w) <= gcb::kTf32MaxRows &&
-           tf32_smem(cpg, p->w) <= kTf32SmemLimit && (p->h + 2) * (p->w + 2) < (1LL << 30) &&
+    return tf32_cpg_supported(cpg) && aligned16(w) && tf32_fits(cpg, p->w, 1, kTf32SmemLimit) &&
+           (p->h + 2) * (p->w + 2) < (1LL << 30) &&
            p->n < (1LL << 30) && p->cin < (1LL << 30);
 }
 
@@ -704,30 +707,39 @@ int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
     if (st != GC_OK) return st;
     const long long N = p->n, C = p->cin, H = p->h, W = p->w, cpg = C / p->groups;
     const long long wp = W + 2, hp2 = H + 2;
-    const long long rows_b = tf32_rows_b(W);
-    const size_t smem = tf32_smem(cpg, W);
-    if (rows_b > gcb::kTf32MaxRows || smem > std::min(kTf32SmemLimit, static_cast<size_t>(facts.smem_optin)))
-        return gc_error(GC_UNSUPPORTED, "3xTF32 path: pixel strip does not fit");
-    // Images per block: every item costs the same MMA time (one 256-pixel
-    // strip, all channel chunks), so pick the block that needs the fewest
-    // waves of items over the SMs; ties go to the smaller block.
-    long long best_nb = 1, best_waves = -1, best_items = 0, best_strips = 0;
-    for (long long nb = 1; nb <= N; ++nb) {
-        const long long out_rows = (nb - 1) * hp2 + H;
-        if (nb > 1 && out_rows * wp > 16 * gcb::kTf32N) break;  // stacking only pays for small planes
-        if (nb * hp2 * wp >= (1LL << 30)) break;
-        const long long strips = ceil_div(out_rows * wp, gcb::kTf32N);
-        const long long items = static_cast<long long>(p->groups) * ceil_div(N, nb) * strips;
-        if (items >= (1LL << 31)) continue;
-        const long long waves = ceil_div(items, facts.sms);
-        if (best_waves < 0 || waves < best_waves) {
-            best_waves = waves;
-            best_nb = nb;
-            best_items = items;
-            best_strips = strips;
+    const size_t limit = std::min(kTf32SmemLimit, static_cast<size_t>(facts.smem_optin));
+    if (!tf32_fits(cpg, W, 1, limit)) return gc_error(GC_UNSUPPORTED, "3xTF32 path: pixel strip does not fit");
+    // Images per block and strips per item.  Every 256-pixel strip costs the
+    // same MMA time; two strips per item share the chunk's weights (half the
+    // weight work per pixel, fewer halo rows) but finish an item's MMAs
+    // before its epilogue, so they must not cost more waves than +15 %.  Only
+    // 64-channel groups, whose weight tiles are the largest, gain from it
+    // (measured); narrower groups keep one strip per item.
+    long long best_nb = 1, best_items = 0, best_strips = 0;
+    int best_sp = 1;
+    double best_cost = -1.0;
+    for (int sp = 1; sp <= (cpg == 64 ? 2 : 1); ++sp) {
+        if (!tf32_fits(cpg, W, sp, limit)) continue;
+        for (long long nb = 1; nb <= N; ++nb) {
+            const long long out_rows = (nb - 1) * hp2 + H;
+            if (nb > 1 && out_rows * wp > 16 * gcb::kTf32N) break;  // stacking only pays for small planes
+            if (nb * hp2 * wp >= (1LL << 30)) break;
+            const long long strips = ceil_div(out_rows * wp, sp * gcb::kTf32N);
+            const long long items = static_cast<long long>(p->groups) * ceil_div(N, nb) * strips;
+            if (items >= (1LL << 31)) continue;
+            const double cost = static_cast<double>(ceil_div(items, facts.sms)) * sp * (sp == 2 ? 0.87 : 1.0);
+            if (best_cost < 0.0 || cost < best_cost - 1e-9) {
+                best_cost = cost;
+                best_nb = nb;
+                best_items = items;
+                best_strips = strips;
+                best_sp = sp;
+            }
         }
     }
-    if (best_waves < 0) return gc_error(GC_UNSUPPORTED, "3xTF32 path: too many work items");
+    if (best_cost < 0.0) return gc_error(GC_UNSUPPORTED, "3xTF32 path: too many work items");
+    const long long rows_b = tf32_rows_b(W, best_sp);
+    const size_t smem = tf32_smem(cpg, W, best_sp);
     gcb::Tf32Params P{};
     P.n = static_cast<int>(N);
     P.c = static_cast<int>(C);
@@ -739,6 +751,7 @@ int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
     P.nb = static_cast<int>(best_nb);
     P.blocks = static_cast<int>(ceil_div(N, best_nb));
     P.out_rows = static_cast<int>((best_nb - 1) * hp2 + H);
+    P.sp = best_sp;
     P.strips = static_cast<int>(best_strips);
     P.items = static_cast<int>(best_items);
     P.chunks = static_cast<int>(cpg / 8);
@@ -775,9 +788,9 @@ int launch_tf32(const gc_shape *p, const float *x, const float *w, float *y, int
     if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
     char buf[256];
     std::snprintf(buf, sizeof(buf),
-                  "kernel=tf32x3 engine=tcgen05 n_cta=%d block=320 smem=%zu M=%d N=%d nb=%d strips=%d items=%d "
-                  "chunks=%d rows_b=%d",
-                  plan.grid, plan.smem, plan.P.m, gcb::kTf32N, plan.P.nb, plan.P.strips, plan.P.items,
+                  "kernel=tf32x3 engine=tcgen05 n_cta=%d block=320 smem=%zu M=%d N=%d nb=%d sp=%d strips=%d "
+                  "items=%d chunks=%d rows_b=%d",
+                  plan.grid, plan.smem, plan.P.m, gcb::kTf32N, plan.P.nb, plan.P.sp, plan.P.strips, plan.P.items,
                   plan.P.chunks, plan.P.rows_b);
     g_plan = buf;
     return GC_OK;

@@ -26,7 +26,7 @@
 // second half w_lo of the same channels, so the epilogue adds the two parts
 // with one warp shuffle.
 //
-// Work item = (group, image block, strip of 256 pixels); pipeline step =
+// Work item = (group, image block, strip of sp * 256 pixels); pipeline step =
 // (item, chunk of 8 input channels).  Per step:
 //   - the converter warps load the step's pixels from global memory into
 //     registers (per thread its own pixel rows, 8 coalesced channel loads
@@ -38,12 +38,16 @@
 //     LBO apart, so a shift by one pixel is +16 bytes of descriptor address),
 //     and split the chunk's weights, which one lane of the weight warp stages
 //     by TMA (2-D box of the [C][cpg*9] weight matrix), into the A tiles;
-//   - one lane of the MMA warp issues the 18 MMAs and commits them to the
+//   - one lane of the MMA warp issues the 18 * sp MMAs and commits them to the
 //     mbarrier that frees the stage.
-// The accumulator of item j lives in TMEM columns 256*(j % 2), so the epilogue
-// of item j (tcgen05.ld -> pair sum -> per-warp transpose in shared memory ->
-// coalesced streaming stores, consecutive lanes on consecutive pixels)
-// overlaps the MMAs of item j+1.  Every wait is bounded; on timeout the kernel
+// TMEM holds 512 accumulator columns: with one strip per item, item j uses
+// columns 256*(j % 2) and the epilogue of item j overlaps all MMAs of item
+// j+1; with two strips per item (the chunk's weights then serve 512 pixels)
+// strip s uses columns 256*s, and the MMAs of item j+1 on strip s start as
+// soon as the epilogue of item j has drained strip s.  The epilogue
+// (tcgen05.ld -> pair sum -> per-warp transpose in shared memory -> coalesced
+// streaming stores, consecutive lanes on consecutive pixels) runs on the
+// converter warps between their steps.  Every wait is bounded; on timeout the kernel
 // records it in the status word, drains what it issued, frees its TMEM and
 // returns.  Inputs are assumed finite: for an infinite input the split is
 // undefined and the outputs it reaches come out NaN.
@@ -63,11 +67,13 @@ struct Tf32Params {
     int nb;              // images stacked into one block
     int blocks;          // ceil(n / nb)
     int out_rows;        // padded rows holding the block's outputs: (nb - 1) * (h + 2) + h
-    int strips;          // ceil(out_rows * wp / 256)
+    int sp;              // 256-pixel strips per item: 1 (two accumulator sets alternate between
+                         // items) or 2 (one set holding both strips)
+    int strips;          // items per block: ceil(out_rows * wp / (sp * 256))
     int items;           // groups * blocks * strips
     int chunks;          // cpg / 8
     int m;               // MMA M: max(64, 2 * cpg)
-    int rows_b;          // pixel rows per step: 256 + 2*wp + 2, rounded up to 8 (<= kTf32MaxRows)
+    int rows_b;          // pixel rows per step: sp*256 + 2*wp + 2, rounded up to 8 (<= kTf32MaxRows)
     unsigned a_bytes;    // one step's weight tiles: 9 taps * m * 32
     unsigned b_bytes;    // one pixel tile (hi or lo): rows_b * 32
     unsigned wraw_bytes; // one staged weight chunk: cpg * 72 * 4
@@ -242,7 +248,7 @@ template <int ROWS>
 __device__ __forceinline__ RowGeom<ROWS> tf32_rows(const Tf32Params &P, int blk, int strip, int ctid) {
     RowGeom<ROWS> gm;
     gm.valid = 0;
-    const int o0 = strip * kTf32N;
+    const int o0 = strip * P.sp * kTf32N;
     const int hp2 = P.h + 2;
     const long long image_floats = static_cast<long long>(P.c) * P.h * P.wd;
 #pragma unroll
@@ -274,7 +280,8 @@ __device__ __forceinline__ void tf32_load_rows(const Tf32Params &P, int g, int c
     }
 }
 
-// Converter warps: epilogue of one item.  Warp w reads lane quadrant w % 4
+// Converter warps: epilogue of strip `sub` of one item (256 accumulator
+// columns at acc).  Warp w reads lane quadrant w % 4
 // and pixel columns [128*(w/4), 128*(w/4) + 128) in chunks of 32.  In the
 // quadrant, lane l (l < HALF) holds the w_hi rows and lane l + HALF the w_lo
 // rows of the same output channel: one shuffle adds them (lane l keeps
@@ -282,8 +289,8 @@ __device__ __forceinline__ void tf32_load_rows(const Tf32Params &P, int g, int c
 // the warp's transpose buffer, so that the stores run with consecutive lanes
 // on consecutive pixels of one output channel.
 template <int M>
-__device__ __forceinline__ void tf32_epilogue(const Tf32Params &P, uint32_t acc, int item, int warp, int lane,
-                                              float *ep) {
+__device__ __forceinline__ void tf32_epilogue(const Tf32Params &P, uint32_t acc, int item, int sub, int warp,
+                                              int lane, float *ep) {
     constexpr int HALF = M / 8;  // output channels per lane quadrant
     int g, blk, strip;
     tf32_decode(P, item, g, blk, strip);
@@ -311,7 +318,7 @@ __device__ __forceinline__ void tf32_epilogue(const Tf32Params &P, uint32_t acc,
         }
         __syncwarp();
         // lane -> pixel o of the chunk
-        const int o = strip * kTf32N + col0 + lane;
+        const int o = (strip * P.sp + sub) * kTf32N + col0 + lane;
         const int vrow = o / P.wp, col = o - vrow * P.wp;
         const int k = vrow / hp2, hh = vrow - k * hp2;
         const int img = blk * P.nb + k;
@@ -405,12 +412,6 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
                 const int item_k = k / P.chunks, chunk = k - item_k * P.chunks;
                 if (!role_wait(&ab_full[s], static_cast<uint32_t>((k >> 1) & 1), abort_word, kStatusMmaTimeout))
                     break;
-                if (chunk == 0 && item_k >= 2 &&
-                    !role_wait(&acc_empty[item_k & 1], static_cast<uint32_t>(((item_k - 2) >> 1) & 1), abort_word,
-                               kStatusMmaTimeout))
-                    break;
-                tc_fence_after();
-                const uint32_t d = tmem_base + static_cast<uint32_t>((item_k & 1) * kTf32N);
                 // Descriptors of the stage's tiles; a shift of the start
                 // address is an add on the descriptor's low field (16-byte
                 // units; every offset stays inside shared memory, so no carry
@@ -419,19 +420,35 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
                 const uint64_t dxh0 = umma_desc(smem_addr(xhi0 + s * P.b_bytes), P.rows_b * 16u, 128);
                 const uint64_t dxl0 = umma_desc(smem_addr(xlo0 + s * P.b_bytes), P.rows_b * 16u, 128);
                 const uint32_t wp = static_cast<uint32_t>(P.wp);
+                bool ok = true;
+                for (int sub = 0; sub < P.sp && ok; ++sub) {
+                    // accumulator set of (item, strip) and the use count of that set
+                    const int buf = P.sp == 1 ? (item_k & 1) : sub;
+                    const int use = P.sp == 1 ? (item_k >> 1) : item_k;
+                    if (chunk == 0 && use >= 1 &&
+                        !role_wait(&acc_empty[buf], static_cast<uint32_t>((use - 1) & 1), abort_word,
+                                   kStatusMmaTimeout)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d = tmem_base + static_cast<uint32_t>(buf * kTf32N);
+                    const uint64_t xs = static_cast<uint64_t>(sub) * kTf32N;  // strip's first pixel row
 #pragma unroll
-                for (int tap = 0; tap < 9; ++tap) {
-                    const uint32_t r = tap / 3, sx = tap % 3;
-                    const uint64_t aoff = static_cast<uint64_t>(tap) * M * 2u;  // M rows of 32 bytes
-                    const uint64_t xoff = r * wp + sx;                          // pixel rows of 16 bytes
-                    if (tap == 0)
-                        umma_tf32(d, da0 + aoff, dxh0 + xoff, kIdesc, chunk != 0);
-                    else
-                        umma_tf32(d, da0 + aoff, dxh0 + xoff, kIdesc, true);
-                    umma_tf32(d, da0 + aoff, dxl0 + xoff, kIdesc, true);
+                    for (int tap = 0; tap < 9; ++tap) {
+                        const uint32_t r = tap / 3, sx = tap % 3;
+                        const uint64_t aoff = static_cast<uint64_t>(tap) * M * 2u;  // M rows of 32 bytes
+                        const uint64_t xoff = xs + r * wp + sx;                     // pixel rows of 16 bytes
+                        if (tap == 0)
+                            umma_tf32(d, da0 + aoff, dxh0 + xoff, kIdesc, chunk != 0);
+                        else
+                            umma_tf32(d, da0 + aoff, dxh0 + xoff, kIdesc, true);
+                        umma_tf32(d, da0 + aoff, dxl0 + xoff, kIdesc, true);
+                    }
                 }
+                if (!ok) break;
                 umma_commit(&ab_empty[s]);
-                if (chunk == P.chunks - 1) umma_commit(&acc_full[item_k & 1]);
+                if (chunk == P.chunks - 1) umma_commit(&acc_full[P.sp == 1 ? (item_k & 1) : 0]);
                 committed = k;
             }
             if (committed >= 0)
@@ -447,6 +464,26 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
         float *const ep = ep0 + warp * kTf32EpiFloats;
         int pending = -1;  // per-CTA item index whose epilogue is due
         bool failed = false;
+        // Epilogue of item `it`: wait for its last MMAs, then drain strip by
+        // strip, releasing each strip's accumulator set as soon as it is read.
+        auto drain = [&](int it) -> bool {
+            const int fbuf = P.sp == 1 ? (it & 1) : 0;
+            const int fuse = P.sp == 1 ? (it >> 1) : it;
+            bool done = true;
+            if (lane == 0)
+                done = role_wait(&acc_full[fbuf], static_cast<uint32_t>(fuse & 1), abort_word, kStatusMmaTimeout);
+            if (!__shfl_sync(0xffffffffu, done ? 1 : 0, 0)) return false;
+            tc_fence_after();
+            for (int sub = 0; sub < P.sp; ++sub) {
+                const int buf = P.sp == 1 ? (it & 1) : sub;
+                tf32_epilogue<M>(P, tmem_base + static_cast<uint32_t>(buf * kTf32N), first + it * stride, sub, warp,
+                                 lane, ep);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&acc_empty[buf]);
+            }
+            return true;
+        };
         // Load side: the item whose row geometry is cached.
         int load_item = -1, load_g = 0;
         RowGeom<ROWS> lgm{};
@@ -527,20 +564,10 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
             load(k + 2, buf);
             // Epilogue of the previous item while this step's MMAs run.
             if (chunk == 0 && pending >= 0) {
-                bool done = true;
-                if (lane == 0)
-                    done = role_wait(&acc_full[pending & 1], static_cast<uint32_t>((pending >> 1) & 1), abort_word,
-                                     kStatusMmaTimeout);
-                if (!__shfl_sync(0xffffffffu, done ? 1 : 0, 0)) {
+                if (!drain(pending)) {
                     failed = true;
                     return;
                 }
-                tc_fence_after();
-                tf32_epilogue<M>(P, tmem_base + static_cast<uint32_t>((pending & 1) * kTf32N),
-                                 first + pending * stride, warp, lane, ep);
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&acc_empty[pending & 1]);
                 pending = -1;
             }
             if (chunk == P.chunks - 1) pending = item_k;
@@ -552,16 +579,7 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
             step(k, xa);
             if (k + 1 < steps && !failed) step(k + 1, xb);
         }
-        bool last_ok = !failed && pending >= 0;
-        if (last_ok && lane == 0)
-            last_ok = role_wait(&acc_full[pending & 1], static_cast<uint32_t>((pending >> 1) & 1), abort_word,
-                                kStatusMmaTimeout);
-        if (__shfl_sync(0xffffffffu, last_ok ? 1 : 0, 0)) {
-            tc_fence_after();
-            tf32_epilogue<M>(P, tmem_base + static_cast<uint32_t>((pending & 1) * kTf32N),
-                             first + pending * stride, warp, lane, ep);
-            tc_fence_before();
-        }
+        if (!failed && pending >= 0) drain(pending);
     }
     tc_fence_before();
     __syncthreads();
