@@ -713,14 +713,16 @@ int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
     // same MMA time; two strips per item share the chunk's weights (half the
     // weight work per pixel, fewer halo rows) but finish an item's MMAs
     // before its epilogue, so they must not cost more waves than +15 %.  Only
-    // 64-channel groups, whose weight tiles are the largest, gain from it
-    // (measured); narrower groups keep one strip per item.
+    // 64-channel groups of large planes (one image per block), whose weight
+    // tiles are the largest, gain from it (measured); narrower groups and
+    // stacked small images keep one strip per item.
     long long best_nb = 1, best_items = 0, best_strips = 0;
     int best_sp = 1;
     double best_cost = -1.0;
     for (int sp = 1; sp <= (cpg == 64 ? 2 : 1); ++sp) {
         if (!tf32_fits(cpg, W, sp, limit)) continue;
         for (long long nb = 1; nb <= N; ++nb) {
+            if (sp == 2 && nb > 1) break;
             const long long out_rows = (nb - 1) * hp2 + H;
             if (nb > 1 && out_rows * wp > 16 * gcb::kTf32N) break;  // stacking only pays for small planes
             if (nb * hp2 * wp >= (1LL << 30)) break;
