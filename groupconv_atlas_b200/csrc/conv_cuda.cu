@@ -823,16 +823,19 @@ int launch_small(const gc_shape *p, const float *x, const float *w, float *y, in
     if (st != GC_OK) return st;
     const long long N = p->n, C = p->cin, cpg = C / p->groups, hw = p->h * p->w;
     const int cob = cpg % 8 == 0 ? 8 : cpg % 4 == 0 ? 4 : cpg % 2 == 0 ? 2 : 1;
+    // Channels per item: the largest block that still leaves every CTA about
+    // two items (at ~3 resident CTAs per SM), so the double-buffered copies
+    // of the next item hide the load latency; else the smallest block.
     long long best_cb = 0;
     for (long long gpi = 1; gpi <= p->groups; ++gpi) {
         if (p->groups % gpi) continue;
         const long long cb = gpi * cpg;
-        const long long smem = (round_up(cb * hw, 4) + cb * cpg * 9) * 4;
-        if (smem > 48 * 1024 && best_cb != 0) break;
+        const long long smem = (round_up(cb * hw, 4) + round_up(cb * cpg * 9, 4)) * 4;  // one stage
+        if (2 * smem > 48 * 1024 && best_cb != 0) break;
         if (smem > facts.smem_optin) break;
         const long long items = N * (C / cb);
-        if (best_cb == 0 || items >= 2LL * facts.sms) best_cb = cb;
-        if (items < 2LL * facts.sms) break;
+        if (best_cb == 0 || items >= 6LL * facts.sms) best_cb = cb;
+        if (items < 6LL * facts.sms) break;
     }
     if (best_cb == 0) return gc_error(GC_UNSUPPORTED, "small-image kernel: one group does not fit in shared memory");
     gcb::SmallParams P{};
@@ -852,8 +855,14 @@ int launch_small(const gc_shape *p, const float *x, const float *w, float *y, in
     P.hw = static_cast<int>(hw);
     P.hwp = static_cast<int>(round_up(hw, 32));
     P.x_floats = static_cast<int>(round_up(best_cb * hw, 4));
+    P.w_floats = static_cast<int>(round_up(best_cb * cpg * 9, 4));
     P.vec = (aligned16(x) && (C * hw) % 4 == 0 && (best_cb * hw) % 4 == 0) ? 1 : 0;
-    const size_t smem = static_cast<size_t>((P.x_floats + best_cb * cpg * 9) * 4);
+    // Ring depth: up to 4 stages within 48 KB (more bytes in flight per CTA),
+    // at least one stage.
+    const size_t stage_bytes = static_cast<size_t>(P.x_floats + P.w_floats) * 4;
+    P.stages = static_cast<int>(std::max<size_t>(1, std::min<size_t>(4, 48 * 1024 / stage_bytes)));
+    while (P.stages > 1 && P.stages * stage_bytes > static_cast<size_t>(facts.smem_optin)) --P.stages;
+    const size_t smem = P.stages * stage_bytes;
     // pixel slots per CTA: up to 256 threads, never more slots than channel blocks
     const long long slots = std::max<long long>(1, std::min<long long>(256 / P.hwp, best_cb / cob));
     const int threads = static_cast<int>(slots * P.hwp);
@@ -867,8 +876,9 @@ int launch_small(const gc_shape *p, const float *x, const float *w, float *y, in
     cudaError_t e = launch_pdl(fn, dim3(grid), dim3(threads), args, smem, stream);
     if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
     char buf[200];
-    std::snprintf(buf, sizeof(buf), "kernel=small grid=%d block=%d smem=%zu ctas_per_sm=%d cob=%d cb=%d items=%d vec=%d",
-                  grid, threads, smem, ctas, cob, P.cb, P.items, P.vec);
+    std::snprintf(buf, sizeof(buf),
+                  "kernel=small grid=%d block=%d smem=%zu ctas_per_sm=%d cob=%d cb=%d items=%d vec=%d stages=%d", grid,
+                  threads, smem, ctas, cob, P.cb, P.items, P.vec, P.stages);
     g_plan = buf;
     return GC_OK;
 }

@@ -141,6 +141,10 @@ __device__ __forceinline__ void cp_async_4(void *dst, const void *src, bool vali
                  "r"(valid ? 4 : 0)
                  : "memory");
 }
+// 16-byte asynchronous copy global -> shared (both addresses 16-byte aligned).
+__device__ __forceinline__ void cp_async_16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() {
     asm volatile("cp.async.commit_group;" ::: "memory");
 }
