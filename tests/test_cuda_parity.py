@@ -155,6 +155,8 @@ TF32_SHAPES = [
     (1, 16, 6, TF32_WIDEST_CPG16, 16), (2, 8, 3, 300, 8),
     # images stacked into one strip: batch not a multiple of the block, 1x1 planes
     (5, 64, 5, 6, 32), (7, 32, 3, 3, 16), (3, 64, 1, 1, 64), (9, 128, 10, 9, 64),
+    # many groups: every CTA crosses group boundaries
+    (3, 512, 9, 10, 16), (2, 512, 12, 12, 32), (1, 256, 20, 30, 8),
 ]
 
 
