@@ -699,8 +699,9 @@ const void *tf32_kernel_for(long long cpg, long long rows_b) {
     }
 }
 
-// Largest strip of M-tiles whose double-buffered stages fit in shared memory
-// and whose two accumulators fit in the 512 TMEM columns.
+// Work split of the tensor-core path: images stacked per block, 256-pixel
+// strips per item (one, or two for 64-channel groups of large planes), items
+// in waves over the SMs.
 int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
     DeviceFacts facts;
     int st = device_facts(dev, facts);
