@@ -468,64 +468,73 @@ def end_to_end(args, native, shape, units, xh, wh, torch, api, shard):
     """Same metric, through the C ABI with host buffers: per step the batch is
     copied host->device in chunks (pinned), convolved chunk by chunk as soon
     as its copy lands, and copied back; three streams overlap the two copy
-    directions with compute."""
+    directions with compute, and two device buffer sets alternate between
+    steps, so the copies of step k+1 never wait for the convolutions of
+    step k."""
     import dataclasses
     n = shape.n
     chunks = max(1, min(8, n))
     bounds = [(i * n // chunks, (i + 1) * n // chunks) for i in range(chunks)]
     bounds = [b for b in bounds if b[1] > b[0]]
-    dx = torch.empty(shape.input, device='cuda')
-    dw = torch.empty(shape.weight, device='cuda')
-    dy = torch.empty(shape.output, device='cuda')
+    dws = [torch.empty(shape.weight, device='cuda') for _ in range(2)]
+    dxs = [torch.empty(shape.input, device='cuda') for _ in range(2)]
+    dys = [torch.empty(shape.output, device='cuda') for _ in range(2)]
     yh = torch.empty(shape.output, pin_memory=True)
     s_in, s_cmp, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
-    calls = []
-    for lo, hi in bounds:
-        sub = dataclasses.replace(shape, n=hi - lo)
-        calls.append(Call(native, sub, dx[lo:hi], dw, dy[lo:hi], s_cmp.cuda_stream))
-    ev_in = [torch.cuda.Event() for _ in bounds]
-    ev_cmp = [torch.cuda.Event() for _ in bounds]
-    ev_out = [torch.cuda.Event() for _ in bounds]
+    calls = [[Call(native, dataclasses.replace(shape, n=hi - lo), dxs[b][lo:hi], dws[b], dys[b][lo:hi],
+                   s_cmp.cuda_stream) for lo, hi in bounds] for b in range(2)]
+    ev_in = [[torch.cuda.Event() for _ in bounds] for _ in range(2)]
+    ev_cmp = [[torch.cuda.Event() for _ in bounds] for _ in range(2)]
+    ev_out = [[torch.cuda.Event() for _ in bounds] for _ in range(2)]
+    used = [False, False]
 
-    def step(first):
+    def step(k):
+        b = k & 1
+        dx, dy = dxs[b], dys[b]
         with torch.cuda.stream(s_in):
-            dw.copy_(wh, non_blocking=True)
+            if used[b]:
+                s_in.wait_event(ev_cmp[b][-1])  # step k-2 finished reading these weights
+            dws[b].copy_(wh, non_blocking=True)
             for j, (lo, hi) in enumerate(bounds):
-                if not first:
-                    s_in.wait_event(ev_cmp[j])  # previous step finished reading dx chunk
+                if used[b]:
+                    s_in.wait_event(ev_cmp[b][j])  # step k-2 finished reading this dx chunk
                 dx[lo:hi].copy_(xh[lo:hi], non_blocking=True)
-                ev_in[j].record(s_in)
+                ev_in[b][j].record(s_in)
         for j in range(len(bounds)):
-            s_cmp.wait_event(ev_in[j])
-            if not first:
-                s_cmp.wait_event(ev_out[j])  # previous step finished reading dy chunk
-            calls[j]()
-            ev_cmp[j].record(s_cmp)
+            s_cmp.wait_event(ev_in[b][j])
+            if used[b]:
+                s_cmp.wait_event(ev_out[b][j])  # step k-2 finished reading this dy chunk
+            calls[b][j]()
+            ev_cmp[b][j].record(s_cmp)
         with torch.cuda.stream(s_out):
             for j, (lo, hi) in enumerate(bounds):
-                s_out.wait_event(ev_cmp[j])
+                s_out.wait_event(ev_cmp[b][j])
                 yh[lo:hi].copy_(dy[lo:hi], non_blocking=True)
-                ev_out[j].record(s_out)
+                ev_out[b][j].record(s_out)
+        used[b] = True
 
     for i in range(3):
-        step(i == 0)
+        step(i)
     torch.cuda.synchronize()
     barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t0.record(s_in)
-    for _ in range(args.e2e_steps):
-        step(False)
+    for i in range(args.e2e_steps):
+        step(3 + i)
     t1.record(s_out)
     torch.cuda.synchronize()
     barrier()
     ms = shard.max_over_ranks(t0.elapsed_time(t1))
+    # the host result of the last step equals that step's device output
+    consistent = bool(torch.equal(yh, dys[(2 + args.e2e_steps) & 1].cpu()))
     step_bytes = 4 * (math.prod(shape.input) + math.prod(shape.weight) + math.prod(shape.output))
     job_bytes = shard.sum_over_ranks(step_bytes)
     return {'value': job_bytes * args.e2e_steps / (ms / 1e3) / 1e9, 'unit': UNIT,
             'h2d_bytes_per_step': 4 * (math.prod(shape.input) + math.prod(shape.weight)),
             'd2h_bytes_per_step': 4 * math.prod(shape.output), 'steps': args.e2e_steps,
             'ms_per_step': ms / args.e2e_steps, 'chunks': len(bounds),
-            'path': 'pinned host -> gc_cuda_conv per chunk (C ABI via ctypes) -> pinned host'}
+            'path': 'pinned host -> gc_cuda_conv per chunk (C ABI via ctypes) -> pinned host',
+            'host_matches_device': consistent}
 
 
 def graph_step_ms(torch, stream, step, count, replays=3):
