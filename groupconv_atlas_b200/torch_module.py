@@ -35,6 +35,11 @@ class B200Conv2d(torch.nn.Module):
                              ph=conv.padding[0], pw=conv.padding[1], dh=conv.dilation[0], dw=conv.dilation[1])
         self._cache = {}
         self._fn = self.native.lib.gc_cuda_conv
+        # raw handle of the current stream; the public accessor builds a
+        # Stream object per call, which costs more than the launch itself
+        raw = getattr(torch._C, '_cuda_getCurrentRawStream', None)
+        self._stream = (lambda dev: raw(dev)) if raw is not None else \
+            (lambda dev: torch.cuda.current_stream(dev).cuda_stream)
 
     def _descriptors(self, x: torch.Tensor):
         key = (tuple(x.shape), x.device.index)
@@ -54,7 +59,7 @@ class B200Conv2d(torch.nn.Module):
         xd.data = x.data_ptr()
         wd.data = self.weight.data_ptr()
         yd.data = y.data_ptr()
-        stream = torch.cuda.current_stream(x.device).cuda_stream
+        stream = self._stream(x.device.index)
         status = self._fn(ct.byref(p), ct.byref(xd), ct.byref(wd), ct.byref(yd), self.implementation,
                           ct.c_void_p(stream))
         if status:
