@@ -887,6 +887,12 @@ int launch_small(const gc_shape *p, const float *x, const float *w, float *y, in
 // ---- general kernel ------------------------------------------------------------------
 constexpr int kGeneralRun = 4;
 
+template <int COB>
+const void *general_kernel_for(bool narrow) {
+    return narrow ? reinterpret_cast<const void *>(&gcb::general_conv_kernel<kGeneralRun, COB, int>)
+                  : reinterpret_cast<const void *>(&gcb::general_conv_kernel<kGeneralRun, COB, long long>);
+}
+
 int launch_general(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const float *w,
                    float *y, int dev, cudaStream_t stream) {
     DeviceFacts facts;
@@ -912,18 +918,33 @@ int launch_general(const gc_shape *p, int64_t ho, int64_t wo, const float *x, co
     P.dw = p->dw;
     P.ho = ho;
     P.wo = wo;
+    // output channels per thread: the largest of 8, 4, 2, 1 dividing the
+    // output channels per group
+    const long long opg = p->cout / p->groups;
+    const int cob = opg % 8 == 0 ? 8 : opg % 4 == 0 ? 4 : opg % 2 == 0 ? 2 : 1;
     P.runs_per_row = ceil_div(wo, kGeneralRun);
-    P.total_runs = p->n * p->cout * ho * P.runs_per_row;
+    P.total_runs = p->n * (p->cout / cob) * ho * P.runs_per_row;
+    // 32-bit indices when every element index (and the run count, and the
+    // worst intermediate of the input index) stays below 2^31
+    const long long lim = 1LL << 31;
+    const long long runs_padded = P.total_runs + static_cast<long long>(facts.sms) * 8 * 256;
+    const bool narrow = p->n * p->cin * p->h * p->w < lim && p->n * p->cout * ho * wo + kGeneralRun < lim &&
+                        p->cout * (p->cin / p->groups) * p->r * p->s < lim && runs_padded < lim &&
+                        p->h + 2 * p->ph + 2 * p->sh + p->r * p->dh < lim &&
+                        p->w + 2 * p->pw + (kGeneralRun + 2) * p->sw + p->s * p->dw < lim;
     const int threads = 256;
     const long long blocks = std::min<long long>(ceil_div(P.total_runs, threads),
                                                  static_cast<long long>(facts.sms) * 8);
+    const void *fn = cob == 8 ? general_kernel_for<8>(narrow)
+                   : cob == 4 ? general_kernel_for<4>(narrow)
+                   : cob == 2 ? general_kernel_for<2>(narrow)
+                              : general_kernel_for<1>(narrow);
     void *args[] = {&P};
-    cudaError_t e = launch_pdl(reinterpret_cast<const void *>(&gcb::general_conv_kernel<kGeneralRun>),
-                               dim3(static_cast<unsigned>(blocks)), dim3(threads), args, 0, stream);
+    cudaError_t e = launch_pdl(fn, dim3(static_cast<unsigned>(blocks)), dim3(threads), args, 0, stream);
     if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
     char buf[160];
-    std::snprintf(buf, sizeof(buf), "kernel=general grid=%lld block=%d run=%d runs=%lld", blocks,
-                  threads, kGeneralRun, P.total_runs);
+    std::snprintf(buf, sizeof(buf), "kernel=general grid=%lld block=%d run=%d cob=%d index=%s runs=%lld", blocks,
+                  threads, kGeneralRun, cob, narrow ? "32" : "64", P.total_runs);
     g_plan = buf;
     return GC_OK;
 }

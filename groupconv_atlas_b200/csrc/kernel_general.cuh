@@ -1,10 +1,15 @@
 // General grouped 2-D cross-correlation (implementation 0): any kernel size,
 // stride, padding, dilation and any Cin/Cout divisible by groups.  It serves
 // the geometries outside the 3x3/s1/p1 engine (strided and dilated layers,
-// depthwise multipliers), so it trades peak speed for generality: a thread
-// owns a run of RUN consecutive output columns of one output row, keeps one
-// accumulator per column, and reuses each weight across the run.  Grid-stride
-// over runs with 64-bit indices; the grid is sized from the SM count.
+// Cin != Cout, depthwise multipliers), so it trades peak speed for
+// generality: a thread owns a run of RUN consecutive output columns of one
+// output row for COB consecutive output channels of one group (COB divides
+// the output channels per group), keeps COB x RUN accumulators, and reuses
+// each input value across the COB channels and each weight across the run.
+// Consecutive threads take consecutive runs of a row, so input loads are
+// coalesced (at the layer's stride) and the threads of a warp share weights
+// (L1 broadcast).  Grid-stride over runs; index arithmetic in 32 bits when
+// every tensor has fewer than 2^31 elements, else 64 bits.
 #pragma once
 #include <cstdint>
 
@@ -19,49 +24,68 @@ struct GeneralParams {
     long long n, cin, cout, h, w, r, s, groups, sh, sw, ph, pw, dh, dw;
     long long ho, wo;
     long long runs_per_row;  // ceil(wo / RUN)
-    long long total_runs;    // n * cout * ho * runs_per_row
+    long long total_runs;    // n * (cout / COB) * ho * runs_per_row
 };
 
-template <int RUN>
+template <int RUN, int COB, typename I>
 __global__ void __launch_bounds__(256) general_conv_kernel(const __grid_constant__ GeneralParams P) {
     griddep_wait();
     griddep_launch_dependents();
-    const long long cpg = P.cin / P.groups;
-    const long long opg = P.cout / P.groups;
-    for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-         idx < P.total_runs; idx += static_cast<long long>(gridDim.x) * blockDim.x) {
-        long long t = idx;
-        const long long ow0 = (t % P.runs_per_row) * RUN;
-        t /= P.runs_per_row;
-        const long long oh = t % P.ho;
-        t /= P.ho;
-        const long long co = t % P.cout;
-        const long long n = t / P.cout;
-        const long long ci0 = (co / opg) * cpg;
-        float acc[RUN];
+    const I cpg = static_cast<I>(P.cin / P.groups);
+    const I opg = static_cast<I>(P.cout / P.groups);
+    const I R = static_cast<I>(P.r), S = static_cast<I>(P.s);
+    const I H = static_cast<I>(P.h), W = static_cast<I>(P.w), HO = static_cast<I>(P.ho), WO = static_cast<I>(P.wo);
+    const I sh = static_cast<I>(P.sh), sw = static_cast<I>(P.sw), ph = static_cast<I>(P.ph), pw = static_cast<I>(P.pw);
+    const I dh = static_cast<I>(P.dh), dw = static_cast<I>(P.dw);
+    const I rpr = static_cast<I>(P.runs_per_row), cobs = static_cast<I>(P.cout / COB);
+    const I total = static_cast<I>(P.total_runs);
+    const I wsize = cpg * R * S;  // weights per output channel
+    for (I idx = static_cast<I>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+         idx += static_cast<I>(gridDim.x) * blockDim.x) {
+        I t = idx;
+        const I ow0 = (t % rpr) * RUN;
+        t /= rpr;
+        const I oh = t % HO;
+        t /= HO;
+        const I co0 = (t % cobs) * COB;
+        const I n = t / cobs;
+        const I ci0 = (co0 / opg) * cpg;
+        float acc[COB][RUN];
 #pragma unroll
-        for (int j = 0; j < RUN; ++j) acc[j] = 0.0f;
-        const float *wco = P.wp + co * cpg * P.r * P.s;
-        for (long long ci = 0; ci < cpg; ++ci) {
-            const float *plane = P.xp + ((n * P.cin + ci0 + ci) * P.h) * P.w;
-            for (long long r = 0; r < P.r; ++r) {
-                const long long ih = oh * P.sh - P.ph + r * P.dh;
-                if (ih < 0 || ih >= P.h) continue;
-                const float *row = plane + ih * P.w;
-                for (long long s = 0; s < P.s; ++s) {
-                    const float wv = __ldg(wco + (ci * P.r + r) * P.s + s);
+        for (int c = 0; c < COB; ++c)
+#pragma unroll
+            for (int j = 0; j < RUN; ++j) acc[c][j] = 0.0f;
+        const float *wco = P.wp + co0 * wsize;
+        const I iw0 = ow0 * sw - pw;
+        for (I ci = 0; ci < cpg; ++ci) {
+            const float *plane = P.xp + ((n * static_cast<I>(P.cin) + ci0 + ci) * H) * W;
+            const float *wci = wco + ci * R * S;
+            for (I r = 0; r < R; ++r) {
+                const I ih = oh * sh - ph + r * dh;
+                if (ih < 0 || ih >= H) continue;
+                const float *row = plane + ih * W;
+                for (I s = 0; s < S; ++s) {
+                    float xv[RUN];
 #pragma unroll
                     for (int j = 0; j < RUN; ++j) {
-                        const long long iw = (ow0 + j) * P.sw - P.pw + s * P.dw;
-                        if (iw >= 0 && iw < P.w) acc[j] = fmaf(__ldg(row + iw), wv, acc[j]);
+                        const I iw = iw0 + j * sw + s * dw;
+                        xv[j] = (iw >= 0 && iw < W) ? __ldg(row + iw) : 0.0f;
+                    }
+#pragma unroll
+                    for (int c = 0; c < COB; ++c) {
+                        const float wv = __ldg(wci + c * wsize + r * S + s);
+#pragma unroll
+                        for (int j = 0; j < RUN; ++j) acc[c][j] = fmaf(xv[j], wv, acc[c][j]);
                     }
                 }
             }
         }
-        float *out = P.yp + ((n * P.cout + co) * P.ho + oh) * P.wo + ow0;
+        float *out = P.yp + ((n * static_cast<I>(P.cout) + co0) * HO + oh) * WO + ow0;
 #pragma unroll
-        for (int j = 0; j < RUN; ++j)
-            if (ow0 + j < P.wo) out[j] = acc[j];
+        for (int c = 0; c < COB; ++c)
+#pragma unroll
+            for (int j = 0; j < RUN; ++j)
+                if (ow0 + j < WO) out[c * HO * WO + j] = acc[c][j];
     }
 }
 
