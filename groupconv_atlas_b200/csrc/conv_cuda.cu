@@ -646,7 +646,16 @@ int launch_direct(const gc_shape *p, const float *x, const float *w, float *y, b
 }
 
 // ---- tcgen05 3xTF32 implicit GEMM ------------------------------------------------------
-bool tf32_cpg_supported(long long cpg) { return cpg == 8 || cpg == 16 || cpg == 32 || cpg == 64; }
+// Output channels per tensor-path item (the kernel's CO): the widest
+// multiple of 8 up to 64 dividing the group (the whole group up to 64
+// channels; blocks of wider groups and of dense layers).  0: not served
+// (groups that are not a multiple of 8 channels).
+long long tf32_co(long long cpg) {
+    for (long long co = 64; co >= 8; co -= 8)
+        if (cpg % co == 0) return co;
+    return 0;
+}
+bool tf32_cpg_supported(long long cpg) { return tf32_co(cpg) != 0; }
 
 // Pixel rows per step and shared memory of the tensor-core path for a shape:
 // weights staged twice, A tiles of max(64, 2 cpg) rows twice, hi/lo pixel
@@ -654,8 +663,9 @@ bool tf32_cpg_supported(long long cpg) { return cpg == 8 || cpg == 16 || cpg == 
 constexpr size_t kTf32SmemLimit = 227 * 1024;  // B200 opt-in shared memory per block
 long long tf32_rows_b(long long w, int sp) { return round_up(sp * gcb::kTf32N + 2 * (w + 2) + 2, 8); }
 size_t tf32_smem(long long cpg, long long w, int sp) {
-    const long long m = std::max(64LL, 2 * cpg);
-    return static_cast<size_t>(2 * cpg * 72 * 4 + 2 * 9 * m * 32 + 4 * tf32_rows_b(w, sp) * 32 +
+    const long long co = tf32_co(cpg);
+    const long long m = 2 * co > 64 ? 128 : 64;
+    return static_cast<size_t>(2 * co * 72 * 4 + 2 * 9 * m * 32 + 4 * tf32_rows_b(w, sp) * 32 +
                                gcb::kConvWarps * gcb::kTf32EpiFloats * 4 + 128);
 }
 bool tf32_fits(long long cpg, long long w, int sp, size_t limit) {
@@ -682,19 +692,24 @@ struct Tf32Plan {
     int grid = 0;
 };
 
-// Kernel instance for a group width and the pixel rows per step (two or
-// four rows per converter thread).
-const void *tf32_kernel_for(long long cpg, long long rows_b) {
+// Kernel instance for an output-channel block width and the pixel rows per
+// step (two or four rows per converter thread).
+template <int CO>
+const void *tf32_instance(bool two) {
+    return two ? reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<CO, 2>)
+               : reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<CO, 4>);
+}
+const void *tf32_kernel_for(long long co, long long rows_b) {
     const bool two = rows_b <= 2 * gcb::kConvThreads;
-    switch (cpg) {
-    case 8: return two ? reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<8, 2>)
-                       : reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<8, 4>);
-    case 16: return two ? reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<16, 2>)
-                        : reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<16, 4>);
-    case 32: return two ? reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<32, 2>)
-                        : reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<32, 4>);
-    case 64: return two ? reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<64, 2>)
-                        : reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<64, 4>);
+    switch (co) {
+    case 8: return tf32_instance<8>(two);
+    case 16: return tf32_instance<16>(two);
+    case 24: return tf32_instance<24>(two);
+    case 32: return tf32_instance<32>(two);
+    case 40: return tf32_instance<40>(two);
+    case 48: return tf32_instance<48>(two);
+    case 56: return tf32_instance<56>(two);
+    case 64: return tf32_instance<64>(two);
     default: return nullptr;
     }
 }
@@ -707,6 +722,7 @@ int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
     int st = device_facts(dev, facts);
     if (st != GC_OK) return st;
     const long long N = p->n, C = p->cin, H = p->h, W = p->w, cpg = C / p->groups;
+    const long long co = tf32_co(cpg), co_blocks = cpg / co;
     const long long wp = W + 2, hp2 = H + 2;
     const size_t limit = std::min(kTf32SmemLimit, static_cast<size_t>(facts.smem_optin));
     if (!tf32_fits(cpg, W, 1, limit)) return gc_error(GC_UNSUPPORTED, "3xTF32 path: pixel strip does not fit");
@@ -720,7 +736,7 @@ int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
     long long best_nb = 1, best_items = 0, best_strips = 0;
     int best_sp = 1;
     double best_cost = -1.0;
-    for (int sp = 1; sp <= (cpg == 64 ? 2 : 1); ++sp) {
+    for (int sp = 1; sp <= (co == 64 ? 2 : 1); ++sp) {
         if (!tf32_fits(cpg, W, sp, limit)) continue;
         for (long long nb = 1; nb <= N; ++nb) {
             if (sp == 2 && nb > 1) break;
@@ -728,7 +744,7 @@ int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
             if (nb > 1 && out_rows * wp > 16 * gcb::kTf32N) break;  // stacking only pays for small planes
             if (nb * hp2 * wp >= (1LL << 30)) break;
             const long long strips = ceil_div(out_rows * wp, sp * gcb::kTf32N);
-            const long long items = static_cast<long long>(p->groups) * ceil_div(N, nb) * strips;
+            const long long items = static_cast<long long>(p->groups) * co_blocks * ceil_div(N, nb) * strips;
             if (items >= (1LL << 31)) continue;
             const double cost = static_cast<double>(ceil_div(items, facts.sms)) * sp * (sp == 2 ? 0.87 : 1.0);
             if (best_cost < 0.0 || cost < best_cost - 1e-9) {
@@ -750,6 +766,7 @@ int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
     P.wd = static_cast<int>(W);
     P.cpg = static_cast<int>(cpg);
     P.groups = static_cast<int>(p->groups);
+    P.co_blocks = static_cast<int>(co_blocks);
     P.wp = static_cast<int>(wp);
     P.nb = static_cast<int>(best_nb);
     P.blocks = static_cast<int>(ceil_div(N, best_nb));
@@ -758,12 +775,12 @@ int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
     P.strips = static_cast<int>(best_strips);
     P.items = static_cast<int>(best_items);
     P.chunks = static_cast<int>(cpg / 8);
-    P.m = static_cast<int>(std::max(64LL, 2 * cpg));
+    P.m = 2 * co > 64 ? 128 : 64;
     P.rows_b = static_cast<int>(rows_b);
     P.a_bytes = static_cast<unsigned>(9 * P.m * 32);
     P.b_bytes = static_cast<unsigned>(rows_b * 32);
-    P.wraw_bytes = static_cast<unsigned>(cpg * 72 * 4);
-    const void *fn = tf32_kernel_for(cpg, rows_b);
+    P.wraw_bytes = static_cast<unsigned>(co * 72 * 4);
+    const void *fn = tf32_kernel_for(co, rows_b);
     int ctas = 0;
     st = kernel_occupancy(dev, fn, gcb::kTf32Threads, smem, facts.smem_optin, ctas);
     if (st != GC_OK) return st;
@@ -784,7 +801,7 @@ int launch_tf32(const gc_shape *p, const float *x, const float *w, float *y, int
     plan.P.y = y;
     CUtensorMap wmap;
     std::memset(&wmap, 0, sizeof(wmap));
-    st = encode_rows_map(wmap, w, p->cout, (p->cin / p->groups) * 9, 72, plan.P.cpg);
+    st = encode_rows_map(wmap, w, p->cout, (p->cin / p->groups) * 9, 72, plan.P.cpg / plan.P.co_blocks);
     if (st != GC_OK) return st;
     void *args[] = {&plan.P, &wmap};
     cudaError_t e = launch_pdl(plan.fn, dim3(plan.grid), dim3(gcb::kTf32Threads), args, plan.smem, stream);
@@ -1097,8 +1114,8 @@ int gc_b200_conv(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_t
         return gc_error(GC_UNSUPPORTED, "small-image kernel needs at most 512 pixels per plane");
     if (kernel == GC_B200_TF32X3 && !tf32_eligible(p, x->data, w->data))
         return gc_error(GC_UNSUPPORTED,
-                        "3xTF32 path needs 8, 16, 32 or 64 channels per group, 16-byte aligned weights "
-                        "and a 256-pixel strip plus halo within 1024 rows and shared memory");
+                        "3xTF32 path needs a multiple of 8 channels per group, 16-byte aligned weights and "
+                        "a 256-pixel strip plus halo within 1024 rows and shared memory");
     int dev = -1;
     st = device_and_stream_checks(x, w, y, stream, dev);
     if (st != GC_OK) return st;

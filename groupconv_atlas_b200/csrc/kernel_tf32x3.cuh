@@ -10,13 +10,15 @@
 //         separates stacked images, so every tap (r, s) is a pure shift of
 //         the pixel tile by r*Wp + s rows, and small images share one tile;
 //   X   : the padded input of the block, 8 channels per K step;
-//   A_tap = [w_hi; w_lo]: the tap's weights split x = hi + lo (hi = x rounded
-//         to TF32, ties away; lo the exact FP32 remainder, of which the tensor
-//         core reads the top 19 bits), stacked along M so one MMA applies both.
+//   A_tap = [w_hi; w_lo]: the tap's weights of a block of CO output channels
+//         (the whole group up to 64 channels, 64-channel blocks of wider
+//         groups and dense layers) split x = hi + lo (hi = x rounded to TF32,
+//         ties away; lo the exact FP32 remainder, of which the tensor core
+//         reads the top 19 bits), stacked along M so one MMA applies both.
 // Two MMAs per tap and 8-channel step: D += A_tap X_hi, D += A_tap X_lo, i.e.
 // D_hi + D_lo = (w_hi + w_lo)(x_hi + x_lo) up to the truncation of the lo
 // parts (below 2^-20 of |x*w| per product, far inside the 1e-5 * sum|x*w|
-// acceptance bound).  tcgen05.mma.kind::tf32 with M = 128 (cpg 64) or 64
+// acceptance bound).  tcgen05.mma.kind::tf32 with M = 128 (CO > 32) or 64
 // rows of weights and N = 256 pixels: at this shape the tensor core runs at
 // its full TF32 rate whatever the per-tap shift of the pixel operand.
 //
@@ -26,7 +28,8 @@
 // second half w_lo of the same channels, so the epilogue adds the two parts
 // with one warp shuffle.
 //
-// Work item = (group, image block, strip of sp * 256 pixels); pipeline step =
+// Work item = (output-channel block, image block, strip of sp * 256 pixels);
+// pipeline step =
 // (item, chunk of 8 input channels).  Per step:
 //   - the converter warps load the step's pixels from global memory into
 //     registers (per thread its own pixel rows, 8 coalesced channel loads
@@ -63,6 +66,7 @@ struct Tf32Params {
     const float *w;
     float *y;
     int n, c, h, wd, cpg, groups;
+    int co_blocks;       // output-channel blocks per group: cpg / CO (CO = the kernel's block width)
     int wp;              // padded row pitch W + 2
     int nb;              // images stacked into one block
     int blocks;          // ceil(n / nb)
@@ -70,9 +74,9 @@ struct Tf32Params {
     int sp;              // 256-pixel strips per item: 1 (two accumulator sets alternate between
                          // items) or 2 (one set holding both strips)
     int strips;          // items per block: ceil(out_rows * wp / (sp * 256))
-    int items;           // groups * blocks * strips
+    int items;           // groups * co_blocks * blocks * strips
     int chunks;          // cpg / 8
-    int m;               // MMA M: max(64, 2 * cpg)
+    int m;               // MMA M: 128 when CO > 32, else 64
     int rows_b;          // pixel rows per step: sp*256 + 2*wp + 2, rounded up to 8 (<= kTf32MaxRows)
     unsigned a_bytes;    // one step's weight tiles: 9 taps * m * 32
     unsigned b_bytes;    // one pixel tile (hi or lo): rows_b * 32
@@ -218,14 +222,15 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
-// Item order: strip fastest, group slowest, so consecutive items of one CTA
-// mostly share the group's weights in L2.
-__device__ __forceinline__ void tf32_decode(const Tf32Params &P, int item, int &g, int &blk, int &strip) {
+// Item order: strip fastest, then image block, then output-channel block of
+// a group, group slowest.  gq = group * co_blocks + block: the item's weights
+// and outputs are channels gq*CO .. gq*CO+CO-1, its inputs the group's.
+__device__ __forceinline__ void tf32_decode(const Tf32Params &P, int item, int &gq, int &blk, int &strip) {
     const unsigned u = static_cast<unsigned>(item);
     const unsigned t = u / static_cast<unsigned>(P.strips);
     strip = static_cast<int>(u - t * static_cast<unsigned>(P.strips));
-    g = static_cast<int>(t / static_cast<unsigned>(P.blocks));
-    blk = static_cast<int>(t - static_cast<unsigned>(g) * static_cast<unsigned>(P.blocks));
+    gq = static_cast<int>(t / static_cast<unsigned>(P.blocks));
+    blk = static_cast<int>(t - static_cast<unsigned>(gq) * static_cast<unsigned>(P.blocks));
 }
 
 // x = hi + lo: hi rounded to TF32 (nearest, ties away from zero) by integer
@@ -268,10 +273,10 @@ __device__ __forceinline__ RowGeom<ROWS> tf32_rows(const Tf32Params &P, int blk,
 
 // The 8 channels of the chunk at every pixel row of this thread (0 outside images).
 template <int ROWS>
-__device__ __forceinline__ void tf32_load_rows(const Tf32Params &P, int g, int chunk, const RowGeom<ROWS> &gm,
+__device__ __forceinline__ void tf32_load_rows(const Tf32Params &P, int gq, int chunk, const RowGeom<ROWS> &gm,
                                                float (&v)[ROWS][8]) {
     const long long hw = static_cast<long long>(P.h) * P.wd;
-    const float *base = P.x + (static_cast<long long>(g) * P.cpg + chunk * 8) * hw;
+    const float *base = P.x + (static_cast<long long>(gq / P.co_blocks) * P.cpg + chunk * 8) * hw;
 #pragma unroll
     for (int r = 0; r < ROWS; ++r) {
         const bool in = (gm.valid >> r) & 1u;
@@ -288,22 +293,22 @@ __device__ __forceinline__ void tf32_load_rows(const Tf32Params &P, int g, int c
 // pixels 0-15 of the chunk, lane l + HALF pixels 16-31).  The sums go through
 // the warp's transpose buffer, so that the stores run with consecutive lanes
 // on consecutive pixels of one output channel.
-template <int M>
+template <int M, int CO>
 __device__ __forceinline__ void tf32_epilogue(const Tf32Params &P, uint32_t acc, int item, int sub, int warp,
                                               int lane, float *ep) {
     constexpr int HALF = M / 8;  // output channels per lane quadrant
     int g, blk, strip;
     tf32_decode(P, item, g, blk, strip);
     const int quad = warp & 3, colhalf = warp >> 2;
-    if (quad * HALF >= P.cpg) return;  // quadrant holds only zero rows (warp-uniform)
-    const int nco = min(HALF, P.cpg - quad * HALF);
+    if (quad * HALF >= CO) return;  // quadrant holds only zero rows (warp-uniform)
+    const int nco = min(HALF, CO - quad * HALF);
     const bool low = (lane & HALF) == 0;
     const bool writer = lane < 2 * HALF && (lane & (HALF - 1)) < nco;
     const int hp2 = P.h + 2;
     const long long hw = static_cast<long long>(P.h) * P.wd;
     const long long image_floats = static_cast<long long>(P.c) * hw;
     const int out_px = P.out_rows * P.wp;
-    float *const ych = P.y + (static_cast<long long>(g) * P.cpg + quad * HALF) * hw;
+    float *const ych = P.y + (static_cast<long long>(g) * CO + quad * HALF) * hw;
     float *const epw = ep + (lane & (HALF - 1)) * 33 + (low ? 0 : 16);
 #pragma unroll 1
     for (int c32 = 0; c32 < 4; ++c32) {
@@ -330,10 +335,10 @@ __device__ __forceinline__ void tf32_epilogue(const Tf32Params &P, uint32_t acc,
     }
 }
 
-template <int CPG, int ROWS>
+template <int CO, int ROWS>
 __global__ void __launch_bounds__(kTf32Threads, 1)
     tf32x3_conv_kernel(const __grid_constant__ Tf32Params P, const __grid_constant__ CUtensorMap wmap) {
-    constexpr int M = CPG * 2 > 64 ? CPG * 2 : 64;
+    constexpr int M = CO * 2 > 64 ? 128 : 64;
     constexpr int RQ = M / 4;      // A rows per lane quadrant
     constexpr int HALF = RQ / 2;   // output channels per quadrant
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -367,7 +372,7 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
         fence_barrier_init();
     }
     // Rows of A no output channel uses (cpg < M / 2) stay zero for the whole kernel.
-    if (CPG * 2 < M)
+    if (CO * 2 < M)
         for (unsigned e = tid; e < 2 * P.a_bytes / 16; e += blockDim.x)
             reinterpret_cast<uint4 *>(a0)[e] = make_uint4(0u, 0u, 0u, 0u);
     if (warp == 0) tmem_alloc(tmem_slot, 2 * kTf32N);
@@ -394,7 +399,7 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
                 int g, blk, strip;
                 tf32_decode(P, first + item_k * stride, g, blk, strip);
                 mbar_arrive_expect_tx(&w_full[s], P.wraw_bytes);
-                tma_load_2d(wraw0 + s * P.wraw_bytes, &wmap, chunk * 72, g * P.cpg, &w_full[s]);
+                tma_load_2d(wraw0 + s * P.wraw_bytes, &wmap, chunk * 72, g * CO, &w_full[s]);
                 issued = k;
             }
             // Loads still in flight must land before the CTA's shared memory
@@ -459,7 +464,7 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
         // Converter / epilogue warps.
         const int ctid = tid;  // 0 .. 255
         const uint32_t lbo_x = P.rows_b * 16u;
-        constexpr int kWVals = 72 * CPG;  // weights per chunk
+        constexpr int kWVals = 72 * CO;  // weights per chunk
         constexpr int kWPerThread = (kWVals + kConvThreads - 1) / kConvThreads;
         float *const ep = ep0 + warp * kTf32EpiFloats;
         int pending = -1;  // per-CTA item index whose epilogue is due
@@ -476,7 +481,7 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
             tc_fence_after();
             for (int sub = 0; sub < P.sp; ++sub) {
                 const int buf = P.sp == 1 ? (it & 1) : sub;
-                tf32_epilogue<M>(P, tmem_base + static_cast<uint32_t>(buf * kTf32N), first + it * stride, sub, warp,
+                tf32_epilogue<M, CO>(P, tmem_base + static_cast<uint32_t>(buf * kTf32N), first + it * stride, sub, warp,
                                  lane, ep);
                 tc_fence_before();
                 __syncwarp();
@@ -516,17 +521,17 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
                 failed = true;
                 return;
             }
-            // Weights: v = ((tap*2 + half)*CPG + co)*4 + j enumerates the chunk's
+            // Weights: v = ((tap*2 + half)*CO + co)*4 + j enumerates the chunk's
             // weights w[co][half*4 + j][tap]; hi goes to A row m_hi(co), lo to
             // m_hi(co) + HALF, at byte tap*M*32 + half*M*16 + row*16 + j*4.
             {
                 const float *wr = reinterpret_cast<const float *>(wraw0 + s * P.wraw_bytes);
                 unsigned char *const at = a0 + s * P.a_bytes;
-#pragma unroll
+#pragma unroll 9
                 for (int q = 0; q < kWPerThread; ++q) {
                     const int v = ctid + q * kConvThreads;
                     if (kWVals % kConvThreads == 0 || v < kWVals) {
-                        const int j = v & 3, co = (v >> 2) % CPG, th = (v >> 2) / CPG;
+                        const int j = v & 3, co = (v >> 2) % CO, th = (v >> 2) / CO;
                         const int half = th & 1, tap = th >> 1;
                         uint32_t hi, lo;
                         tf32_split(wr[co * 72 + (half * 4 + j) * 9 + tap], hi, lo);

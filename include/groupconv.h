@@ -109,7 +109,8 @@ typedef enum {
     GC_B200_GENERAL = 1,    /* any geometry, one output column run per thread   */
     GC_B200_DIRECT_LDG = 2, /* B geometry, smem band staged by cp.async         */
     GC_B200_DIRECT_TMA = 3, /* B geometry, smem band staged by TMA tensor loads */
-    GC_B200_TF32X3 = 4,     /* B geometry, 8-64 channels per group: tcgen05 3xTF32 implicit GEMM */
+    GC_B200_TF32X3 = 4,     /* B geometry, a multiple of 8 channels per group (dense
+                               layers too): tcgen05 3xTF32 implicit GEMM */
     GC_B200_SMALL = 5       /* B geometry, small images (whole planes per CTA, any width) */
 } gc_b200_kernel;
 

@@ -34,18 +34,25 @@ def test_golden_all_implementations(native, torch_cuda, golden_cases):
             assert_matches(c.shape, c.x, c.w, y, c.y32, label=f'{c.name} impl{impl} [{plan}]')
 
 
+def tf32_co(cpg):
+    """Output channels per tensor-path item: the widest multiple of 8 up to 64
+    dividing the group; 0: not served."""
+    return next((co for co in range(64, 7, -8) if cpg % co == 0), 0)
+
+
 def tf32_fits(cpg, w):
     """A 256-pixel strip plus its 2 * (W + 2) + 2 halo rows must fit the
     converters' 1024 rows and the shared memory: weights staged twice, A tiles
-    of max(64, 2 cpg) rows twice, four pixel tiles, the epilogue buffers and
-    the barriers."""
+    of 64 or 128 rows twice, four pixel tiles, the epilogue buffers and the
+    barriers."""
+    co = tf32_co(cpg)
     rows_b = -(-(256 + 2 * (w + 2) + 2) // 8) * 8
-    smem = 2 * cpg * 288 + 2 * 9 * max(64, 2 * cpg) * 32 + 4 * rows_b * 32 + 8 * 16 * 33 * 4 + 128
+    smem = 2 * co * 288 + 2 * 9 * (128 if 2 * co > 64 else 64) * 32 + 4 * rows_b * 32 + 8 * 16 * 33 * 4 + 128
     return rows_b <= 1024 and smem <= 227 * 1024
 
 
 def tf32_eligible(s):
-    return s.b_geometry and s.cpg in (8, 16, 32, 64) and tf32_fits(s.cpg, s.w)
+    return s.b_geometry and tf32_co(s.cpg) > 0 and tf32_fits(s.cpg, s.w)
 
 
 TF32_WIDEST_CPG16 = max(w for w in range(1, 1024) if tf32_fits(16, w))
@@ -157,7 +164,18 @@ TF32_SHAPES = [
     (5, 64, 5, 6, 32), (7, 32, 3, 3, 16), (3, 64, 1, 1, 64), (9, 128, 10, 9, 64),
     # many groups: every CTA crosses group boundaries
     (3, 512, 9, 10, 16), (2, 512, 12, 12, 32), (1, 256, 20, 30, 8),
+    # 24/40/48/56-channel groups; wide groups and dense layers in output-channel blocks
+    (2, 96, 11, 13, 48), (2, 48, 10, 9, 24), (1, 80, 12, 11, 40), (1, 112, 9, 8, 56),
+    (2, 256, 9, 10, 128), (1, 256, 12, 14, 256), (2, 192, 8, 9, 96), (1, 160, 7, 9, 80), (1, 144, 8, 8, 72),
 ]
+
+
+def test_tf32x3_refuses_unserved_group_width(native, torch_cuda):
+    s = Shape(n=1, cin=40, cout=40, h=6, w=7, groups=2)  # 20 channels per group
+    x, wt = inputs(s, 5)
+    with pytest.raises(NativeError) as err:
+        run(native, torch_cuda, s, x, wt, kernel='tf32x3')
+    assert err.value.status == GC_UNSUPPORTED
 
 
 def test_tf32x3_refuses_rows_beyond_reach(native, torch_cuda):
