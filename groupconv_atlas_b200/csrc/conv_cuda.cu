@@ -37,7 +37,68 @@ using gcb::GeneralParams;
 
 constexpr int kStages = 3;
 
+// The last launch's plan on this thread, kept as numbers and formatted only
+// when gc_b200_last_plan asks for it (formatting costs about a third of a
+// microsecond, a tenth of the host time of a call).
+struct PlanRecord {
+    enum Kind { kNone, kDirect, kWide, kTf32, kSmall, kGeneral } kind = kNone;
+    const char *name = "";  // variant name, static storage
+    bool tma = false;
+    long long v[14] = {};
+};
+thread_local PlanRecord g_last;
 thread_local std::string g_plan;
+
+std::string format_plan(const PlanRecord &r) {
+    char buf[400];
+    const long long *v = r.v;
+    switch (r.kind) {
+    case PlanRecord::kDirect:
+        std::snprintf(buf, sizeof(buf),
+                      "kernel=direct_%s engine=group variant=%s grid=%lld block=%lld smem=%lld ctas_per_sm=%lld "
+                      "cb=%lld bh=%lld items=%lld cells=%lld stages=%lld pitch=%lld rows=%lld bulk_w=%lld "
+                      "vec_store=%lld",
+                      r.tma ? "tma" : "ldg", r.name, v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7], v[8], v[9],
+                      v[10], v[11], v[12]);
+        break;
+    case PlanRecord::kWide:
+        std::snprintf(buf, sizeof(buf),
+                      "kernel=direct_%s engine=wide variant=%s grid=%lld block=%lld smem=%lld ctas_per_sm=%lld "
+                      "kc=%lld chunks=%lld co_item=%lld bh=%lld items=%lld cells=%lld pitch=%lld rows=%lld "
+                      "vec_store=%lld",
+                      r.tma ? "tma" : "ldg", r.name, v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7], v[8], v[9],
+                      v[10], v[11], v[12]);
+        break;
+    case PlanRecord::kTf32:
+        std::snprintf(buf, sizeof(buf),
+                      "kernel=tf32x3 engine=tcgen05 n_cta=%lld block=320 smem=%lld M=%lld N=%lld nb=%lld sp=%lld "
+                      "strips=%lld items=%lld chunks=%lld rows_b=%lld",
+                      v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7], v[8], v[9]);
+        break;
+    case PlanRecord::kSmall:
+        std::snprintf(buf, sizeof(buf),
+                      "kernel=small grid=%lld block=%lld smem=%lld ctas_per_sm=%lld cob=%lld cb=%lld items=%lld "
+                      "vec=%lld stages=%lld",
+                      v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7], v[8]);
+        break;
+    case PlanRecord::kGeneral:
+        std::snprintf(buf, sizeof(buf), "kernel=general grid=%lld block=%lld run=%lld cob=%lld index=%s runs=%lld",
+                      v[0], v[1], v[2], v[3], v[4] ? "32" : "64", v[5]);
+        break;
+    default:
+        buf[0] = '\0';
+    }
+    return buf;
+}
+
+template <class... T>
+void record_plan(PlanRecord::Kind kind, const char *name, bool tma, T... values) {
+    g_last.kind = kind;
+    g_last.name = name;
+    g_last.tma = tma;
+    const long long vals[] = {static_cast<long long>(values)...};
+    for (size_t i = 0; i < sizeof...(T); ++i) g_last.v[i] = vals[i];
+}
 
 long long round_up(long long v, long long m) { return (v + m - 1) / m * m; }
 long long ceil_div(long long a, long long b) { return (a + b - 1) / b; }
@@ -605,7 +666,6 @@ int launch_direct(const gc_shape *p, const float *x, const float *w, float *y, b
     CUtensorMap map;
     std::memset(&map, 0, sizeof(map));
     void *args[2];
-    char buf[360];
     if (!plan.wide) {
         plan.D.x = x;
         plan.D.w = w;
@@ -615,12 +675,6 @@ int launch_direct(const gc_shape *p, const float *x, const float *w, float *y, b
             if (st != GC_OK) return st;
         }
         args[0] = &plan.D;
-        std::snprintf(buf, sizeof(buf),
-                      "kernel=direct_%s engine=group variant=%s grid=%d block=%d smem=%zu ctas_per_sm=%d "
-                      "cb=%d bh=%d items=%d cells=%d stages=%d pitch=%d rows=%d bulk_w=%d vec_store=%d",
-                      tma ? "tma" : "ldg", plan.var->name, plan.grid, plan.threads, plan.smem,
-                      plan.ctas_per_sm, plan.D.cb, plan.D.bh, plan.D.items, plan.D.cells, plan.D.stages,
-                      plan.D.pitch, plan.D.rows, plan.D.bulk_w, plan.D.vec_store);
     } else {
         plan.Wp.x = x;
         plan.Wp.w = w;
@@ -630,18 +684,19 @@ int launch_direct(const gc_shape *p, const float *x, const float *w, float *y, b
             if (st != GC_OK) return st;
         }
         args[0] = &plan.Wp;
-        std::snprintf(buf, sizeof(buf),
-                      "kernel=direct_%s engine=wide variant=%s grid=%d block=%d smem=%zu ctas_per_sm=%d "
-                      "kc=%d chunks=%d co_item=%d bh=%d items=%lld cells=%d pitch=%d rows=%d vec_store=%d",
-                      tma ? "tma" : "ldg", plan.var->name, plan.grid, plan.threads, plan.smem,
-                      plan.ctas_per_sm, plan.Wp.kc, plan.Wp.chunks, plan.Wp.co_item, plan.Wp.bh,
-                      plan.Wp.items, plan.Wp.cells, plan.Wp.pitch, plan.Wp.rows, plan.Wp.vec_store);
     }
     args[1] = &map;
     const void *fn = tma ? plan.var->fn_tma : plan.var->fn_ldg;
     cudaError_t e = launch_pdl(fn, dim3(plan.grid), dim3(plan.threads), args, plan.smem, stream);
     if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
-    g_plan = buf;
+    if (!plan.wide)
+        record_plan(PlanRecord::kDirect, plan.var->name, tma, plan.grid, plan.threads, plan.smem, plan.ctas_per_sm,
+                    plan.D.cb, plan.D.bh, plan.D.items, plan.D.cells, plan.D.stages, plan.D.pitch, plan.D.rows,
+                    plan.D.bulk_w, plan.D.vec_store);
+    else
+        record_plan(PlanRecord::kWide, plan.var->name, tma, plan.grid, plan.threads, plan.smem, plan.ctas_per_sm,
+                    plan.Wp.kc, plan.Wp.chunks, plan.Wp.co_item, plan.Wp.bh, plan.Wp.items, plan.Wp.cells,
+                    plan.Wp.pitch, plan.Wp.rows, plan.Wp.vec_store);
     return GC_OK;
 }
 
@@ -806,13 +861,8 @@ int launch_tf32(const gc_shape *p, const float *x, const float *w, float *y, int
     void *args[] = {&plan.P, &wmap};
     cudaError_t e = launch_pdl(plan.fn, dim3(plan.grid), dim3(gcb::kTf32Threads), args, plan.smem, stream);
     if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
-    char buf[256];
-    std::snprintf(buf, sizeof(buf),
-                  "kernel=tf32x3 engine=tcgen05 n_cta=%d block=320 smem=%zu M=%d N=%d nb=%d sp=%d strips=%d "
-                  "items=%d chunks=%d rows_b=%d",
-                  plan.grid, plan.smem, plan.P.m, gcb::kTf32N, plan.P.nb, plan.P.sp, plan.P.strips, plan.P.items,
-                  plan.P.chunks, plan.P.rows_b);
-    g_plan = buf;
+    record_plan(PlanRecord::kTf32, "", false, plan.grid, plan.smem, plan.P.m, gcb::kTf32N, plan.P.nb, plan.P.sp,
+                plan.P.strips, plan.P.items, plan.P.chunks, plan.P.rows_b);
     return GC_OK;
 }
 
@@ -893,11 +943,7 @@ int launch_small(const gc_shape *p, const float *x, const float *w, float *y, in
     void *args[] = {&P};
     cudaError_t e = launch_pdl(fn, dim3(grid), dim3(threads), args, smem, stream);
     if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
-    char buf[200];
-    std::snprintf(buf, sizeof(buf),
-                  "kernel=small grid=%d block=%d smem=%zu ctas_per_sm=%d cob=%d cb=%d items=%d vec=%d stages=%d", grid,
-                  threads, smem, ctas, cob, P.cb, P.items, P.vec, P.stages);
-    g_plan = buf;
+    record_plan(PlanRecord::kSmall, "", false, grid, threads, smem, ctas, cob, P.cb, P.items, P.vec, P.stages);
     return GC_OK;
 }
 
@@ -959,10 +1005,7 @@ int launch_general(const gc_shape *p, int64_t ho, int64_t wo, const float *x, co
     void *args[] = {&P};
     cudaError_t e = launch_pdl(fn, dim3(static_cast<unsigned>(blocks)), dim3(threads), args, 0, stream);
     if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
-    char buf[160];
-    std::snprintf(buf, sizeof(buf), "kernel=general grid=%lld block=%d run=%d cob=%d index=%s runs=%lld", blocks,
-                  threads, kGeneralRun, cob, narrow ? "32" : "64", P.total_runs);
-    g_plan = buf;
+    record_plan(PlanRecord::kGeneral, "", false, blocks, threads, kGeneralRun, cob, narrow ? 1 : 0, P.total_runs);
     return GC_OK;
 }
 
@@ -1123,7 +1166,10 @@ int gc_b200_conv(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_t
     return run_kernel(p, x, w, y, kernel, dev, stream);
 }
 
-const char *gc_b200_last_plan(void) { return g_plan.c_str(); }
+const char *gc_b200_last_plan(void) {
+    g_plan = format_plan(g_last);
+    return g_plan.c_str();
+}
 
 int gc_b200_device_status(uint32_t *status, int clear) {
     if (status == nullptr) return gc_error(GC_INVALID, "null status pointer");

@@ -12,6 +12,8 @@ batch - tests check slices against the oracle, benchmarks run the full batch.
   config4  MobileNetV2 block, N4, depthwise 3x3 on C144 56x56 (see bench.py)   seed 2
   config5  N1024 C256 56x56 groups 32 (cpg 8) and groups 4 (cpg 64)
            x~U[-1,1), w~U[-1,1)/sqrt(9 cpg),                                      seed 3
+  atlas    the reference's 80-shape Atlas: N{1,32} x H=W{7,14,28,56,112}
+           x cpg{1,2,4,8,16,32,64,256}, C256; x, w ~U[-1,1) seeded per shape id
 """
 from __future__ import annotations
 
@@ -131,6 +133,21 @@ def sweep_shapes(count=80, seed=1):
             for n, c, cpg, hw in itertools.product(SWEEP_N, SWEEP_C, SWEEP_CPG, SWEEP_HW) if cpg <= c]
     picks = np.random.default_rng(seed).choice(len(grid), size=count, replace=False)
     return [grid[i] for i in sorted(int(i) for i in picks)]
+
+
+ATLAS_N = (1, 32)
+ATLAS_HW = (7, 14, 28, 56, 112)
+ATLAS_CPG = (1, 2, 4, 8, 16, 32, 64, 256)
+ATLAS_C = 256
+
+
+def atlas_shapes():
+    """The reference's frozen 80-shape Atlas (configs/atlas.json): C256, 3x3,
+    stride 1, pad 1, N x H=W x cpg over the grid above, in the file's order
+    (N, then H, then cpg ascending); cpg 256 is a dense layer (one group).
+    Inputs are the reference's per-shape seeding (``api.inputs``)."""
+    return [Shape(n=n, cin=ATLAS_C, cout=ATLAS_C, h=hw, w=hw, groups=ATLAS_C // cpg)
+            for n, hw, cpg in itertools.product(ATLAS_N, ATLAS_HW, ATLAS_CPG)]
 
 
 def sweep_inputs(shape, first=0, count=None):
