@@ -52,7 +52,7 @@ def parse_args(argv=None):
     ap.add_argument('--impl', choices=['ours', 'reference'], default='ours')
     ap.add_argument('--workload', default='config2',
                     choices=['config1', 'config2', 'config4_leaf', 'config5_g32', 'config5_g4', 'config4_block',
-                             'config3', 'atlas'])
+                             'config3', 'atlas', 'model_layers'])
     ap.add_argument('--scaling', choices=['weak', 'strong'], default=None,
                     help='weak: each rank runs the full workload batch; strong: the batch is sharded')
     ap.add_argument('--shape', default=None,
@@ -795,35 +795,34 @@ def run_sweep(args):
     return 0 if line['all_points_ok'] else 1
 
 
-def run_atlas(args):
-    """The reference's 80-shape Atlas (C256, N{1,32} x H=W{7..112} x cpg{1..64,256})
-    measured the reference's way: per shape, paired batches of device timings
-    of gc_cuda_conv (implementation 3) and torch.nn.functional.conv2d (TF32
-    off, benchmark mode), the two run in a seeded random order within each
-    batch (bench/cuda_run.py:231-248); a sample is one CUDA-graph replay of
-    `repeats` calls (about 1 ms of work, at most 20 calls) over rotating
-    buffers larger than L2 where the shape allows; the speed-up and its 95 %
-    interval come from the paired batch-median bootstrap (bench/stats.py).
-    Inputs are the reference's seeded per-shape inputs; every output is
-    checked at 64 FP64 points before timing."""
+def paired_shape_rows(args, entries):
+    """Per shape of `entries` ((Shape, extra row fields) pairs): paired
+    batches of device timings of gc_cuda_conv (implementation 3, or 0 for
+    layers outside B geometry) and
+    torch.nn.functional.conv2d (TF32 off, benchmark mode), the two run in a
+    seeded random order within each batch (bench/cuda_run.py:231-248); a
+    sample is one CUDA-graph replay of `repeats` calls (about 1 ms of work, at
+    most 20 calls) over rotating buffers larger than L2 where the shape
+    allows; the speed-up and its 95 % interval come from the paired
+    batch-median bootstrap (bench/stats.py).  Inputs are the reference's
+    seeded per-shape inputs; every output is checked at 64 FP64 points before
+    timing, against the reference's fixed tolerances and against the
+    1e-5 * sum|x*w| bound.  Returns one row per shape."""
     import random
     import torch
     import torch.nn.functional as F
-    from groupconv_atlas_b200 import api, stats, workloads
+    from groupconv_atlas_b200 import api, stats
     from oracle import oracle as orc
-    rank, world, local = dist_setup()
-    if rank != 0:
-        return 0
-    torch.cuda.set_device(local)
-    set_fp32_precision(torch)
-    torch.backends.cudnn.benchmark = True
     native = api.Native()
     stream = torch.cuda.Stream()
     batches, samples = args.atlas_batches, args.atlas_samples
     rows = []
-    for s in workloads.atlas_shapes():
+    for s, extra in entries:
+        # implementations 1-3 serve B geometry (3x3, stride 1, pad 1, Cin ==
+        # Cout) only; every other layer runs on implementation 0
+        impl = 3 if (s.r, s.s, s.sh, s.sw, s.ph, s.pw, s.dh, s.dw, s.cin) == (3, 3, 1, 1, 1, 1, 1, 1, s.cout) else 0
         x_host, w_host = api.inputs(s)
-        nbytes = 4 * (2 * math.prod(s.input) + math.prod(s.weight))
+        nbytes = 4 * (math.prod(s.input) + math.prod(s.output) + math.prod(s.weight))
         sets = int(max(1, min(8, math.ceil(3 * L2_BYTES / nbytes))))
         g = torch.Generator(device='cuda').manual_seed(int(s.id[3:11], 16))
         with torch.cuda.stream(stream):
@@ -831,7 +830,7 @@ def run_atlas(args):
                                                       for _ in range(sets - 1)]
             ys = [torch.empty(s.output, device='cuda') for _ in range(sets)]
             w = torch.from_numpy(w_host).cuda()
-            native.cuda(s, xs[0], w, ys[0], 3, stream.cuda_stream)
+            native.cuda(s, xs[0], w, ys[0], impl, stream.cuda_stream)
             plan = native.last_plan()
             stream.synchronize()
             y0 = ys[0].cpu().numpy()
@@ -841,8 +840,9 @@ def run_atlas(args):
         expected = orc.oracle_points(s, x_host, w_host, check['points'])
         bound_ok = bool(np.all(np.abs(got - expected) <= orc.BOUND_FACTOR * abs_sum))
         del x_host, y0
-        calls = {'ours': lambda k: native.cuda(s, xs[k % sets], w, ys[k % sets], 3, stream.cuda_stream),
-                 'cudnn': lambda k: F.conv2d(xs[k % sets], w, padding=1, groups=s.groups)}
+        conv = dict(stride=(s.sh, s.sw), padding=(s.ph, s.pw), dilation=(s.dh, s.dw), groups=s.groups)
+        calls = {'ours': lambda k: native.cuda(s, xs[k % sets], w, ys[k % sets], impl, stream.cuda_stream),
+                 'cudnn': lambda k: F.conv2d(xs[k % sets], w, **conv)}
         graphs, repeats = {}, {}
         with torch.cuda.stream(stream), torch.inference_mode():
             for name, call in calls.items():
@@ -872,27 +872,71 @@ def run_atlas(args):
                     us = [ev[2 * i].elapsed_time(ev[2 * i + 1]) * 1e3 / repeats[name] for i in range(samples)]
                     medians[name].append(statistics.median(us))
         cmp = stats.compare_batches(medians['cudnn'], medians['ours'])
-        rows.append({'shape': [s.n, s.cin, s.h, s.w, s.cpg], 'shape_id': s.id,
+        rows.append({**extra, 'shape': [s.n, s.cin, s.h, s.w, s.cpg], 'stride': s.sh, 'implementation': impl,
+                     'shape_id': s.id,
                      'kernel': plan.split()[0].split('=')[1], 'us': statistics.median(medians['ours']),
                      'cudnn_us': statistics.median(medians['cudnn']), 'speedup_vs_cudnn': cmp['speedup'],
                      'ci95': cmp['ci95'], 'classification': cmp['classification'],
                      'repeats': repeats, 'points_ok': check['passed'], 'bound_ok': bound_ok,
-                     'max_abs_err': check['max_abs'], 'reduction_terms': s.cpg * 9})
+                     'max_abs_err': check['max_abs'], 'reduction_terms': s.cpg * s.r * s.s})
         del graphs, xs, ys
         torch.cuda.empty_cache()
+    return rows
+
+
+def shape_set_line(args, workload, metric, rows, data, extra=None):
     geo = lambda v: math.exp(statistics.fmean(math.log(max(x, 1e-12)) for x in v))
     counts = {c: sum(r['classification'] == c for r in rows) for c in ('WIN', 'TIE', 'LOSS', 'UNCERTAIN')}
     ok = all(r['bound_ok'] and (r['points_ok'] or r['reduction_terms'] > 576) for r in rows)
-    line = {'metric': 'atlas: geomean speedup of gc_cuda_conv over torch/cuDNN (TF32 off), 80 shapes',
-            'value': geo(r['speedup_vs_cudnn'] for r in rows), 'unit': 'x', 'n_gpus': 1,
-            'steps': batches * samples, 'warmup': 10, 'higher_is_better': True, 'scaling': 'weak',
-            'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic: the reference seeding per shape id, x, w ~U[-1,1)',
-            'config': {'workload': 'atlas', 'shapes': len(rows), 'batches': batches, 'samples_per_batch': samples,
+    line = {'metric': metric, 'value': geo(r['speedup_vs_cudnn'] for r in rows), 'unit': 'x', 'n_gpus': 1,
+            'steps': args.atlas_batches * args.atlas_samples, 'warmup': 10, 'higher_is_better': True,
+            'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': data,
+            'config': {'workload': workload, 'shapes': len(rows), 'batches': args.atlas_batches,
+                       'samples_per_batch': args.atlas_samples,
                        'timing': 'CUDA-graph replay, both sides, seeded random order per batch',
                        'l2': 'rotating input/output sets, 3x L2 where the shape allows'},
-            'classification': counts, 'all_checks_ok': ok, 'rows': rows}
+            'classification': counts, 'all_checks_ok': ok, **(extra or {}), 'rows': rows}
     print(json.dumps(line), flush=True)
     return 0 if ok else 1
+
+
+def run_atlas(args):
+    """The reference's 80-shape Atlas (C256, N{1,32} x H=W{7..112} x
+    cpg{1..64,256}) measured the reference's way (paired_shape_rows)."""
+    import torch
+    from groupconv_atlas_b200 import workloads
+    rank, world, local = dist_setup()
+    if rank != 0:
+        return 0
+    torch.cuda.set_device(local)
+    set_fp32_precision(torch)
+    torch.backends.cudnn.benchmark = True
+    rows = paired_shape_rows(args, [(s, {}) for s in workloads.atlas_shapes()])
+    return shape_set_line(args, 'atlas', 'atlas: geomean speedup of gc_cuda_conv over torch/cuDNN (TF32 off), '
+                          '80 shapes', rows, 'synthetic: the reference seeding per shape id, x, w ~U[-1,1)')
+
+
+def run_model_layers(args):
+    """The reference's 12 frozen model-layer operations: the 8 without bias
+    measured like the Atlas; the 4 biased ConvNeXt layers reported as
+    unsupported (the ABI has no bias), as bench/model_run.py does."""
+    import torch
+    from groupconv_atlas_b200 import workloads
+    rank, world, local = dist_setup()
+    if rank != 0:
+        return 0
+    torch.cuda.set_device(local)
+    set_fp32_precision(torch)
+    torch.backends.cudnn.benchmark = True
+    layers = workloads.model_layers()
+    rows = paired_shape_rows(args, [(l.shape, {'model': l.model, 'module_path': l.module_path})
+                                    for l in layers if not l.bias])
+    unsupported = [{'model': l.model, 'module_path': l.module_path, 'n': l.shape.n, 'status': 'UNSUPPORTED',
+                    'reason': 'bias not implemented'} for l in layers if l.bias]
+    return shape_set_line(args, 'model_layers', 'model layers: geomean speedup of gc_cuda_conv over torch/cuDNN '
+                          '(TF32 off), 8 no-bias layers', rows,
+                          'synthetic: the reference seeding per shape id, x, w ~U[-1,1)',
+                          {'unsupported': unsupported})
 
 
 def main(argv=None):
@@ -905,6 +949,8 @@ def main(argv=None):
         return run_sweep(args)
     if args.workload == 'atlas':
         return run_atlas(args)
+    if args.workload == 'model_layers':
+        return run_model_layers(args)
     return run_ours(args)
 
 

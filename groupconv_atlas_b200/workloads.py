@@ -150,6 +150,39 @@ def atlas_shapes():
             for n, hw, cpg in itertools.product(ATLAS_N, ATLAS_HW, ATLAS_CPG)]
 
 
+@dataclasses.dataclass(frozen=True)
+class ModelLayer:
+    model: str
+    module_path: str
+    shape: Shape
+    bias: bool
+
+
+def model_layers():
+    """The reference's 12 frozen model-layer operations
+    (configs/model-shapes-protocol.json: torchvision forward hooks at 224x224,
+    batches 1 and 4): MobileNetV2 depthwise 3x3 (stride 1 and 2), ResNeXt50
+    grouped 3x3 with 32 groups (stride 1 and 2), and ConvNeXt-tiny depthwise
+    7x7, which carry a bias the ABI does not have and are reported as
+    unsupported, as the reference does (bench/model_run.py).  Inputs are the
+    reference's per-shape seeding (``api.inputs``)."""
+    def layer(model, path, bias, **geo):
+        return [ModelLayer(model, path, Shape(n=n, **geo), bias) for n in (1, 4)]
+    mbv2_s1 = layer('mobilenet_v2', 'features.3.conv.1.0', False, cin=144, cout=144, h=56, w=56, groups=144)
+    mbv2_s2 = layer('mobilenet_v2', 'features.2.conv.1.0', False, cin=96, cout=96, h=112, w=112, groups=96, sh=2, sw=2)
+    rx_s1 = layer('resnext50_32x4d', 'layer1.0.conv2', False, cin=128, cout=128, h=56, w=56, groups=32)
+    rx_s2 = layer('resnext50_32x4d', 'layer2.0.conv2', False, cin=256, cout=256, h=56, w=56, groups=32, sh=2, sw=2)
+    cn_1 = layer('convnext_tiny', 'features.1.0.block.0', True, cin=96, cout=96, h=56, w=56, r=7, s=7, groups=96,
+                 ph=3, pw=3)
+    cn_3 = layer('convnext_tiny', 'features.3.0.block.0', True, cin=192, cout=192, h=28, w=28, r=7, s=7, groups=192,
+                 ph=3, pw=3)
+    # the protocol's order: per model, batch 1 then batch 4, layers in selection order
+    layers = []
+    for a, b in ((mbv2_s1, mbv2_s2), (rx_s1, rx_s2), (cn_1, cn_3)):
+        layers += [a[0], b[0], a[1], b[1]]
+    return layers
+
+
 def sweep_inputs(shape, first=0, count=None):
     """Seeded uniform inputs of one sweep shape (seed derived from its id)."""
     seed = int(shape.id[3:11], 16)

@@ -11,6 +11,9 @@ It writes ``atlas_fixture.json`` next to this script:
           groups and the reference's shape id, in the file's order.
   stats   paired batch-median inputs and the reference's own
           bench/stats.py compare_batches / describe results for them.
+  model_layers  the reference's 12 frozen model-layer operations
+          (configs/model-shapes-protocol.json): geometry, bias flag, model,
+          module path and shape id.
 """
 from __future__ import annotations
 
@@ -48,9 +51,14 @@ def main():
         c = (cand * (1 + spread * rng.standard_normal(batches))).round(4).tolist()
         cases.append({'base': b, 'candidate': c, 'compare': ref.compare_batches(b, c),
                       'describe_base': ref.describe(b)})
-    out = {'source': 'configs/atlas.json and bench/stats.py of the reference', 'atlas': shapes, 'stats': cases}
+    proto = json.loads((Path(args.reference) / 'configs' / 'model-shapes-protocol.json').read_text())
+    keys = ('n', 'cin', 'cout', 'h', 'w', 'r', 's', 'groups', 'sh', 'sw', 'ph', 'pw', 'dh', 'dw', 'bias', 'model',
+            'module_path', 'shape_id')
+    layers = [{k: s[k] for k in keys} for s in proto['frozen_shapes']]
+    out = {'source': 'configs/atlas.json, configs/model-shapes-protocol.json and bench/stats.py of the reference',
+           'atlas': shapes, 'stats': cases, 'model_layers': layers}
     (HERE / 'atlas_fixture.json').write_text(json.dumps(out, indent=1) + '\n')
-    print(f'{len(shapes)} shapes, {len(cases)} statistics cases')
+    print(f'{len(shapes)} shapes, {len(cases)} statistics cases, {len(layers)} model layers')
 
 
 if __name__ == '__main__':

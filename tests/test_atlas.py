@@ -49,3 +49,17 @@ def test_classification_thresholds():
 def test_compare_batches_rejects_unpaired_or_nonpositive(base, cand):
     with pytest.raises(ValueError):
         stats.compare_batches(base, cand)
+
+
+def test_model_layers_match_reference_protocol():
+    layers = workloads.model_layers()
+    assert len(layers) == len(FIXTURE['model_layers']) == 12
+    for layer, ref in zip(layers, FIXTURE['model_layers']):
+        s = layer.shape
+        got = dict(n=s.n, cin=s.cin, cout=s.cout, h=s.h, w=s.w, r=s.r, s=s.s, groups=s.groups, sh=s.sh, sw=s.sw,
+                   ph=s.ph, pw=s.pw, dh=s.dh, dw=s.dw, bias=layer.bias, model=layer.model,
+                   module_path=layer.module_path)
+        assert got == {k: ref[k] for k in got}
+        if not layer.bias:  # biased operations carry the reference's operation id, not a Shape id
+            assert s.id == ref['shape_id']
+    assert sum(layer.bias for layer in layers) == 4
