@@ -26,6 +26,7 @@
 #include "device_util.cuh"
 #include "kernel_direct.cuh"
 #include "kernel_general.cuh"
+#include "kernel_dw.cuh"
 #include "kernel_wide.cuh"
 #include "kernel_tf32x3.cuh"
 #include "kernel_small.cuh"
@@ -41,7 +42,7 @@ constexpr int kStages = 3;
 // when gc_b200_last_plan asks for it (formatting costs about a third of a
 // microsecond, a tenth of the host time of a call).
 struct PlanRecord {
-    enum Kind { kNone, kDirect, kWide, kTf32, kSmall, kGeneral } kind = kNone;
+    enum Kind { kNone, kDirect, kWide, kTf32, kSmall, kGeneral, kDw, kDwS2 } kind = kNone;
     const char *name = "";  // variant name, static storage
     bool tma = false;
     long long v[14] = {};
@@ -80,6 +81,17 @@ std::string format_plan(const PlanRecord &r) {
                       "kernel=small grid=%lld block=%lld smem=%lld ctas_per_sm=%lld cob=%lld cb=%lld items=%lld "
                       "vec=%lld stages=%lld",
                       v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7], v[8]);
+        break;
+    case PlanRecord::kDw:
+        std::snprintf(buf, sizeof(buf),
+                      "kernel=general engine=depthwise k=%lld grid=%lld block=256 smem=%lld bh=%lld bands=%lld "
+                      "pitch=%lld items=%lld",
+                      v[0], v[1], v[2], v[3], v[4], v[5], v[6]);
+        break;
+    case PlanRecord::kDwS2:
+        std::snprintf(buf, sizeof(buf),
+                      "kernel=general engine=depthwise_s2 grid=%lld block=256 cells=%lld vec_in=%lld vec_out=%lld",
+                      v[0], v[1], v[2], v[3]);
         break;
     case PlanRecord::kGeneral:
         std::snprintf(buf, sizeof(buf), "kernel=general grid=%lld block=%lld run=%lld cob=%lld index=%s runs=%lld",
@@ -947,6 +959,114 @@ int launch_small(const gc_shape *p, const float *x, const float *w, float *y, in
     return GC_OK;
 }
 
+// ---- depthwise kernel for strided, dilated and 5x5/7x7 layers ---------------------------
+constexpr size_t kDwSmemLimit = 48 * 1024;  // stage per CTA: several CTAs per SM, no opt-in
+
+// Two stages of the input rows a band of bh output rows reaches.
+size_t dw_smem(const gc_shape *p, int64_t wo, long long bh) {
+    const long long rows = (bh - 1) * p->sh + (p->r - 1) * p->dh + 1;
+    const long long pitch = (wo - 1) * p->sw + (p->s - 1) * p->dw + 1;
+    return static_cast<size_t>(2 * rows * pitch * 4);
+}
+
+// Depthwise layers (groups == Cin == Cout) with a square 3x3, 5x5 or 7x7
+// kernel whose one-output-row stage fits, and 32-bit in-plane indices.
+bool dw_eligible(const gc_shape *p, int64_t ho, int64_t wo) {
+    return p->groups == p->cin && p->cin == p->cout && p->r == p->s && (p->r == 3 || p->r == 5 || p->r == 7) &&
+           p->h * p->w < (1LL << 31) && ho * wo < (1LL << 31) && p->sh * wo < (1LL << 30) &&
+           p->dh * p->r < (1LL << 20) && p->dw * p->s < (1LL << 20) && p->ph < (1LL << 20) &&
+           p->pw < (1LL << 20) && p->cin < (1LL << 31) && dw_smem(p, wo, 1) <= kDwSmemLimit;
+}
+
+int launch_dw(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const float *w, float *y, int dev,
+              cudaStream_t stream) {
+    DeviceFacts facts;
+    int st = device_facts(dev, facts);
+    if (st != GC_OK) return st;
+    // Output rows per item: the largest band whose stage fits and that still
+    // gives every SM eight items, else the smallest that fits.
+    long long bh = 1;
+    for (long long cand : {64LL, 32LL, 16LL, 8LL, 4LL, 2LL, 1LL}) {
+        if (cand > ho || dw_smem(p, wo, cand) > kDwSmemLimit) continue;
+        bh = cand;
+        if (p->n * p->cin * ceil_div(ho, cand) >= 8LL * facts.sms) break;
+    }
+    gcb::DwParams P;
+    P.x = x;
+    P.w = w;
+    P.y = y;
+    P.n = static_cast<int>(p->n);
+    P.c = static_cast<int>(p->cin);
+    P.h = static_cast<int>(p->h);
+    P.wd = static_cast<int>(p->w);
+    P.sh = static_cast<int>(p->sh);
+    P.sw = static_cast<int>(p->sw);
+    P.ph = static_cast<int>(p->ph);
+    P.pw = static_cast<int>(p->pw);
+    P.dh = static_cast<int>(p->dh);
+    P.dw = static_cast<int>(p->dw);
+    P.ho = static_cast<int>(ho);
+    P.wo = static_cast<int>(wo);
+    P.bh = static_cast<int>(bh);
+    P.bands = static_cast<int>(ceil_div(ho, bh));
+    P.pitch = static_cast<int>((wo - 1) * p->sw + (p->s - 1) * p->dw + 1);
+    P.items = p->n * p->cin * P.bands;
+    const size_t smem = dw_smem(p, wo, bh);
+    const void *fn = p->r == 3   ? reinterpret_cast<const void *>(&gcb::dw_conv_kernel<3>)
+                     : p->r == 5 ? reinterpret_cast<const void *>(&gcb::dw_conv_kernel<5>)
+                                 : reinterpret_cast<const void *>(&gcb::dw_conv_kernel<7>);
+    int ctas = 0;
+    st = kernel_occupancy(dev, fn, 256, smem, facts.smem_optin, ctas);
+    if (st != GC_OK) return st;
+    if (ctas < 1) return gc_error(GC_UNSUPPORTED, "depthwise kernel: does not fit on an SM");
+    const int grid = static_cast<int>(std::min<long long>(P.items, static_cast<long long>(facts.sms) * ctas));
+    void *args[] = {&P};
+    cudaError_t e = launch_pdl(fn, dim3(grid), dim3(256), args, smem, stream);
+    if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+    record_plan(PlanRecord::kDw, "", false, p->r, grid, smem, bh, P.bands, P.pitch, P.items);
+    return GC_OK;
+}
+
+// Depthwise 3x3, stride 2, padding 1, dilation 1 with 32-bit in-plane indices.
+bool dw_s2_eligible(const gc_shape *p) {
+    return p->groups == p->cin && p->cin == p->cout && p->r == 3 && p->s == 3 && p->sh == 2 && p->sw == 2 &&
+           p->ph == 1 && p->pw == 1 && p->dh == 1 && p->dw == 1 && p->h * p->w < (1LL << 31) &&
+           p->w < (1LL << 29) && p->h < (1LL << 29) && p->cin < (1LL << 31);
+}
+
+int launch_dw_s2(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const float *w, float *y, int dev,
+                 cudaStream_t stream) {
+    DeviceFacts facts;
+    int st = device_facts(dev, facts);
+    if (st != GC_OK) return st;
+    gcb::DwS2Params P;
+    P.x = x;
+    P.w = w;
+    P.y = y;
+    P.n = static_cast<int>(p->n);
+    P.c = static_cast<int>(p->cin);
+    P.h = static_cast<int>(p->h);
+    P.wd = static_cast<int>(p->w);
+    P.ho = static_cast<int>(ho);
+    P.wo = static_cast<int>(wo);
+    P.qcols = static_cast<int>(ceil_div(wo, 4));
+    P.prows = static_cast<int>(ceil_div(ho, 2));
+    P.cells = p->n * p->cin * P.prows * P.qcols;
+    P.vec_in = p->w % 4 == 0 && aligned16(x);
+    P.vec_out = wo % 4 == 0 && aligned16(y);
+    const void *fn = reinterpret_cast<const void *>(&gcb::dw_s2_conv_kernel);
+    int ctas = 0;
+    st = kernel_occupancy(dev, fn, 256, 0, facts.smem_optin, ctas);
+    if (st != GC_OK) return st;
+    if (ctas < 1) return gc_error(GC_UNSUPPORTED, "stride-2 depthwise kernel: does not fit on an SM");
+    const long long blocks = std::min<long long>(ceil_div(P.cells, 256), static_cast<long long>(facts.sms) * ctas);
+    void *args[] = {&P};
+    cudaError_t e = launch_pdl(fn, dim3(static_cast<unsigned>(blocks)), dim3(256), args, 0, stream);
+    if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+    record_plan(PlanRecord::kDwS2, "", false, blocks, P.cells, P.vec_in, P.vec_out);
+    return GC_OK;
+}
+
 // ---- general kernel ------------------------------------------------------------------
 constexpr int kGeneralRun = 4;
 
@@ -958,6 +1078,8 @@ const void *general_kernel_for(bool narrow) {
 
 int launch_general(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const float *w,
                    float *y, int dev, cudaStream_t stream) {
+    if (dw_s2_eligible(p)) return launch_dw_s2(p, ho, wo, x, w, y, dev, stream);
+    if (dw_eligible(p, ho, wo)) return launch_dw(p, ho, wo, x, w, y, dev, stream);
     DeviceFacts facts;
     int st = device_facts(dev, facts);
     if (st != GC_OK) return st;

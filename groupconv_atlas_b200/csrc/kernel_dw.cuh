@@ -1,0 +1,195 @@
+// Depthwise 2-D cross-correlation (groups == Cin == Cout) for the layers the
+// 3x3/s1/p1 engine does not take: strided, dilated or wider square kernels
+// (K = 3, 5 or 7).  Implementation 0 routes such layers here instead of the
+// general kernel (reference k0, csrc/cuda/groupconv.cu:17-37, computes the
+// same sums).
+//
+// Work item = (image, channel, band of BH output rows).  A CTA stages the
+// input rows the band reaches - (BH-1)*sh + (K-1)*dh + 1 rows, the columns
+// from -pw to the last one an output touches, zero outside the image - into
+// shared memory with 4-byte asynchronous copies (one warp per row, lanes on
+// consecutive columns, zero fill outside the image), then every thread
+// computes outputs of the band from shared memory with the channel's K*K
+// weights in registers, consecutive threads on consecutive output columns
+// (coalesced stores).  Two stages alternate: the copies of a CTA's next item
+// are in flight while it computes the current one.  The per-output sum runs
+// over (r, s) in row-major order with fused multiply-adds from zero, as the
+// reference's k0 does.
+#pragma once
+#include <cstdint>
+
+#include "device_util.cuh"
+
+namespace gcb {
+
+struct DwParams {
+    const float *x;
+    const float *w;
+    float *y;
+    int n, c, h, wd;             // input
+    int sh, sw, ph, pw, dh, dw;  // geometry (kernel size is the template K)
+    int ho, wo;                  // output
+    int bh;                      // output rows per item
+    int bands;                   // ceil(ho / bh)
+    int pitch;                   // staged columns: -pw .. (wo-1)*sw + (K-1)*dw - pw
+    long long items;             // n * c * bands
+};
+
+template <int K>
+__global__ void __launch_bounds__(256) dw_conv_kernel(const __grid_constant__ DwParams P) {
+    extern __shared__ __align__(16) float tile[];  // two stages of stage_floats
+    griddep_wait();
+    griddep_launch_dependents();
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
+    const int stage_floats = ((P.bh - 1) * P.sh + (K - 1) * P.dh + 1) * P.pitch;
+    const long long plane_in = static_cast<long long>(P.h) * P.wd;
+    const long long plane_out = static_cast<long long>(P.ho) * P.wo;
+    // Issues the copies of one item's input rows into a stage (one commit group).
+    auto stage = [&](long long item, float *dst) {
+        const long long plane = item / P.bands;
+        const int band = static_cast<int>(item - plane * P.bands);
+        const int oh0 = band * P.bh;
+        const int rows_in = (min(P.bh, P.ho - oh0) - 1) * P.sh + (K - 1) * P.dh + 1;
+        const int ih0 = oh0 * P.sh - P.ph;
+        const float *xp = P.x + plane * plane_in;
+        for (int i = warp; i < rows_in; i += nwarps) {
+            const int ih = ih0 + i;
+            const bool row_in = ih >= 0 && ih < P.h;
+            const float *xr = xp + static_cast<long long>(row_in ? ih : 0) * P.wd;
+            float *tr = dst + i * P.pitch;
+            for (int j = lane; j < P.pitch; j += 32) {
+                const int iw = j - P.pw;
+                const bool in = row_in && iw >= 0 && iw < P.wd;
+                cp_async_4(tr + j, in ? xr + iw : xp, in);  // zero fill outside the image
+            }
+        }
+        cp_async_commit();
+    };
+    long long item = blockIdx.x;
+    if (item < P.items) stage(item, tile);
+    for (int k = 0; item < P.items; ++k, item += gridDim.x) {
+        const long long next = item + gridDim.x;
+        if (next < P.items) stage(next, tile + ((k + 1) & 1) * stage_floats);
+        if (next < P.items)
+            cp_async_wait<1>();  // this item's copies have landed (the next item's may not)
+        else
+            cp_async_wait<0>();
+        __syncthreads();
+        const long long plane = item / P.bands;
+        const int band = static_cast<int>(item - plane * P.bands);
+        const int c = static_cast<int>(plane % P.c);
+        const int oh0 = band * P.bh;
+        const int rows_out = min(P.bh, P.ho - oh0);
+        float wr[K * K];
+#pragma unroll
+        for (int q = 0; q < K * K; ++q) wr[q] = __ldg(P.w + static_cast<long long>(c) * (K * K) + q);
+        const float *st = tile + (k & 1) * stage_floats;
+        float *yp = P.y + plane * plane_out + static_cast<long long>(oh0) * P.wo;
+        const int outs = rows_out * P.wo;
+        for (int o = tid; o < outs; o += blockDim.x) {
+            const int orow = o / P.wo, ow = o - orow * P.wo;
+            const float *t0 = st + orow * P.sh * P.pitch + ow * P.sw;
+            float acc = 0.0f;
+#pragma unroll
+            for (int r = 0; r < K; ++r)
+#pragma unroll
+                for (int s = 0; s < K; ++s) acc = fmaf(t0[r * P.dh * P.pitch + s * P.dw], wr[r * K + s], acc);
+            yp[o] = acc;
+        }
+        __syncthreads();  // every thread is done with this stage before it is refilled
+    }
+}
+
+}  // namespace gcb
+
+namespace gcb {
+
+// Depthwise 3x3, stride 2, padding 1, dilation 1 (the downsampling layers of
+// MobileNet-style networks): a thread owns a cell of 2 output rows x 4 output
+// columns of one plane and reads the 5 x 9 input values it covers straight
+// from global memory - per input row the 8 columns 2*ow0 .. 2*ow0+7 as two
+// 16-byte loads when the row is 16-byte aligned and the cell is interior,
+// plus column 2*ow0-1 - so every input value is read about once and a warp's
+// loads are contiguous.  72 fused multiply-adds in (r, s) order per cell,
+// 16-byte stores when the output row allows.  Grid-stride over cells, columns
+// fastest.
+struct DwS2Params {
+    const float *x;
+    const float *w;
+    float *y;
+    int n, c, h, wd, ho, wo;
+    int qcols;        // ceil(wo / 4)
+    int prows;        // ceil(ho / 2)
+    long long cells;  // n * c * prows * qcols
+    int vec_in;       // input rows 16-byte aligned (wd % 4 == 0, x aligned)
+    int vec_out;      // output rows 16-byte aligned (wo % 4 == 0, y aligned)
+};
+
+__global__ void __launch_bounds__(256) dw_s2_conv_kernel(const __grid_constant__ DwS2Params P) {
+    griddep_wait();
+    griddep_launch_dependents();
+    const long long plane_in = static_cast<long long>(P.h) * P.wd;
+    const long long plane_out = static_cast<long long>(P.ho) * P.wo;
+    const long long per_plane = static_cast<long long>(P.prows) * P.qcols;
+    for (long long cell = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; cell < P.cells;
+         cell += static_cast<long long>(gridDim.x) * blockDim.x) {
+        const long long plane = cell / per_plane;
+        const int rest = static_cast<int>(cell - plane * per_plane);
+        const int pr = rest / P.qcols, qc = rest - pr * P.qcols;
+        const int oh0 = 2 * pr, ow0 = 4 * qc;
+        const int c = static_cast<int>(plane % P.c);
+        const float *xp = P.x + plane * plane_in;
+        const int iw0 = 2 * ow0;  // input column of tap s = 1 for output column ow0
+        float v[5][9];            // rows 2*oh0-1 .. 2*oh0+3, columns iw0-1 .. iw0+7
+        const bool interior = P.vec_in && iw0 + 7 < P.wd;
+#pragma unroll
+        for (int t = 0; t < 5; ++t) {
+            const int ih = 2 * oh0 - 1 + t;
+            const bool row_in = ih >= 0 && ih < P.h;
+            const float *xr = xp + static_cast<long long>(row_in ? ih : 0) * P.wd;
+            v[t][0] = row_in && iw0 >= 1 ? __ldg(xr + iw0 - 1) : 0.0f;
+            if (interior) {
+                const float4 a = row_in ? __ldg(reinterpret_cast<const float4 *>(xr + iw0)) : make_float4(0, 0, 0, 0);
+                const float4 b =
+                    row_in ? __ldg(reinterpret_cast<const float4 *>(xr + iw0 + 4)) : make_float4(0, 0, 0, 0);
+                v[t][1] = a.x; v[t][2] = a.y; v[t][3] = a.z; v[t][4] = a.w;
+                v[t][5] = b.x; v[t][6] = b.y; v[t][7] = b.z; v[t][8] = b.w;
+            } else {
+#pragma unroll
+                for (int u = 1; u < 9; ++u) {
+                    const int iw = iw0 - 1 + u;
+                    v[t][u] = row_in && iw < P.wd ? __ldg(xr + iw) : 0.0f;
+                }
+            }
+        }
+        float wr[9];
+#pragma unroll
+        for (int q = 0; q < 9; ++q) wr[q] = __ldg(P.w + static_cast<long long>(c) * 9 + q);
+        float *yp = P.y + plane * plane_out;
+#pragma unroll
+        for (int rr = 0; rr < 2; ++rr) {
+            const int oh = oh0 + rr;
+            if (oh >= P.ho) break;
+            float o[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int r = 0; r < 3; ++r)
+#pragma unroll
+                    for (int s = 0; s < 3; ++s) acc = fmaf(v[2 * rr + r][2 * q + s], wr[r * 3 + s], acc);
+                o[q] = acc;
+            }
+            float *yr = yp + static_cast<long long>(oh) * P.wo + ow0;
+            if (P.vec_out && ow0 + 3 < P.wo) {
+                *reinterpret_cast<float4 *>(yr) = make_float4(o[0], o[1], o[2], o[3]);
+            } else {
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    if (ow0 + q < P.wo) yr[q] = o[q];
+            }
+        }
+    }
+}
+
+}  // namespace gcb

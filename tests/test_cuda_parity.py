@@ -196,3 +196,46 @@ def test_tf32x3_tensor_core_path(native, torch_cuda, n, c, h, w, cpg):
     res = assert_matches(s, x, wt, y, label=f'{s} {plan}')
     assert res['max_ratio_to_bound'] < 0.5, res
     assert native.device_status(clear=True) == 0
+
+
+# Depthwise layers outside B geometry: the depthwise engine behind
+# implementation 0 (strided, dilated, 5x5 and 7x7 kernels, padding wider than
+# the kernel, wide rows whose stage limits the band height).
+DW_SHAPES = [
+    dict(n=1, cin=96, cout=96, h=112, w=112, groups=96, sh=2, sw=2),  # MobileNetV2 features.2 geometry
+    dict(n=2, cin=32, cout=32, h=57, w=61, groups=32, sh=2, sw=2),
+    dict(n=1, cin=24, cout=24, h=33, w=35, r=5, s=5, groups=24, ph=2, pw=2),
+    dict(n=2, cin=16, cout=16, h=28, w=28, r=7, s=7, groups=16, ph=3, pw=3),  # ConvNeXt geometry, no bias
+    dict(n=1, cin=16, cout=16, h=30, w=29, groups=16, dh=2, dw=2, ph=2, pw=2),
+    dict(n=1, cin=8, cout=8, h=31, w=40, groups=8, sh=3, sw=2, ph=0, pw=1),
+    dict(n=1, cin=4, cout=4, h=6, w=7, groups=4, ph=3, pw=4),
+    dict(n=1, cin=8, cout=8, h=300, w=20, r=5, s=5, groups=8, ph=2, pw=2),
+    dict(n=1, cin=2, cout=2, h=10, w=2000, groups=2, sh=2, sw=2),
+    dict(n=3, cin=5, cout=5, h=9, w=9, r=7, s=7, groups=5, sh=2, sw=2, ph=1, pw=1, dh=1, dw=1),
+    # 3x3 stride 2 (the register-blocked stride-2 engine): aligned rows, odd widths, tiny planes
+    dict(n=3, cin=8, cout=8, h=20, w=24, groups=8, sh=2, sw=2),
+    dict(n=1, cin=4, cout=4, h=1, w=1, groups=4, sh=2, sw=2),
+    dict(n=2, cin=3, cout=3, h=2, w=3, groups=3, sh=2, sw=2),
+    dict(n=1, cin=6, cout=6, h=15, w=28, groups=6, sh=2, sw=2),
+]
+
+
+@pytest.mark.parametrize('geo', DW_SHAPES, ids=lambda g: '-'.join(f'{k}{v}' for k, v in g.items()))
+@pytest.mark.parametrize('entry', ['impl0', 'general'])
+def test_depthwise_engine(native, torch_cuda, geo, entry):
+    s = Shape(**geo)
+    x, w = inputs(s)
+    if entry == 'impl0':
+        y, plan = run(native, torch_cuda, s, x, w, impl=0)
+    else:
+        y, plan = run(native, torch_cuda, s, x, w, kernel='general')
+    assert plan.startswith('kernel=general engine=depthwise'), plan
+    assert_matches(s, x, w, y, label=str(geo))
+
+
+def test_depthwise_engine_leaves_other_kernel_sizes_to_the_general_kernel(native, torch_cuda):
+    s = Shape(n=1, cin=4, cout=4, h=12, w=12, r=9, s=9, groups=4, ph=4, pw=4)
+    x, w = inputs(s)
+    y, plan = run(native, torch_cuda, s, x, w, impl=0)
+    assert plan.startswith('kernel=general grid='), plan
+    assert_matches(s, x, w, y, label='9x9 depthwise')
