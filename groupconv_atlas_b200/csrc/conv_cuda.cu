@@ -962,11 +962,17 @@ int launch_small(const gc_shape *p, const float *x, const float *w, float *y, in
 // ---- depthwise kernel for strided, dilated and 5x5/7x7 layers ---------------------------
 constexpr size_t kDwSmemLimit = 48 * 1024;  // stage per CTA: several CTAs per SM, no opt-in
 
+// Staged columns per input row: every column an output reaches, and for
+// stride 1 / dilation 1 (four outputs per thread) whole quads of outputs.
+bool dw_unit(const gc_shape *p) { return p->sw == 1 && p->dw == 1; }
+long long dw_pitch(const gc_shape *p, int64_t wo) {
+    return dw_unit(p) ? round_up(wo, 4) + p->s - 1 : (wo - 1) * p->sw + (p->s - 1) * p->dw + 1;
+}
+
 // Two stages of the input rows a band of bh output rows reaches.
 size_t dw_smem(const gc_shape *p, int64_t wo, long long bh) {
     const long long rows = (bh - 1) * p->sh + (p->r - 1) * p->dh + 1;
-    const long long pitch = (wo - 1) * p->sw + (p->s - 1) * p->dw + 1;
-    return static_cast<size_t>(2 * rows * pitch * 4);
+    return static_cast<size_t>(2 * rows * dw_pitch(p, wo) * 4);
 }
 
 // Depthwise layers (groups == Cin == Cout) with a square 3x3, 5x5 or 7x7
@@ -975,7 +981,7 @@ bool dw_eligible(const gc_shape *p, int64_t ho, int64_t wo) {
     return p->groups == p->cin && p->cin == p->cout && p->r == p->s && (p->r == 3 || p->r == 5 || p->r == 7) &&
            p->h * p->w < (1LL << 31) && ho * wo < (1LL << 31) && p->sh * wo < (1LL << 30) &&
            p->dh * p->r < (1LL << 20) && p->dw * p->s < (1LL << 20) && p->ph < (1LL << 20) &&
-           p->pw < (1LL << 20) && p->cin < (1LL << 31) && dw_smem(p, wo, 1) <= kDwSmemLimit;
+           p->pw < (1LL << 20) && p->n * p->cin * ho < (1LL << 31) && dw_smem(p, wo, 1) <= kDwSmemLimit;
 }
 
 int launch_dw(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const float *w, float *y, int dev,
@@ -1009,12 +1015,16 @@ int launch_dw(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const f
     P.wo = static_cast<int>(wo);
     P.bh = static_cast<int>(bh);
     P.bands = static_cast<int>(ceil_div(ho, bh));
-    P.pitch = static_cast<int>((wo - 1) * p->sw + (p->s - 1) * p->dw + 1);
+    P.pitch = static_cast<int>(dw_pitch(p, wo));
     P.items = p->n * p->cin * P.bands;
     const size_t smem = dw_smem(p, wo, bh);
-    const void *fn = p->r == 3   ? reinterpret_cast<const void *>(&gcb::dw_conv_kernel<3>)
-                     : p->r == 5 ? reinterpret_cast<const void *>(&gcb::dw_conv_kernel<5>)
-                                 : reinterpret_cast<const void *>(&gcb::dw_conv_kernel<7>);
+    const bool unit = dw_unit(p);
+    const void *fn = p->r == 3   ? (unit ? reinterpret_cast<const void *>(&gcb::dw_conv_kernel<3, true>)
+                                         : reinterpret_cast<const void *>(&gcb::dw_conv_kernel<3, false>))
+                     : p->r == 5 ? (unit ? reinterpret_cast<const void *>(&gcb::dw_conv_kernel<5, true>)
+                                         : reinterpret_cast<const void *>(&gcb::dw_conv_kernel<5, false>))
+                                 : (unit ? reinterpret_cast<const void *>(&gcb::dw_conv_kernel<7, true>)
+                                         : reinterpret_cast<const void *>(&gcb::dw_conv_kernel<7, false>));
     int ctas = 0;
     st = kernel_occupancy(dev, fn, 256, smem, facts.smem_optin, ctas);
     if (st != GC_OK) return st;

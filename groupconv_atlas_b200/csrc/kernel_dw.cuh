@@ -31,24 +31,25 @@ struct DwParams {
     int ho, wo;                  // output
     int bh;                      // output rows per item
     int bands;                   // ceil(ho / bh)
-    int pitch;                   // staged columns: -pw .. (wo-1)*sw + (K-1)*dw - pw
-    long long items;             // n * c * bands
+    int pitch;                   // staged columns from -pw: (wo-1)*sw + (K-1)*dw + 1, or
+                                 // ceil(wo/4)*4 + K - 1 for stride 1 and dilation 1
+    long long items;             // n * c * bands (below 2^31)
 };
 
-template <int K>
+template <int K, bool UNIT>
 __global__ void __launch_bounds__(256) dw_conv_kernel(const __grid_constant__ DwParams P) {
     extern __shared__ __align__(16) float tile[];  // two stages of stage_floats
     griddep_wait();
     griddep_launch_dependents();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nwarps = blockDim.x >> 5;
     const int stage_floats = ((P.bh - 1) * P.sh + (K - 1) * P.dh + 1) * P.pitch;
+    const int items = static_cast<int>(P.items);
     const long long plane_in = static_cast<long long>(P.h) * P.wd;
     const long long plane_out = static_cast<long long>(P.ho) * P.wo;
     // Issues the copies of one item's input rows into a stage (one commit group).
-    auto stage = [&](long long item, float *dst) {
-        const long long plane = item / P.bands;
-        const int band = static_cast<int>(item - plane * P.bands);
-        const int oh0 = band * P.bh;
+    auto stage = [&](int item, float *dst) {
+        const int plane = item / P.bands;
+        const int oh0 = (item - plane * P.bands) * P.bh;
         const int rows_in = (min(P.bh, P.ho - oh0) - 1) * P.sh + (K - 1) * P.dh + 1;
         const int ih0 = oh0 * P.sh - P.ph;
         const float *xp = P.x + plane * plane_in;
@@ -65,36 +66,61 @@ __global__ void __launch_bounds__(256) dw_conv_kernel(const __grid_constant__ Dw
         }
         cp_async_commit();
     };
-    long long item = blockIdx.x;
-    if (item < P.items) stage(item, tile);
-    for (int k = 0; item < P.items; ++k, item += gridDim.x) {
-        const long long next = item + gridDim.x;
-        if (next < P.items) stage(next, tile + ((k + 1) & 1) * stage_floats);
-        if (next < P.items)
+    int item = blockIdx.x;
+    if (item < items) stage(item, tile);
+    for (int k = 0; item < items; ++k, item += gridDim.x) {
+        const int next = item + gridDim.x;
+        if (next < items) stage(next, tile + ((k + 1) & 1) * stage_floats);
+        if (next < items)
             cp_async_wait<1>();  // this item's copies have landed (the next item's may not)
         else
             cp_async_wait<0>();
         __syncthreads();
-        const long long plane = item / P.bands;
-        const int band = static_cast<int>(item - plane * P.bands);
-        const int c = static_cast<int>(plane % P.c);
-        const int oh0 = band * P.bh;
+        const int plane = item / P.bands;
+        const int c = plane % P.c;
+        const int oh0 = (item - plane * P.bands) * P.bh;
         const int rows_out = min(P.bh, P.ho - oh0);
         float wr[K * K];
 #pragma unroll
         for (int q = 0; q < K * K; ++q) wr[q] = __ldg(P.w + static_cast<long long>(c) * (K * K) + q);
         const float *st = tile + (k & 1) * stage_floats;
         float *yp = P.y + plane * plane_out + static_cast<long long>(oh0) * P.wo;
-        const int outs = rows_out * P.wo;
-        for (int o = tid; o < outs; o += blockDim.x) {
-            const int orow = o / P.wo, ow = o - orow * P.wo;
-            const float *t0 = st + orow * P.sh * P.pitch + ow * P.sw;
-            float acc = 0.0f;
+        if constexpr (UNIT) {
+            // stride 1, dilation 1: four consecutive outputs of a row per
+            // thread, one register window of 4 + K - 1 staged values per tap
+            // row (the stage holds at least ceil(wo / 4) * 4 + K - 1 columns)
+            const int quads = (P.wo + 3) >> 2;
+            for (int g = tid; g < rows_out * quads; g += blockDim.x) {
+                const int orow = g / quads, ow0 = (g - orow * quads) * 4;
+                float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-            for (int r = 0; r < K; ++r)
+                for (int r = 0; r < K; ++r) {
+                    const float *row = st + (orow * P.sh + r * P.dh) * P.pitch + ow0;
+                    float v[4 + K - 1];
 #pragma unroll
-                for (int s = 0; s < K; ++s) acc = fmaf(t0[r * P.dh * P.pitch + s * P.dw], wr[r * K + s], acc);
-            yp[o] = acc;
+                    for (int u = 0; u < 4 + K - 1; ++u) v[u] = row[u];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j)
+#pragma unroll
+                        for (int s = 0; s < K; ++s) acc[j] = fmaf(v[j + s], wr[r * K + s], acc[j]);
+                }
+                float *yr = yp + static_cast<long long>(orow) * P.wo + ow0;
+#pragma unroll
+                for (int j = 0; j < 4; ++j)
+                    if (ow0 + j < P.wo) yr[j] = acc[j];
+            }
+        } else {
+            const int outs = rows_out * P.wo;
+            for (int o = tid; o < outs; o += blockDim.x) {
+                const int orow = o / P.wo, ow = o - orow * P.wo;
+                const float *t0 = st + orow * P.sh * P.pitch + ow * P.sw;
+                float acc = 0.0f;
+#pragma unroll
+                for (int r = 0; r < K; ++r)
+#pragma unroll
+                    for (int s = 0; s < K; ++s) acc = fmaf(t0[r * P.dh * P.pitch + s * P.dw], wr[r * K + s], acc);
+                yp[o] = acc;
+            }
         }
         __syncthreads();  // every thread is done with this stage before it is refilled
     }
