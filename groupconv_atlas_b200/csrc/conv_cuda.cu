@@ -90,8 +90,9 @@ std::string format_plan(const PlanRecord &r) {
         break;
     case PlanRecord::kDwS2:
         std::snprintf(buf, sizeof(buf),
-                      "kernel=general engine=depthwise_s2 grid=%lld block=256 cells=%lld vec_in=%lld vec_out=%lld",
-                      v[0], v[1], v[2], v[3]);
+                      "kernel=general engine=depthwise_s2 k=%lld grid=%lld block=256 cells=%lld vec_in=%lld "
+                      "vec_out=%lld",
+                      v[0], v[1], v[2], v[3], v[4]);
         break;
     case PlanRecord::kGeneral:
         std::snprintf(buf, sizeof(buf), "kernel=general grid=%lld block=%lld run=%lld cob=%lld index=%s runs=%lld",
@@ -1037,10 +1038,12 @@ int launch_dw(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const f
     return GC_OK;
 }
 
-// Depthwise 3x3, stride 2, padding 1, dilation 1 with 32-bit in-plane indices.
+// Depthwise 3x3 or 5x5, stride 2, padding K/2, dilation 1 with 32-bit
+// in-plane indices.
 bool dw_s2_eligible(const gc_shape *p) {
-    return p->groups == p->cin && p->cin == p->cout && p->r == 3 && p->s == 3 && p->sh == 2 && p->sw == 2 &&
-           p->ph == 1 && p->pw == 1 && p->dh == 1 && p->dw == 1 && p->h * p->w < (1LL << 31) &&
+    return p->groups == p->cin && p->cin == p->cout && (p->r == 3 || p->r == 5) && p->s == p->r && p->sh == 2 &&
+           p->sw == 2 && p->ph == p->r / 2 && p->pw == p->r / 2 && p->dh == 1 && p->dw == 1 &&
+           p->h * p->w < (1LL << 31) &&
            p->w < (1LL << 29) && p->h < (1LL << 29) && p->cin < (1LL << 31);
 }
 
@@ -1064,7 +1067,8 @@ int launch_dw_s2(const gc_shape *p, int64_t ho, int64_t wo, const float *x, cons
     P.cells = p->n * p->cin * P.prows * P.qcols;
     P.vec_in = p->w % 4 == 0 && aligned16(x);
     P.vec_out = wo % 4 == 0 && aligned16(y);
-    const void *fn = reinterpret_cast<const void *>(&gcb::dw_s2_conv_kernel);
+    const void *fn = p->r == 3 ? reinterpret_cast<const void *>(&gcb::dw_s2_conv_kernel<3>)
+                               : reinterpret_cast<const void *>(&gcb::dw_s2_conv_kernel<5>);
     int ctas = 0;
     st = kernel_occupancy(dev, fn, 256, 0, facts.smem_optin, ctas);
     if (st != GC_OK) return st;
@@ -1073,7 +1077,7 @@ int launch_dw_s2(const gc_shape *p, int64_t ho, int64_t wo, const float *x, cons
     void *args[] = {&P};
     cudaError_t e = launch_pdl(fn, dim3(static_cast<unsigned>(blocks)), dim3(256), args, 0, stream);
     if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
-    record_plan(PlanRecord::kDwS2, "", false, blocks, P.cells, P.vec_in, P.vec_out);
+    record_plan(PlanRecord::kDwS2, "", false, p->r, blocks, P.cells, P.vec_in, P.vec_out);
     return GC_OK;
 }
 

@@ -217,6 +217,10 @@ DW_SHAPES = [
     dict(n=1, cin=4, cout=4, h=1, w=1, groups=4, sh=2, sw=2),
     dict(n=2, cin=3, cout=3, h=2, w=3, groups=3, sh=2, sw=2),
     dict(n=1, cin=6, cout=6, h=15, w=28, groups=6, sh=2, sw=2),
+    # 5x5 stride 2 padding 2 (EfficientNet / MobileNetV3 downsampling geometry)
+    dict(n=2, cin=16, cout=16, h=28, w=28, r=5, s=5, groups=16, sh=2, sw=2, ph=2, pw=2),
+    dict(n=1, cin=8, cout=8, h=19, w=36, r=5, s=5, groups=8, sh=2, sw=2, ph=2, pw=2),
+    dict(n=1, cin=4, cout=4, h=3, w=5, r=5, s=5, groups=4, sh=2, sw=2, ph=2, pw=2),
 ]
 
 
