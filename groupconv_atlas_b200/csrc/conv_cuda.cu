@@ -73,8 +73,8 @@ std::string format_plan(const PlanRecord &r) {
     case PlanRecord::kTf32:
         std::snprintf(buf, sizeof(buf),
                       "kernel=tf32x3 engine=tcgen05 n_cta=%lld block=320 smem=%lld M=%lld N=%lld nb=%lld sp=%lld "
-                      "strips=%lld items=%lld chunks=%lld rows_b=%lld",
-                      v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7], v[8], v[9]);
+                      "strips=%lld items=%lld chunks=%lld rows_b=%lld ks=%lld",
+                      v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7], v[8], v[9], v[10]);
         break;
     case PlanRecord::kSmall:
         std::snprintf(buf, sizeof(buf),
@@ -801,8 +801,9 @@ int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
     // 64-channel groups of large planes (one image per block), whose weight
     // tiles are the largest, gain from it (measured); narrower groups and
     // stacked small images keep one strip per item.
-    long long best_nb = 1, best_items = 0, best_strips = 0;
+    long long best_nb = 1, best_items = 0, best_strips = 0, best_ks = 1;
     int best_sp = 1;
+    const long long chunks = cpg / 8;
     double best_cost = -1.0;
     for (int sp = 1; sp <= (co == 64 ? 2 : 1); ++sp) {
         if (!tf32_fits(cpg, W, sp, limit)) continue;
@@ -814,13 +815,26 @@ int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
             const long long strips = ceil_div(out_rows * wp, sp * gcb::kTf32N);
             const long long items = static_cast<long long>(p->groups) * co_blocks * ceil_div(N, nb) * strips;
             if (items >= (1LL << 31)) continue;
-            const double cost = static_cast<double>(ceil_div(items, facts.sms)) * sp * (sp == 2 ? 0.87 : 1.0);
+            // Too few output tiles for the GPU: split the input channels
+            // into the most parts (dividing the chunks) that still fit one
+            // wave, so that the serial chain of steps per CTA shrinks.
+            long long ks = 1;
+            if (sp == 1 && 2 * items <= facts.sms)
+                for (long long d = chunks; d > 1; --d)
+                    if (chunks % d == 0 && items * d <= facts.sms) {
+                        ks = d;
+                        break;
+                    }
+            // estimated time: waves of items x steps per item
+            const double cost = static_cast<double>(ceil_div(items * ks, facts.sms)) * (chunks / ks) * sp *
+                                (sp == 2 ? 0.87 : 1.0);
             if (best_cost < 0.0 || cost < best_cost - 1e-9) {
                 best_cost = cost;
                 best_nb = nb;
-                best_items = items;
+                best_items = items * ks;
                 best_strips = strips;
                 best_sp = sp;
+                best_ks = ks;
             }
         }
     }
@@ -842,7 +856,8 @@ int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
     P.sp = best_sp;
     P.strips = static_cast<int>(best_strips);
     P.items = static_cast<int>(best_items);
-    P.chunks = static_cast<int>(cpg / 8);
+    P.chunks = static_cast<int>(chunks / best_ks);
+    P.ksplit = static_cast<int>(best_ks);
     P.m = 2 * co > 64 ? 128 : 64;
     P.rows_b = static_cast<int>(rows_b);
     P.a_bytes = static_cast<unsigned>(9 * P.m * 32);
@@ -872,10 +887,25 @@ int launch_tf32(const gc_shape *p, const float *x, const float *w, float *y, int
     st = encode_rows_map(wmap, w, p->cout, (p->cin / p->groups) * 9, 72, plan.P.cpg / plan.P.co_blocks);
     if (st != GC_OK) return st;
     void *args[] = {&plan.P, &wmap};
-    cudaError_t e = launch_pdl(plan.fn, dim3(plan.grid), dim3(gcb::kTf32Threads), args, plan.smem, stream);
+    cudaError_t e;
+    if (plan.P.ksplit == 1) {
+        e = launch_pdl(plan.fn, dim3(plan.grid), dim3(gcb::kTf32Threads), args, plan.smem, stream);
+    } else {
+        // The parts of the input channels add into y: zero it first (a plain
+        // stream-ordered launch follows the memset).
+        e = cudaMemsetAsync(y, 0, static_cast<size_t>(p->n * p->cout * p->h * p->w) * sizeof(float), stream);
+        if (e == cudaSuccess) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(plan.grid);
+            cfg.blockDim = dim3(gcb::kTf32Threads);
+            cfg.dynamicSmemBytes = plan.smem;
+            cfg.stream = stream;
+            e = cudaLaunchKernelExC(&cfg, plan.fn, args);
+        }
+    }
     if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
     record_plan(PlanRecord::kTf32, "", false, plan.grid, plan.smem, plan.P.m, gcb::kTf32N, plan.P.nb, plan.P.sp,
-                plan.P.strips, plan.P.items, plan.P.chunks, plan.P.rows_b);
+                plan.P.strips, plan.P.items, plan.P.chunks, plan.P.rows_b, plan.P.ksplit);
     return GC_OK;
 }
 

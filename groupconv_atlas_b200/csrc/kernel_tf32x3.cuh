@@ -28,8 +28,10 @@
 // second half w_lo of the same channels, so the epilogue adds the two parts
 // with one warp shuffle.
 //
-// Work item = (output-channel block, image block, strip of sp * 256 pixels);
-// pipeline step =
+// Work item = (output-channel block, image block, strip of sp * 256 pixels,
+// part of the input channels); layers with too few output tiles to fill the
+// GPU split the input channels into ksplit parts whose partial sums are added
+// into the zeroed output, all other layers have ksplit = 1.  Pipeline step =
 // (item, chunk of 8 input channels).  Per step:
 //   - the converter warps load the step's pixels from global memory into
 //     registers (per thread its own pixel rows, 8 coalesced channel loads
@@ -74,8 +76,11 @@ struct Tf32Params {
     int sp;              // 256-pixel strips per item: 1 (two accumulator sets alternate between
                          // items) or 2 (one set holding both strips)
     int strips;          // items per block: ceil(out_rows * wp / (sp * 256))
-    int items;           // groups * co_blocks * blocks * strips
-    int chunks;          // cpg / 8
+    int items;           // groups * co_blocks * blocks * strips * ksplit
+    int chunks;          // 8-channel steps per item: cpg / 8 / ksplit
+    int ksplit;          // parts the input channels of an output tile are split into: 1, or (layers
+                         // with too few tiles to fill the GPU) several items whose partial sums are
+                         // added into y, zeroed before the launch
     int m;               // MMA M: 128 when CO > 32, else 64
     int rows_b;          // pixel rows per step: sp*256 + 2*wp + 2, rounded up to 8 (<= kTf32MaxRows)
     unsigned a_bytes;    // one step's weight tiles: 9 taps * m * 32
@@ -222,11 +227,16 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, i
         : "memory");
 }
 
-// Item order: strip fastest, then image block, then output-channel block of
-// a group, group slowest.  gq = group * co_blocks + block: the item's weights
-// and outputs are channels gq*CO .. gq*CO+CO-1, its inputs the group's.
-__device__ __forceinline__ void tf32_decode(const Tf32Params &P, int item, int &gq, int &blk, int &strip) {
-    const unsigned u = static_cast<unsigned>(item);
+// Item order: input-channel split fastest, then strip, then image block,
+// then output-channel block of a group, group slowest.  gq = group *
+// co_blocks + block: the item's weights and outputs are channels gq*CO ..
+// gq*CO+CO-1, its inputs the group's 8-channel chunks split*chunks ..
+// (split+1)*chunks-1.
+__device__ __forceinline__ void tf32_decode(const Tf32Params &P, int item, int &gq, int &blk, int &strip,
+                                            int &split) {
+    const unsigned u0 = static_cast<unsigned>(item);
+    const unsigned u = u0 / static_cast<unsigned>(P.ksplit);
+    split = static_cast<int>(u0 - u * static_cast<unsigned>(P.ksplit));
     const unsigned t = u / static_cast<unsigned>(P.strips);
     strip = static_cast<int>(u - t * static_cast<unsigned>(P.strips));
     gq = static_cast<int>(t / static_cast<unsigned>(P.blocks));
@@ -297,8 +307,8 @@ template <int M, int CO>
 __device__ __forceinline__ void tf32_epilogue(const Tf32Params &P, uint32_t acc, int item, int sub, int warp,
                                               int lane, float *ep) {
     constexpr int HALF = M / 8;  // output channels per lane quadrant
-    int g, blk, strip;
-    tf32_decode(P, item, g, blk, strip);
+    int g, blk, strip, split;
+    tf32_decode(P, item, g, blk, strip, split);
     const int quad = warp & 3, colhalf = warp >> 2;
     if (quad * HALF >= CO) return;  // quadrant holds only zero rows (warp-uniform)
     const int nco = min(HALF, CO - quad * HALF);
@@ -329,7 +339,12 @@ __device__ __forceinline__ void tf32_epilogue(const Tf32Params &P, uint32_t acc,
         const int img = blk * P.nb + k;
         if (o < out_px && hh < P.h && col < P.wd && img < P.n) {
             float *yp = ych + img * image_floats + static_cast<long long>(hh) * P.wd + col;
-            for (int j = 0; j < nco; ++j) st_stream(yp + j * hw, ep[j * 33 + lane]);
+            if (P.ksplit == 1) {
+                for (int j = 0; j < nco; ++j) st_stream(yp + j * hw, ep[j * 33 + lane]);
+            } else {
+                // a part of the input channels: add into the zeroed output
+                for (int j = 0; j < nco; ++j) atomicAdd(yp + j * hw, ep[j * 33 + lane]);
+            }
         }
         __syncwarp();
     }
@@ -396,10 +411,10 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
                     released = k - 2;
                 }
                 const int item_k = k / P.chunks, chunk = k - item_k * P.chunks;
-                int g, blk, strip;
-                tf32_decode(P, first + item_k * stride, g, blk, strip);
+                int g, blk, strip, split;
+                tf32_decode(P, first + item_k * stride, g, blk, strip, split);
                 mbar_arrive_expect_tx(&w_full[s], P.wraw_bytes);
-                tma_load_2d(wraw0 + s * P.wraw_bytes, &wmap, chunk * 72, g * CO, &w_full[s]);
+                tma_load_2d(wraw0 + s * P.wraw_bytes, &wmap, (split * P.chunks + chunk) * 72, g * CO, &w_full[s]);
                 issued = k;
             }
             // Loads still in flight must land before the CTA's shared memory
@@ -490,18 +505,18 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
             return true;
         };
         // Load side: the item whose row geometry is cached.
-        int load_item = -1, load_g = 0;
+        int load_item = -1, load_g = 0, load_split = 0;
         RowGeom<ROWS> lgm{};
         auto load = [&](int j, float (&buf)[ROWS][8]) {  // step j's pixel rows into buf
             if (j >= steps) return;
             const int item_j = j / P.chunks, chunk_j = j - item_j * P.chunks;
             if (item_j != load_item) {
                 int blk, strip;
-                tf32_decode(P, first + item_j * stride, load_g, blk, strip);
+                tf32_decode(P, first + item_j * stride, load_g, blk, strip, load_split);
                 lgm = tf32_rows<ROWS>(P, blk, strip, ctid);
                 load_item = item_j;
             }
-            tf32_load_rows<ROWS>(P, load_g, chunk_j, lgm, buf);
+            tf32_load_rows<ROWS>(P, load_g, load_split * P.chunks + chunk_j, lgm, buf);
         };
         // One pipeline step: wait for the stage, convert the weights and the
         // rows held in buf, publish, refill buf with step k+2, and run a due

@@ -2,6 +2,8 @@
 the same seeded inputs.  Acceptance per output element:
 |y - y_fp64| <= 1e-5 * sum|x*w| (FP64 oracle), plus the reference's own gates
 (1e-4 atol/rtol vs its FP32 output, 64 FP64 points)."""
+import re
+
 import numpy as np
 import pytest
 
@@ -195,6 +197,29 @@ def test_tf32x3_tensor_core_path(native, torch_cuda, n, c, h, w, cpg):
     assert plan.startswith('kernel=tf32x3'), plan
     res = assert_matches(s, x, wt, y, label=f'{s} {plan}')
     assert res['max_ratio_to_bound'] < 0.5, res
+    assert native.device_status(clear=True) == 0
+
+
+# Layers with too few output tiles to fill the GPU: the input channels are
+# split over several CTAs whose partial sums add into the zeroed output.
+SPLIT_SHAPES = [(1, 256, 7, 7, 256), (1, 256, 14, 14, 256), (1, 64, 7, 7, 64), (1, 128, 12, 13, 128),
+                (2, 32, 6, 9, 32), (32, 256, 7, 7, 256)]
+
+
+@pytest.mark.parametrize('n,c,h,w,cpg', SPLIT_SHAPES)
+@pytest.mark.parametrize('entry', ['impl3', 'tf32x3'])
+def test_tf32x3_input_channel_split(native, torch_cuda, n, c, h, w, cpg, entry):
+    s = Shape(n=n, cin=c, cout=c, h=h, w=w, groups=c // cpg)
+    x, wt = inputs(s, 5)
+    for _ in range(2):  # the output is zeroed by every call, not only the first
+        if entry == 'impl3':
+            y, plan = run(native, torch_cuda, s, x, wt, impl=3, sentinel=True)
+        else:
+            y, plan = run(native, torch_cuda, s, x, wt, kernel='tf32x3', sentinel=True)
+        assert plan.startswith('kernel=tf32x3'), plan
+        assert int(re.search(r'\bks=(\d+)', plan).group(1)) > 1, plan
+        res = assert_matches(s, x, wt, y, label=f'{s} {plan}')
+        assert res['max_ratio_to_bound'] < 0.5, res
     assert native.device_status(clear=True) == 0
 
 
