@@ -90,9 +90,9 @@ std::string format_plan(const PlanRecord &r) {
         break;
     case PlanRecord::kDwS2:
         std::snprintf(buf, sizeof(buf),
-                      "kernel=general engine=depthwise_s2 k=%lld grid=%lld block=256 cells=%lld vec_in=%lld "
-                      "vec_out=%lld",
-                      v[0], v[1], v[2], v[3], v[4]);
+                      "kernel=general engine=depthwise_cells k=%lld stride=%lld grid=%lld block=256 cells=%lld "
+                      "vec_in=%lld vec_out=%lld",
+                      v[0], v[5], v[1], v[2], v[3], v[4]);
         break;
     case PlanRecord::kGeneral:
         std::snprintf(buf, sizeof(buf), "kernel=general grid=%lld block=%lld run=%lld cob=%lld index=%s runs=%lld",
@@ -1068,11 +1068,12 @@ int launch_dw(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const f
     return GC_OK;
 }
 
-// Depthwise 3x3 or 5x5, stride 2, padding K/2, dilation 1 with 32-bit
-// in-plane indices.
+// Depthwise 3x3 or 5x5, stride 2 (or 3x3 stride 1), padding K/2, dilation
+// 1 with 32-bit in-plane indices.
 bool dw_s2_eligible(const gc_shape *p) {
-    return p->groups == p->cin && p->cin == p->cout && (p->r == 3 || p->r == 5) && p->s == p->r && p->sh == 2 &&
-           p->sw == 2 && p->ph == p->r / 2 && p->pw == p->r / 2 && p->dh == 1 && p->dw == 1 &&
+    const bool s2 = p->sh == 2 && p->sw == 2, s1 = p->sh == 1 && p->sw == 1 && p->r == 3;
+    return p->groups == p->cin && p->cin == p->cout && (p->r == 3 || p->r == 5) && p->s == p->r && (s1 || s2) &&
+           p->ph == p->r / 2 && p->pw == p->r / 2 && p->dh == 1 && p->dw == 1 &&
            p->h * p->w < (1LL << 31) &&
            p->w < (1LL << 29) && p->h < (1LL << 29) && p->cin < (1LL << 31);
 }
@@ -1094,11 +1095,13 @@ int launch_dw_s2(const gc_shape *p, int64_t ho, int64_t wo, const float *x, cons
     P.wo = static_cast<int>(wo);
     P.qcols = static_cast<int>(ceil_div(wo, 4));
     P.prows = static_cast<int>(ceil_div(ho, 2));
+    const int stride = static_cast<int>(p->sh);
     P.cells = p->n * p->cin * P.prows * P.qcols;
     P.vec_in = p->w % 4 == 0 && aligned16(x);
     P.vec_out = wo % 4 == 0 && aligned16(y);
-    const void *fn = p->r == 3 ? reinterpret_cast<const void *>(&gcb::dw_s2_conv_kernel<3>)
-                               : reinterpret_cast<const void *>(&gcb::dw_s2_conv_kernel<5>);
+    const void *fn = stride == 1  ? reinterpret_cast<const void *>(&gcb::dw_s2_conv_kernel<3, 1>)
+                     : p->r == 3 ? reinterpret_cast<const void *>(&gcb::dw_s2_conv_kernel<3, 2>)
+                                 : reinterpret_cast<const void *>(&gcb::dw_s2_conv_kernel<5, 2>);
     int ctas = 0;
     st = kernel_occupancy(dev, fn, 256, 0, facts.smem_optin, ctas);
     if (st != GC_OK) return st;
@@ -1107,7 +1110,7 @@ int launch_dw_s2(const gc_shape *p, int64_t ho, int64_t wo, const float *x, cons
     void *args[] = {&P};
     cudaError_t e = launch_pdl(fn, dim3(static_cast<unsigned>(blocks)), dim3(256), args, 0, stream);
     if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
-    record_plan(PlanRecord::kDwS2, "", false, p->r, blocks, P.cells, P.vec_in, P.vec_out);
+    record_plan(PlanRecord::kDwS2, "", false, p->r, blocks, P.cells, P.vec_in, P.vec_out, stride);
     return GC_OK;
 }
 
@@ -1258,6 +1261,14 @@ int run_kernel(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_ten
 int auto_kernel(const gc_shape *p, const gc_tensor *x, const gc_tensor *w) {
     const long long cpg = p->cin / p->groups;
     if (cpg >= 16 && tf32_eligible(p, x->data, w->data)) return GC_B200_TF32X3;
+    // Depthwise layers of little work - planes of at most 256 pixels, or at
+    // most 256K outputs in all, but not the very smallest (under 32K outputs,
+    // where the small-image kernel's launch is cheaper) - run on the
+    // register-cell kernel behind the general family (measured: N32 C256 7x7
+    // 3.2 vs 6.2 us, 14x14 7.9 vs 13.5 us, N1 C256 28x28 2.3 vs 3.0 us).
+    const long long outs = p->n * p->cout * p->h * p->w;
+    if (cpg == 1 && dw_s2_eligible(p) && outs >= (32LL << 10) && (p->h * p->w <= 256 || outs <= (256LL << 10)))
+        return GC_B200_GENERAL;
     // Small planes that the TMA tiles cannot stage (or that are narrower than
     // a TMA tile's halo) run whole planes per CTA.
     if (small_eligible(p) && (!tma_eligible(p, x->data) || p->w <= 16)) return GC_B200_SMALL;

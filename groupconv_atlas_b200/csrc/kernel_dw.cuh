@@ -130,16 +130,16 @@ __global__ void __launch_bounds__(256) dw_conv_kernel(const __grid_constant__ Dw
 
 namespace gcb {
 
-// Depthwise KxK (K = 3 or 5), stride 2, padding K/2, dilation 1 (the
-// downsampling layers of MobileNet- and EfficientNet-style networks): a
-// thread owns a cell of 2 output rows x 4 output columns of one plane and
-// reads the (K+2) x (K+6) input values it covers straight from global memory
-// - per input row the 8 columns 2*ow0 .. 2*ow0+7 as two 16-byte loads when
-// the row is 16-byte aligned and the cell is interior, and the K-2 columns
-// either side one by one - so every input value is read about once and a
-// warp's loads are contiguous.  8*K*K fused multiply-adds in (r, s) order per
-// cell, 16-byte stores when the output row allows.  Grid-stride over cells,
-// columns fastest.
+// Depthwise KxK (K = 3 or 5), stride S (1 or 2), padding K/2, dilation 1
+// (the downsampling layers of MobileNet- and EfficientNet-style networks at
+// S = 2; small planes at S = 1): a thread owns a cell of 2 output rows x 4
+// output columns of one plane and reads the (S+K) x (3S+K) input values it
+// covers straight from global memory - per input row the 4S columns S*ow0 ..
+// S*ow0+4S-1 as 16-byte loads when the row is 16-byte aligned and the cell is
+// interior, and the columns either side one by one - so every input value is
+// read about once and a warp's loads are contiguous.  8*K*K fused
+// multiply-adds in (r, s) order per cell, 16-byte stores when the output row
+// allows.  Grid-stride over cells, columns fastest.
 struct DwS2Params {
     const float *x;
     const float *w;
@@ -152,11 +152,12 @@ struct DwS2Params {
     int vec_out;      // output rows 16-byte aligned (wo % 4 == 0, y aligned)
 };
 
-template <int K>
+template <int K, int S>
 __global__ void __launch_bounds__(256) dw_s2_conv_kernel(const __grid_constant__ DwS2Params P) {
     constexpr int PAD = K / 2;      // padding of the layer
-    constexpr int ROWS = K + 2;     // input rows of a cell
-    constexpr int COLS = K + 6;     // input columns of a cell: 2*ow0 - PAD .. 2*ow0 + 5 + K - PAD
+    constexpr int ROWS = S + K;     // input rows of a cell
+    constexpr int COLS = 3 * S + K; // input columns of a cell: S*ow0 - PAD .. S*ow0 + 3S + K - 1 - PAD
+    constexpr int NV = 4 * S;       // aligned middle columns, loaded 4 at a time
     griddep_wait();
     griddep_launch_dependents();
     const long long plane_in = static_cast<long long>(P.h) * P.wd;
@@ -170,25 +171,29 @@ __global__ void __launch_bounds__(256) dw_s2_conv_kernel(const __grid_constant__
         const int oh0 = 2 * pr, ow0 = 4 * qc;
         const int c = static_cast<int>(plane % P.c);
         const float *xp = P.x + plane * plane_in;
-        const int iw0 = 2 * ow0;      // the cell's 16-byte aligned input column
+        const int iw0 = S * ow0;      // the cell's 16-byte aligned input column
         const int col0 = iw0 - PAD;   // input column of v[.][0]
         float v[ROWS][COLS];
-        const bool interior = P.vec_in && col0 >= 0 && iw0 + 8 + (K - 2 - PAD) <= P.wd;
+        const bool interior = P.vec_in && col0 >= 0 && col0 + COLS <= P.wd;
 #pragma unroll
         for (int t = 0; t < ROWS; ++t) {
-            const int ih = 2 * oh0 - PAD + t;
+            const int ih = S * oh0 - PAD + t;
             const bool row_in = ih >= 0 && ih < P.h;
             const float *xr = xp + static_cast<long long>(row_in ? ih : 0) * P.wd;
             if (interior) {
-                const float4 a = row_in ? __ldg(reinterpret_cast<const float4 *>(xr + iw0)) : make_float4(0, 0, 0, 0);
-                const float4 b =
-                    row_in ? __ldg(reinterpret_cast<const float4 *>(xr + iw0 + 4)) : make_float4(0, 0, 0, 0);
-                v[t][PAD + 0] = a.x; v[t][PAD + 1] = a.y; v[t][PAD + 2] = a.z; v[t][PAD + 3] = a.w;
-                v[t][PAD + 4] = b.x; v[t][PAD + 5] = b.y; v[t][PAD + 6] = b.z; v[t][PAD + 7] = b.w;
+#pragma unroll
+                for (int q4 = 0; q4 < NV / 4; ++q4) {
+                    const float4 a =
+                        row_in ? __ldg(reinterpret_cast<const float4 *>(xr + iw0 + 4 * q4)) : make_float4(0, 0, 0, 0);
+                    v[t][PAD + 4 * q4 + 0] = a.x;
+                    v[t][PAD + 4 * q4 + 1] = a.y;
+                    v[t][PAD + 4 * q4 + 2] = a.z;
+                    v[t][PAD + 4 * q4 + 3] = a.w;
+                }
 #pragma unroll
                 for (int u = 0; u < PAD; ++u) v[t][u] = row_in ? __ldg(xr + col0 + u) : 0.0f;
 #pragma unroll
-                for (int u = PAD + 8; u < COLS; ++u) v[t][u] = row_in ? __ldg(xr + col0 + u) : 0.0f;
+                for (int u = PAD + NV; u < COLS; ++u) v[t][u] = row_in ? __ldg(xr + col0 + u) : 0.0f;
             } else {
 #pragma unroll
                 for (int u = 0; u < COLS; ++u) {
@@ -212,7 +217,7 @@ __global__ void __launch_bounds__(256) dw_s2_conv_kernel(const __grid_constant__
 #pragma unroll
                 for (int r = 0; r < K; ++r)
 #pragma unroll
-                    for (int s = 0; s < K; ++s) acc = fmaf(v[2 * rr + r][2 * q + s], wr[r * K + s], acc);
+                    for (int s = 0; s < K; ++s) acc = fmaf(v[S * rr + r][S * q + s], wr[r * K + s], acc);
                 o[q] = acc;
             }
             float *yr = yp + static_cast<long long>(oh) * P.wo + ow0;
