@@ -539,7 +539,28 @@ def end_to_end(args, native, shape, units, xh, wh, torch, api, shard):
     consistent = bool(torch.equal(yh, dys[(2 + args.e2e_steps) & 1].cpu()))
     step_bytes = 4 * (math.prod(shape.input) + math.prod(shape.weight) + math.prod(shape.output))
     job_bytes = shard.sum_over_ranks(step_bytes)
-    return {'value': job_bytes * args.e2e_steps / (ms / 1e3) / 1e9, 'unit': UNIT,
+    # The link's bound: the same bytes copied in both directions at once
+    # (the step's input host->device while its output goes device->host),
+    # with no convolution.
+    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    c0.record(s_in)
+    for _ in range(5):
+        s_out.wait_event(c0)
+        with torch.cuda.stream(s_in):
+            dxs[0].copy_(xh, non_blocking=True)
+        with torch.cuda.stream(s_out):
+            yh.copy_(dys[0], non_blocking=True)
+        s_in.wait_stream(s_out)
+    c1.record(s_in)
+    torch.cuda.synchronize()
+    link_ms = shard.max_over_ranks(c0.elapsed_time(c1) / 5)
+    bound = job_bytes / (link_ms / 1e3) / 1e9
+    e2e_value = job_bytes * args.e2e_steps / (ms / 1e3) / 1e9
+    return {'value': e2e_value, 'unit': UNIT,
+            'link_bound': {'value': bound, 'unit': UNIT, 'frac': e2e_value / bound, 'ms_per_step': link_ms,
+                           'what': 'the step\'s input host->device and output device->host copied at once '
+                                   '(pinned), no convolution'},
             'h2d_bytes_per_step': 4 * (math.prod(shape.input) + math.prod(shape.weight)),
             'd2h_bytes_per_step': 4 * math.prod(shape.output), 'steps': args.e2e_steps,
             'ms_per_step': ms / args.e2e_steps, 'chunks': len(bounds),
