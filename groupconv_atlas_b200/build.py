@@ -75,6 +75,45 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
     return LIBRARY
 
 
+TORCH_EXT_SOURCE = PACKAGE / 'torch_ext' / 'conv_op.cpp'
+
+
+def torch_ext_path() -> Path:
+    """The PyTorch binding's extension module next to this file."""
+    import sysconfig
+    return PACKAGE / ('_gcb_torch' + sysconfig.get_config_var('EXT_SUFFIX'))
+
+
+def build_torch_ext(force: bool = False, verbose: bool = False) -> Path:
+    """Compile the PyTorch front end (torch_ext/conv_op.cpp, a thin C++ caller
+    of gc_cuda_conv that allocates the output with PyTorch) against the
+    in-tree library, when it is older than its sources."""
+    import sysconfig
+    import torch
+    from torch.utils import cpp_extension
+    target = torch_ext_path()
+    deps = [TORCH_EXT_SOURCE, INCLUDE / 'groupconv.h', LIBRARY, Path(__file__)]
+    if not force and target.exists() and all(d.stat().st_mtime <= target.stat().st_mtime for d in deps):
+        return target
+    cuda_include = Path(nvcc()).resolve().parent.parent / 'include'
+    torch_lib = cpp_extension.library_paths()[0]
+    abi = int(torch.compiled_with_cxx11_abi())
+    cmd = ['g++', '-O2', '-std=c++17', '-shared', '-fPIC', f'-D_GLIBCXX_USE_CXX11_ABI={abi}',
+           '-DTORCH_EXTENSION_NAME=_gcb_torch', '-DTORCH_API_INCLUDE_EXTENSION_H',
+           *[f'-I{d}' for d in cpp_extension.include_paths()], f'-I{sysconfig.get_paths()["include"]}',
+           f'-I{cuda_include}', f'-I{INCLUDE}', str(TORCH_EXT_SOURCE),
+           f'-L{PACKAGE}', '-lgroupconv', f'-L{torch_lib}', '-lc10', '-lc10_cuda', '-ltorch', '-ltorch_cpu',
+           '-ltorch_python', f'-Wl,-rpath,$ORIGIN', f'-Wl,-rpath,{torch_lib}', '-o', str(target) + '.part']
+    if verbose:
+        print(' '.join(cmd), flush=True)
+    result = subprocess.run(cmd, capture_output=True, text=True)
+    if result.returncode != 0:
+        sys.stderr.write(result.stdout + result.stderr)
+        raise RuntimeError(f'g++ failed with exit code {result.returncode}')
+    Path(str(target) + '.part').replace(target)
+    return target
+
+
 def main(argv=None) -> int:
     parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     parser.add_argument('--force', action='store_true')

@@ -48,3 +48,36 @@ def test_mobilenet_block_substitution(native, torch_cuda):
         again = cand(x)
     torch.cuda.synchronize()
     assert torch.equal(again, out)
+
+
+def test_cpp_front_end_reports_status_like_the_c_abi(native):
+    """Both host paths of the module turn a rejected call into NativeError with
+    the library's status (a CPU tensor is not CUDA device memory: GC_INVALID)."""
+    from groupconv_atlas_b200 import api
+    conv = torch.nn.Conv2d(4, 4, 3, padding=1, groups=4, bias=False)
+    x = torch.randn(1, 4, 6, 6)
+    for cpp in (True, False):
+        mod = torch_module.B200Conv2d(conv, native, cpp=cpp)
+        if cpp:
+            assert mod._op is not None, 'C++ front end not built'
+        with pytest.raises(api.NativeError) as err:
+            mod(x)
+        assert err.value.status == 1
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize('geo', [dict(c=144, h=56, stride=1), dict(c=96, h=112, stride=2), dict(c=64, h=28, stride=1)])
+def test_cpp_front_end_matches_ctypes_path(native, torch_cuda, geo):
+    """The C++ front end and the ctypes path launch the same kernel: identical outputs."""
+    torch.manual_seed(4)
+    conv = torch.nn.Conv2d(geo['c'], geo['c'], 3, stride=geo['stride'], padding=1, groups=geo['c'] // 8 if geo['c'] == 64 else geo['c'],
+                           bias=False).cuda()
+    x = torch.randn(2, geo['c'], geo['h'], geo['h'], device='cuda')
+    impl = 3 if geo['stride'] == 1 else 0  # implementations 1-3 take B geometry only
+    with torch.inference_mode():
+        a = torch_module.B200Conv2d(conv, native, implementation=impl, cpp=True)(x)
+        b = torch_module.B200Conv2d(conv, native, implementation=impl, cpp=False)(x)
+        ref = torch.nn.functional.conv2d(x, conv.weight, stride=geo['stride'], padding=1, groups=conv.groups)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
+    assert orc.error_metrics(a.cpu().numpy(), ref.cpu().numpy())['passed']
