@@ -394,31 +394,48 @@ int choose_pitch(int W, int qcols, int cw, int rblocks, int vr, int rows, int ce
     int best = base, best_cost = 1 << 30;
     for (int p = base; p <= base + 60; p += 4) {
         if (tma && p > 256) break;
-        // exact per-lane addresses: channel block, row block (rb * vr rows), quad
+        // exact per-lane addresses: channel block, row block (rb * vr rows),
+        // quad, in the kernel's cell order (make_cell: quad fastest for
+        // depthwise, row block fastest for grouped layers)
         const int warps = std::min((cells + 31) / 32, 8);
         int cost = 0;
         for (int wp = 0; wp < warps; ++wp) {
             long long addr[32];
             for (int lane = 0; lane < 32; ++lane) {
                 const int cell = std::min(wp * 32 + lane, cells - 1);
-                const int q = cell % qcols, rbc = cell / qcols;
-                const int rb = rbc % rblocks, cbk = rbc / rblocks;
+                int q, rb, cbk;
+                if (cpg == 1) {
+                    q = cell % qcols;
+                    rb = (cell / qcols) % rblocks;
+                    cbk = cell / qcols / rblocks;
+                } else {
+                    rb = cell % rblocks;
+                    q = (cell / rblocks) % qcols;
+                    cbk = cell / rblocks / qcols;
+                }
                 const int g = cbk * cob / cpg;
                 addr[lane] = ((static_cast<long long>(g) * cpg * rows + rb * vr) * p + q * cw + 4) * 4;
             }
-            int worst = 0;
-            for (int bank = 0; bank < 8; ++bank) {
-                long long seen[32];
-                int n = 0;
-                for (int lane = 0; lane < 32; ++lane) {
-                    if ((addr[lane] / 16) % 8 != bank) continue;
-                    bool dup = false;
-                    for (int i = 0; i < n; ++i) dup |= seen[i] == addr[lane];
-                    if (!dup) seen[n++] = addr[lane];
+            // Depthwise (4-byte loads): the warp's distinct addresses per
+            // 16-byte bank group.  Grouped layers (16-byte loads, served in
+            // four phases of 8 lanes): per phase, the most distinct addresses
+            // in one bank group, summed over the phases.
+            const int phases = cpg == 1 ? 1 : 4, width = 32 / phases;
+            for (int ph = 0; ph < phases; ++ph) {
+                int worst = 0;
+                for (int bank = 0; bank < 8; ++bank) {
+                    long long seen[32];
+                    int n = 0;
+                    for (int lane = ph * width; lane < (ph + 1) * width; ++lane) {
+                        if ((addr[lane] / 16) % 8 != bank) continue;
+                        bool dup = false;
+                        for (int i = 0; i < n; ++i) dup |= seen[i] == addr[lane];
+                        if (!dup) seen[n++] = addr[lane];
+                    }
+                    worst = std::max(worst, n);
                 }
-                worst = std::max(worst, n);
+                cost += worst;
             }
-            cost += worst;
         }
         if (cost < best_cost) {
             best_cost = cost;

@@ -209,10 +209,23 @@ __device__ __forceinline__ Cell make_cell(const DirectParams &P, int tid, int cp
     const int lane = tid & 31;
     c.has_cell = tid < P.cells;
     const int cell = c.has_cell ? tid : P.cells - 1;
-    const int q = cell % P.qcols;
-    const int rbc = cell / P.qcols;
-    const int rb = rbc % P.rblocks;
-    const int cob = rbc / P.rblocks;
+    // Cell order: depthwise cells run along the row (quad fastest), since
+    // their halo columns come from the neighbouring lanes; grouped cells put
+    // the row block fastest, so that with a row pitch of an odd number of
+    // 16-byte chunks per row block every 8-lane phase of a 16-byte shared
+    // load touches 8 different bank groups.
+    int q, rb, cob;
+    if (cpg == 1) {
+        q = cell % P.qcols;
+        const int rbc = cell / P.qcols;
+        rb = rbc % P.rblocks;
+        cob = rbc / P.rblocks;
+    } else {
+        rb = cell % P.rblocks;
+        const int qc = cell / P.rblocks;
+        q = qc % P.qcols;
+        cob = qc / P.qcols;
+    }
     c.col0 = q * CW;
     c.row0 = rb * VR;
     c.co_item = cob * COB;
