@@ -395,8 +395,8 @@ int choose_pitch(int W, int qcols, int cw, int rblocks, int vr, int rows, int ce
     for (int p = base; p <= base + 60; p += 4) {
         if (tma && p > 256) break;
         // exact per-lane addresses: channel block, row block (rb * vr rows),
-        // quad, in the kernel's cell order (make_cell: quad fastest for
-        // depthwise, row block fastest for grouped layers)
+        // quad, in the kernel's cell order (make_cell: quad fastest below 8
+        // channels per group, row block fastest from 8 on)
         const int warps = std::min((cells + 31) / 32, 8);
         int cost = 0;
         for (int wp = 0; wp < warps; ++wp) {
@@ -404,7 +404,7 @@ int choose_pitch(int W, int qcols, int cw, int rblocks, int vr, int rows, int ce
             for (int lane = 0; lane < 32; ++lane) {
                 const int cell = std::min(wp * 32 + lane, cells - 1);
                 int q, rb, cbk;
-                if (cpg == 1) {
+                if (cpg < 8) {
                     q = cell % qcols;
                     rb = (cell / qcols) % rblocks;
                     cbk = cell / qcols / rblocks;
@@ -416,11 +416,12 @@ int choose_pitch(int W, int qcols, int cw, int rblocks, int vr, int rows, int ce
                 const int g = cbk * cob / cpg;
                 addr[lane] = ((static_cast<long long>(g) * cpg * rows + rb * vr) * p + q * cw + 4) * 4;
             }
-            // Depthwise (4-byte loads): the warp's distinct addresses per
-            // 16-byte bank group.  Grouped layers (16-byte loads, served in
-            // four phases of 8 lanes): per phase, the most distinct addresses
-            // in one bank group, summed over the phases.
-            const int phases = cpg == 1 ? 1 : 4, width = 32 / phases;
+            // Below 8 channels per group: the warp's distinct addresses per
+            // 16-byte bank group (the model these tiles were tuned with).
+            // From 8 on (16-byte loads served in four phases of 8 lanes): per
+            // phase, the most distinct addresses in one bank group, summed
+            // over the phases.
+            const int phases = cpg < 8 ? 1 : 4, width = 32 / phases;
             for (int ph = 0; ph < phases; ++ph) {
                 int worst = 0;
                 for (int bank = 0; bank < 8; ++bank) {

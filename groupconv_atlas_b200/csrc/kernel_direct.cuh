@@ -209,13 +209,14 @@ __device__ __forceinline__ Cell make_cell(const DirectParams &P, int tid, int cp
     const int lane = tid & 31;
     c.has_cell = tid < P.cells;
     const int cell = c.has_cell ? tid : P.cells - 1;
-    // Cell order: depthwise cells run along the row (quad fastest), since
-    // their halo columns come from the neighbouring lanes; grouped cells put
-    // the row block fastest, so that with a row pitch of an odd number of
-    // 16-byte chunks per row block every 8-lane phase of a 16-byte shared
-    // load touches 8 different bank groups.
+    // Cell order: quad fastest (depthwise cells take their halo columns from
+    // the neighbouring lanes; for groups of 2 and 4 channels, which are
+    // bandwidth-bound, this order measured faster); for groups of 8 or more
+    // channels (FFMA-bound) the row block fastest, so that with a row pitch
+    // of an odd number of 16-byte chunks per row block every 8-lane phase of
+    // a 16-byte shared load touches 8 different bank groups.
     int q, rb, cob;
-    if (cpg == 1) {
+    if (cpg < 8) {
         q = cell % P.qcols;
         const int rbc = cell / P.qcols;
         rb = rbc % P.rblocks;
