@@ -300,6 +300,10 @@ def run_ours(args):
     rank, world, local = dist_setup()
     torch.cuda.set_device(local)
     if world > 1:
+        # NCCL's own log lines (its version banner, when the environment asks
+        # for it) go to stderr unless the caller chose a file: stdout carries
+        # only the JSON line
+        os.environ.setdefault('NCCL_DEBUG_FILE', '/dev/stderr')
         dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=180),
                                 device_id=torch.device('cuda', local))
     native = api.Native()
