@@ -20,10 +20,14 @@ import torch
 
 from . import api
 
-try:  # the C++ front end (built next to the library by build.build_torch_ext)
-    from . import _gcb_torch
-except ImportError:
-    _gcb_torch = None
+def _cpp_conv():
+    """The C++ front end's entry point (built next to the library by
+    build.build_torch_ext), or None when it has not been built."""
+    try:
+        from . import _gcb_torch
+    except ImportError:
+        return None
+    return _gcb_torch.conv
 
 
 class B200Conv2d(torch.nn.Module):
@@ -46,7 +50,7 @@ class B200Conv2d(torch.nn.Module):
         # The C++ front end allocates the output and calls gc_cuda_conv on the
         # current stream without Python in between (about 3 us less host time
         # per call than the ctypes path below, which serves when it is absent).
-        self._op = _gcb_torch.conv if (cpp and _gcb_torch is not None) else None
+        self._op = _cpp_conv() if cpp else None
         g = self.geometry
         self._geo = (g['cout'], g['r'], g['s'], g['groups'], g['sh'], g['sw'], g['ph'], g['pw'], g['dh'], g['dw'])
         # gc_cuda_conv through a prototype taking plain addresses: the cached

@@ -21,9 +21,11 @@ def pytest_configure(config):
 
 @pytest.fixture(scope='session')
 def native():
-    """The in-tree libgroupconv.so (rebuilt first when a source is newer)."""
+    """The in-tree libgroupconv.so and its PyTorch front end (each rebuilt
+    first when a source is newer)."""
     from groupconv_atlas_b200 import api, build
     build.build()
+    build.build_torch_ext()
     return api.Native()
 
 
