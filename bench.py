@@ -664,6 +664,9 @@ def set_fp32_precision(torch):
         torch.backends.cudnn.allow_tf32 = False
 
 
+GRAPH_STEPS, GRAPH_REPLAYS = 50, 3  # the block's graph timing: calls captured, replays timed
+
+
 def run_block(args):
     """Config 4: torchvision MobileNetV2 features[3] (random Kaiming-normal
     init, seed 2, eval), N4 input N(0,1); the reference block runs every conv
@@ -702,7 +705,8 @@ def run_block(args):
         for name, mod in mods:
             for _ in range(20):
                 mod(x)
-            results[name + '_graph_us'] = graph_step_ms(torch, stream, lambda k, m=mod: m(x), 50) * 1e3
+            results[name + '_graph_us'] = graph_step_ms(torch, stream, lambda k, m=mod: m(x), GRAPH_STEPS,
+                                                        GRAPH_REPLAYS) * 1e3
         # Synchronized API time: rounds alternate between the two blocks (host
         # timing drifts over seconds); per block the median over rounds.
         rounds, per_round = 10, max(1, args.steps // 10)
@@ -740,7 +744,9 @@ def run_block(args):
             'speedup_api': results['cudnn_api_us'] / results['ours_api_us'], 'check': check,
             'e2e': {'value': e2e_us, 'unit': 'us', 'h2d_bytes_per_step': x.numel() * 4,
                     'd2h_bytes_per_step': out.numel() * 4},
-            'gpu_launches': None}
+            # the timed region of `value`: GRAPH_REPLAYS replays of GRAPH_STEPS
+            # block calls, one gc_cuda_conv launch each
+            'gpu_launches': GRAPH_STEPS * GRAPH_REPLAYS * len(replaced)}
     print(json.dumps(line), flush=True)
     return 0
 
