@@ -5,30 +5,39 @@
     python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...
     python bench.py --impl reference ...     # the reference's CPU implementation
 
-A step is one gc_cuda_conv call (implementation 3, the production choice)
-over one batch of synthetic input already resident in HBM.  Default workload:
-the depthwise N32 C256 56x56 convolution, one batch per GPU ("weak": every
-rank runs its own batch, no collective on the data path).  ``--workload
-config5_g32 --scaling strong`` shards the N1024 batch across the ranks.
+A step is one pass of gc_cuda_conv (implementation 3, the production choice)
+over one batch of synthetic input already resident in HBM.  Default
+workload: the large-batch ResNeXt-style layer N1024 C256 56x56, 32 groups
+(8 channels per group), strong-scaled: the batch is split across the ranks
+by ``shard.units_for_rank`` (contiguous image ranges passed to the unchanged
+C ABI by pointer offset; group blocks when there are fewer images than
+ranks), no collective on the data path.  The same line carries secondary
+blocks measured the same way (``--blocks``; default the 64-channel-group
+variant of that layer on the tensor-core path and the depthwise N32 C256
+56x56 layer), each with its own roofline, cuDNN ratio and end-to-end figure.
 
-Reported: ``value`` (GB/s of algorithmic bytes, whole job, device time of K
-back-to-back steps, max over ranks), ``e2e`` (same metric through the C ABI
-with the batch in pinned host memory and both copies inside the timed
-region), ``roofline`` of the kernel, ``cudnn`` (torch.nn.functional.conv2d,
-TF32 off, benchmark mode, same buffers), ``cpu_baseline`` (the reference's CPU
-library on the host cores), ``clocks`` sampled through NVML while timing.
+Reported per workload: ``value`` (GB/s of algorithmic bytes, whole job,
+device time of K back-to-back steps, max over ranks) and ``gflops``,
+``e2e`` (same metric through the C ABI with the batch in pinned host memory
+and both copies inside the timed region), ``roofline`` of the kernel against
+the bound that applies (HBM copy rate, FP32 FFMA rate or the 3xTF32
+tensor-core ceiling, each measured), ``cudnn`` (torch.nn.functional.conv2d in
+a fresh process, TF32 off, benchmark mode), ``cpu_baseline`` (the
+reference's CPU library on the host cores), ``clocks`` sampled through NVML
+while timing.
 """
 from __future__ import annotations
 
 import argparse
 import ctypes as ct
+import dataclasses
 import datetime
 import json
 import math
 import os
 import statistics
+import subprocess
 import sys
-import threading
 import time
 from pathlib import Path
 
@@ -38,129 +47,120 @@ if str(ROOT) not in sys.path:
 
 import numpy as np  # noqa: E402
 
+from groupconv_atlas_b200.clocks import ClockSampler  # noqa: E402
+
 METRIC = 'grouped-conv GB/s & GFLOP/s (% of B200 roofline), latency ratio vs cuDNN, 1/2/4/8 GPU'
 UNIT = 'GB/s'
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_PEAKS = {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0}
+WORKLOADS = ['config1', 'config2', 'config4_leaf', 'config5_g32', 'config5_g4', 'config4_block', 'config3', 'atlas',
+             'model_layers']
+DEFAULT_BLOCKS = 'config5_g4,config2'
 
 
 def parse_args(argv=None):
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument('--gpus', type=int, default=1)
-    ap.add_argument('--steps', type=int, default=2000)
-    ap.add_argument('--warmup', type=int, default=20)
+    ap.add_argument('--steps', type=int, default=20)
+    ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', choices=['ours', 'reference'], default='ours')
-    ap.add_argument('--workload', default='config2',
-                    choices=['config1', 'config2', 'config4_leaf', 'config5_g32', 'config5_g4', 'config4_block',
-                             'config3', 'atlas', 'model_layers'])
+    ap.add_argument('--workload', default='config5_g32', choices=WORKLOADS)
     ap.add_argument('--scaling', choices=['weak', 'strong'], default=None,
-                    help='weak: each rank runs the full workload batch; strong: the batch is sharded')
+                    help='weak: each rank runs the full workload batch; strong: the batch is sharded '
+                         '(default: strong for the N1024 layers, weak otherwise)')
+    ap.add_argument('--blocks', default=None,
+                    help='comma-separated secondary workloads measured into the same line '
+                         f'(default {DEFAULT_BLOCKS} with the default workload, none otherwise; "" for none)')
     ap.add_argument('--shape', default=None,
                     help='N,C,H,W,CPG: a custom 3x3/s1/p1 shape (uniform inputs) instead of --workload')
     ap.add_argument('--batch', type=int, default=None,
                     help='override the workload batch (small cases for profiling)')
-    ap.add_argument('--e2e-steps', type=int, default=20)
+    ap.add_argument('--e2e-steps', type=int, default=10)
     ap.add_argument('--no-e2e', action='store_true')
     ap.add_argument('--no-cudnn', action='store_true')
     ap.add_argument('--no-cpu-baseline', action='store_true')
     ap.add_argument('--cpu-seconds', type=float, default=10.0, help='CPU baseline sample budget')
     ap.add_argument('--atlas-batches', type=int, default=10, help='atlas: paired batches per shape')
     ap.add_argument('--atlas-samples', type=int, default=30, help='atlas: samples per batch and implementation')
+    ap.add_argument('--cudnn-leg', default=None, help=argparse.SUPPRESS)  # internal: the fresh cuDNN process
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error('--warmup must be at least 3')
     if args.shape:
         args.workload = 'custom:' + args.shape
     if args.scaling is None:
-        args.scaling = 'strong' if args.workload.startswith('config5') else 'weak'
+        args.scaling = default_scaling(args.workload)
+    if args.blocks is None:
+        args.blocks = DEFAULT_BLOCKS if (args.workload == 'config5_g32' and not args.shape and args.batch is None) else ''
+    args.block_list = [b for b in args.blocks.split(',') if b]
     return args
 
 
-def measured_peaks():
-    path = ROOT / 'MEASURED_PEAKS.json'
-    if path.exists():
-        data = json.loads(path.read_text())
-        return {'hbm_gbs': float(data['hbm_gbs']), 'bf16_tflops': float(data.get('bf16_tflops', 0))}, 'measured'
-    return dict(FALLBACK_PEAKS), 'fallback'
+def default_scaling(workload):
+    return 'strong' if workload.startswith('config5') else 'weak'
+
+
+def _json(path):
+    return json.loads(path.read_text()) if path.exists() else None
+
+
+def peaks():
+    """Roofline denominators.  HBM: the driver-measured copy rate of this
+    pool's B200s (MEASURED_PEAKS.json).  FP32 FFMA and the tensor core's TF32
+    rate: this library's own probes (gc_b200_probe_*), measured on a B200 of
+    the same pool and committed in profiles/peaks.json.  Each has a labelled
+    fallback when its file is absent."""
+    out = {}
+    mp = _json(ROOT / 'MEASURED_PEAKS.json')
+    if mp:
+        out['hbm_gbs'], out['hbm_source'] = float(mp['hbm_gbs']), 'measured copy bandwidth (MEASURED_PEAKS.json)'
+        bf16 = float(mp.get('bf16_tflops', 0)) or FALLBACK_PEAKS['bf16_tflops']
+    else:
+        out['hbm_gbs'], out['hbm_source'] = FALLBACK_PEAKS['hbm_gbs'], 'fallback copy bandwidth'
+        bf16 = FALLBACK_PEAKS['bf16_tflops']
+    pk = _json(ROOT / 'profiles' / 'peaks.json')
+    if pk:
+        out['ffma_tflops'] = float(pk['ffma_tflops'])
+        out['ffma_source'] = f"measured FFMA probe (profiles/peaks.json, {pk['when']})"
+        out['tf32x3_tflops'] = float(pk['tf32x3_tflops'])
+        out['tf32x3_source'] = (f"measured tcgen05 TF32 MMA probe / 3 (three TF32 products per FP32 product; "
+                                f"profiles/peaks.json, {pk['when']})")
+    else:
+        out['ffma_tflops'] = 148 * 128 * 2 * 1.965e9 / 1e12
+        out['ffma_source'] = 'nominal: 148 SMs x 128 FMA/clk x 2 x 1.965 GHz (no probe record)'
+        out['tf32x3_tflops'] = bf16 / 2 / 3
+        out['tf32x3_source'] = 'bf16 dense GEMM rate / 2 (TF32 rate) / 3 (no probe record)'
+    return out
 
 
 def recorded_traffic(workload):
     """DRAM bytes per launch of the dominant kernel, from a committed ncu summary."""
-    path = ROOT / 'profiles' / 'traffic.json'
-    if not path.exists():
-        return None
-    entry = json.loads(path.read_text()).get(workload)
+    data = _json(ROOT / 'profiles' / 'traffic.json')
+    entry = (data or {}).get(workload)
     return None if entry is None else entry.get('dram_bytes_per_launch')
 
 
-class ClockSampler:
-    """Samples SM clock, power and clock-event reasons through NVML (read only)."""
-    REASONS = {
-        'hw_slowdown': 'nvmlClocksEventReasonHwSlowdown',
-        'hw_thermal_slowdown': 'nvmlClocksEventReasonHwThermalSlowdown',
-        'sw_thermal_slowdown': 'nvmlClocksEventReasonSwThermalSlowdown',
-        'sw_power_cap': 'nvmlClocksEventReasonSwPowerCap',
-        'hw_power_brake_slowdown': 'nvmlClocksEventReasonHwPowerBrakeSlowdown',
-    }
-
-    def __init__(self, device_index, period=0.005):
-        self.period = period
-        self.samples = []
-        self._stop = threading.Event()
-        self._thread = None
-        try:
-            import pynvml
-            pynvml.nvmlInit()
-            self.nvml = pynvml
-            # NVML enumerates physical GPUs; map through CUDA_VISIBLE_DEVICES if set.
-            visible = os.environ.get('CUDA_VISIBLE_DEVICES')
-            index = device_index
-            if visible:
-                ids = [v.strip() for v in visible.split(',') if v.strip()]
-                if device_index < len(ids) and ids[device_index].isdigit():
-                    index = int(ids[device_index])
-            self.handle = pynvml.nvmlDeviceGetHandleByIndex(index)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM)
-        except Exception as exc:  # no NVML: report why instead of clocks
-            self.nvml = None
-            self.error = str(exc)
-
-    def _run(self):
-        n = self.nvml
-        while not self._stop.is_set():
-            try:
-                sm = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
-                reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
-                power = n.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
-                self.samples.append((sm, reasons, power))
-            except Exception:
-                pass
-            time.sleep(self.period)
-
-    def __enter__(self):
-        if self.nvml is not None:
-            self._thread = threading.Thread(target=self._run, daemon=True)
-            self._thread.start()
-        return self
-
-    def __exit__(self, *exc):
-        self._stop.set()
-        if self._thread is not None:
-            self._thread.join()
-
-    def summary(self):
-        if self.nvml is None:
-            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': [], 'error': self.error}
-        if not self.samples:
-            return {'sm_mhz': None, 'sm_max_mhz': self.max_mhz, 'reasons': [], 'samples': 0}
-        active = set()
-        for _, mask, _ in self.samples:
-            for name, const in self.REASONS.items():
-                if mask & getattr(self.nvml, const):
-                    active.add(name)
-        return {'sm_mhz': statistics.median(s[0] for s in self.samples), 'sm_max_mhz': self.max_mhz,
-                'reasons': sorted(active), 'samples': len(self.samples),
-                'power_w_max': max(s[2] for s in self.samples)}
+def roofline_of(plan, step_bytes, step_flops, launches, kernel_ms, pk):
+    """Roofline of the dominant kernel: algorithmic bytes and FLOPs per launch
+    over the average launch duration, against the bound that applies.  The
+    tensor-core plans are bound by the 3xTF32 ceiling; the others by HBM or
+    by the FP32 FFMA rate, whichever gives the longer minimum time."""
+    achieved_gbs = (step_bytes / launches) / (kernel_ms / 1e3) / 1e9
+    achieved_tflops = (step_flops / launches) / (kernel_ms / 1e3) / 1e12
+    t_hbm = (step_bytes / launches) / (pk['hbm_gbs'] * 1e9)
+    t_ffma = (step_flops / launches) / (pk['ffma_tflops'] * 1e12)
+    common = {'hbm_achieved_gbs': achieved_gbs, 'hbm_frac': achieved_gbs / pk['hbm_gbs'],
+              'fp32_tflops': achieved_tflops}
+    if plan.startswith('kernel=tf32x3'):
+        return {'bound': 'tensor', 'achieved': achieved_tflops, 'peak': pk['tf32x3_tflops'], 'unit': 'TFLOP/s',
+                'frac': achieved_tflops / pk['tf32x3_tflops'], 'peak_source': pk['tf32x3_source'],
+                'ffma_frac': achieved_tflops / pk['ffma_tflops'], **common}
+    if t_ffma > t_hbm:
+        return {'bound': 'fp32', 'achieved': achieved_tflops, 'peak': pk['ffma_tflops'], 'unit': 'TFLOP/s',
+                'frac': achieved_tflops / pk['ffma_tflops'], 'peak_source': pk['ffma_source'], **common}
+    return {'bound': 'hbm', 'achieved': achieved_gbs, 'peak': pk['hbm_gbs'], 'unit': 'GB/s',
+            'frac': achieved_gbs / pk['hbm_gbs'], 'peak_source': pk['hbm_source'],
+            'ffma_frac': achieved_tflops / pk['ffma_tflops'], **common}
 
 
 def dist_setup():
@@ -235,15 +235,26 @@ def cpu_baseline(name, images_total, seconds):
                       f'{cores} threads'}
 
 
+def workload_config(name, shape):
+    """The `config` object of a line: the same keys and values in both arms
+    (the workload, its full shape, how the timing keeps L2 from serving
+    re-reads).  Launch plans and the parallel split go elsewhere."""
+    n, c, h, w = shape.input
+    batch_bytes = 4 * 2 * n * c * h * w
+    l2 = (f'inputs larger than L2: one step reads and writes {batch_bytes / 2**30:.2f} GiB > L2 126 MiB'
+          if batch_bytes > 3 * L2_BYTES else
+          'rotating input/output sets larger than 3x the 126 MiB L2 (GPU arm); one set per step')
+    return {'workload': name, 'shape': dataclasses.asdict(shape), 'l2': l2}
+
+
 def run_reference(args):
     rank, world, _ = dist_setup()
     if rank != 0:
         return 0  # the CPU reference runs on rank 0 only
-    import dataclasses
     from groupconv_atlas_b200 import workloads
-    wl = workloads.by_name(args.workload, with_x=False)
+    wl = workloads.by_name(args.workload, batch=args.batch, with_x=False)
     m = sample_images(args.workload, wl.shape.n, 0.25)
-    wl, x, w = workload_host(args.workload, 0, m)
+    _, x, w = workload_host(args.workload, 0, m)
     shape = dataclasses.replace(wl.shape, n=m)
     run, kind, cores = cpu_reference_runner(shape, x, w)
     out = np.empty(shape.output, np.float32)
@@ -256,15 +267,14 @@ def run_reference(args):
     step_bytes = 4 * (math.prod(shape.input) + math.prod(shape.weight) + math.prod(shape.output))
     step_flops = 2 * math.prod(shape.output) * shape.cpg * 9
     value = step_bytes * args.steps / elapsed / 1e9
+    sample = f'{m} of the workload\'s {wl.shape.n} images per step, GC_BLOCKED schedule, {cores} threads'
     line = {'impl': 'reference', 'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': args.gpus,
             'steps': args.steps, 'warmup': args.warmup, 'ms_per_step': elapsed / args.steps * 1e3,
             'higher_is_better': True, 'scaling': args.scaling, 'vs_baseline': None, 'dtype': 'f32',
-            'data': 'synthetic (seeded, per-image generators)',
+            'data': 'synthetic (seeded per-image generators, distributions of the workload definition)',
             'gflops': step_flops * args.steps / elapsed / 1e9,
-            'config': {'workload': args.workload, 'shape': dataclasses.asdict(wl.shape),
-                       'step': f'{m} images of the batch per step'},
-            'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': cores, 'kind': kind,
-                             'sample': f'{m} images per step, GC_BLOCKED, {cores} threads'},
+            'config': workload_config(args.workload, wl.shape),
+            'cpu_baseline': {'value': value, 'unit': UNIT, 'cores': cores, 'kind': kind, 'sample': sample},
             'e2e': {'value': value, 'unit': UNIT, 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -290,40 +300,104 @@ class Call:
             self.native.check(status)
 
 
-def run_ours(args):
-    import dataclasses
-    import torch
-    import torch.distributed as dist
-    from groupconv_atlas_b200 import api, shard, workloads
-    from oracle import oracle as orc
+@dataclasses.dataclass
+class Piece:
+    """One gc_cuda_conv call of a rank: a unit of ``shard.units_for_rank``
+    (or a chunk of one) as a sub-shape with element offsets into the
+    rank-local x, the full weights and the rank-local y."""
+    shape: object
+    x_off: int
+    w_off: int
+    y_off: int
 
-    rank, world, local = dist_setup()
-    torch.cuda.set_device(local)
-    if world > 1:
-        # NCCL's own log lines (its version banner, when the environment asks
-        # for it) go to stderr unless the caller chose a file: stdout carries
-        # only the JSON line
-        os.environ.setdefault('NCCL_DEBUG_FILE', '/dev/stderr')
-        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=180),
-                                device_id=torch.device('cuda', local))
-    native = api.Native()
-    full = workloads.by_name(args.workload, batch=args.batch, with_x=False)
-    if args.scaling == 'weak':
-        units = [shard.Unit(0, full.shape.n, 0, full.shape.cin)]
-        first_image = rank * full.shape.n  # each rank: its own batch of the same shape
-        job_images = full.shape.n * world
-    else:
-        units = shard.units_for_rank(full.shape, world, rank)
-        first_image = units[0].n0 if units else 0
-        job_images = full.shape.n
-    n_images = sum(u.images() for u in units) if args.scaling == 'strong' else full.shape.n
-    local_shape = dataclasses.replace(full.shape, n=max(1, units[-1].n1 - units[0].n0) if args.scaling == 'strong'
-                                      else full.shape.n)
-    # Host data of this rank's images (pinned), weights.
-    x_host = workloads.images(full.shape, full.seed, full.dist, first_image, local_shape.n)
+    @property
+    def x_len(self):
+        return math.prod(self.shape.input)
+
+    @property
+    def w_len(self):
+        return math.prod(self.shape.weight)
+
+    @property
+    def y_len(self):
+        return math.prod(self.shape.output)
+
+    @property
+    def bytes(self):
+        return 4 * (self.x_len + self.w_len + self.y_len)
+
+    @property
+    def flops(self):
+        return 2 * self.y_len * self.shape.cpg * self.shape.r * self.shape.s
+
+
+def rank_work(full, scaling, world, rank):
+    """(first image, image count, units relative to that first image) of this
+    rank: weak scaling gives every rank its own batch of the workload's shape
+    (images rank*N .. rank*N+N-1 of the seeded stream); strong scaling splits
+    the one batch with shard.units_for_rank."""
+    from groupconv_atlas_b200 import shard
+    if scaling == 'weak':
+        return rank * full.n, full.n, [shard.Unit(0, full.n, 0, full.cin)]
+    units = shard.units_for_rank(full, world, rank)
+    if not units:
+        return 0, 0, []
+    first = units[0].n0
+    return first, units[-1].n1 - first, [shard.Unit(u.n0 - first, u.n1 - first, u.c0, u.c1) for u in units]
+
+
+def pieces_of(units, local_shape, chunks=1):
+    """Pieces of the rank's units; with chunks > 1 a unit of several images
+    is split into up to `chunks` image ranges (the end-to-end pipeline)."""
+    from groupconv_atlas_b200 import shard
+    out = []
+    for u in units:
+        n = u.images()
+        parts = max(1, min(chunks, n))
+        for i in range(parts):
+            lo, hi = u.n0 + i * n // parts, u.n0 + (i + 1) * n // parts
+            if hi <= lo:
+                continue
+            v = shard.Unit(lo, hi, u.c0, u.c1)
+            out.append(Piece(v.shape(local_shape), *v.offsets(local_shape)))
+    return out
+
+
+def gate(pieces, x_local, w_full, y_local):
+    """The correctness gate before timing: 64 FP64 points of every piece's
+    output, each checked on the piece's own sub-shape and views (outputs of
+    channels or images the rank does not compute are never read).  x_local,
+    w_full and y_local are the rank-local input, the weights and the
+    rank-local output (numpy arrays or tensors, flattened here).  Returns the
+    failures as (piece index, failed point count); empty when all pass."""
+    from oracle import oracle as orc
+    xf, wf, yf = x_local.reshape(-1), w_full.reshape(-1), y_local.reshape(-1)
+    failed = []
+    for i, p in enumerate(pieces):
+        xv = xf[p.x_off:p.x_off + p.x_len].reshape(p.shape.input)
+        wv = wf[p.w_off:p.w_off + p.w_len].reshape(p.shape.weight)
+        yv = yf[p.y_off:p.y_off + p.y_len].reshape(p.shape.output)
+        check = orc.check_points(p.shape, xv, wv, yv)
+        if not check['passed']:
+            failed.append((i, check['failed_points']))
+    return failed
+
+
+def measure_workload(args, name, scaling, ctx, primary):
+    """Everything one workload reports: correctness gate, device-timed
+    steps, roofline, end to end, cuDNN and CPU baselines."""
+    import torch
+    from groupconv_atlas_b200 import shard, workloads
+    native, rank, world, local = ctx['native'], ctx['rank'], ctx['world'], ctx['local']
+    full = workloads.by_name(name, batch=args.batch if primary else None, with_x=False)
+    first, local_n, units = rank_work(full.shape, scaling, world, rank)
+    local_shape = dataclasses.replace(full.shape, n=max(1, local_n))
+    x_host = workloads.images(full.shape, full.seed, full.dist, first, local_shape.n)
     w_host = full.w
     xh = torch.from_numpy(x_host).pin_memory()
     wh = torch.from_numpy(w_host).pin_memory()
+    del x_host
+    pieces = pieces_of(units, local_shape)
     set_bytes = 4 * (math.prod(local_shape.input) + math.prod(local_shape.output))
     sets = int(min(4096, max(1, math.ceil(3 * L2_BYTES / set_bytes))))
     stream = torch.cuda.Stream()
@@ -332,40 +406,30 @@ def run_ours(args):
     ys = [torch.empty(local_shape.output, device='cuda') for _ in range(sets)]
     torch.cuda.synchronize()
 
-    def unit_views(xt, yt):
-        out = []
-        for u in units if args.scaling == 'strong' else [shard.Unit(0, local_shape.n, 0, local_shape.cin)]:
-            if args.scaling == 'strong':
-                u = shard.Unit(u.n0 - units[0].n0, u.n1 - units[0].n0, u.c0, u.c1)
-            sub = u.shape(local_shape)
-            ox, ow, oy = u.offsets(local_shape)
-            xv = xt.view(-1)[ox:ox + math.prod(sub.input)].view(sub.input)
-            wv = dw.view(-1)[ow:ow + math.prod(sub.weight)].view(sub.weight)
-            yv = yt.view(-1)[oy:oy + math.prod(sub.output)].view(sub.output)
-            out.append((sub, xv, wv, yv))
-        return out
+    def view(t, off, shape):
+        return t.view(-1)[off:off + math.prod(shape)].view(shape)
 
-    calls = [[Call(native, sub, xv, wv, yv, stream.cuda_stream) for sub, xv, wv, yv in unit_views(xs[i], ys[i])]
-             for i in range(sets)]
-    launches_per_step = len(calls[0])
-    step_bytes = sum(4 * (math.prod(s.input) + math.prod(s.weight) + math.prod(s.output))
-                     for s, *_ in unit_views(xs[0], ys[0]))
-    step_flops = sum(2 * math.prod(s.output) * s.cpg * 9 for s, *_ in unit_views(xs[0], ys[0]))
+    calls = [[Call(native, p.shape, view(xs[i], p.x_off, p.shape.input), view(dw, p.w_off, p.shape.weight),
+                   view(ys[i], p.y_off, p.shape.output), stream.cuda_stream) for p in pieces] for i in range(sets)]
+    launches = len(pieces)
+    step_bytes = sum(p.bytes for p in pieces)
+    step_flops = sum(p.flops for p in pieces)
 
-    # Correctness gate before timing: 64 FP64 points of this rank's output.
+    # Correctness gate before timing: 64 FP64 points of every piece's output
+    # (each unit's own sub-shape and views).
+    plan = ''
     with torch.cuda.stream(stream):
         for c in calls[0]:
             c()
-    plan = native.last_plan()
+            plan = native.last_plan()
     stream.synchronize()
-    y0 = ys[0].cpu().numpy()
-    check = orc.check_points(local_shape, x_host, w_host, y0)
-    if not check['passed']:
-        raise SystemExit(f'correctness gate failed on rank {rank}: {check["failed_points"]} points [{plan}]')
+    failed = gate(pieces, xh.numpy(), wh.numpy(), ys[0])  # y indexed point by point on the device
+    if failed:
+        raise SystemExit(f'{name}: correctness gate failed on rank {rank}: {failed} [{plan}]')
     if native.device_status(clear=True):
         raise SystemExit('device status word set after the correctness gate')
 
-    # Device-timed region: K back-to-back steps, events around every step.
+    # Device-timed region: K back-to-back steps.
     with torch.cuda.stream(stream):
         for k in range(args.warmup):
             for c in calls[k % sets]:
@@ -386,144 +450,163 @@ def run_ours(args):
     barrier()
     elapsed_ms = region0.elapsed_time(region1)
     # Average launch duration for the roofline: the events bracketing the
-    # timed region on the launch stream, over the launches inside it.
-    # (Consecutive launches overlap prologue and tail through programmatic
+    # timed region on the launch stream, over the launches inside it
+    # (consecutive launches overlap prologue and tail through programmatic
     # dependent launch, so the region, not an event pair per launch, is the
-    # per-launch cost; an event between launches would break that overlap.)
-    kernel_ms = elapsed_ms / (args.steps * launches_per_step)
+    # per-launch cost).
+    kernel_ms = elapsed_ms / (args.steps * max(1, launches))
 
     def graph_step(k):
         for c in calls[k % sets]:
             c()
-    with torch.cuda.stream(stream):
-        graph_kernel_ms = graph_step_ms(torch, stream, graph_step, min(args.steps, 50)) / launches_per_step
+    graph_kernel_ms = None
+    if launches:
+        with torch.cuda.stream(stream):
+            graph_kernel_ms = graph_step_ms(torch, stream, graph_step, min(args.steps, 50)) / launches
     max_elapsed = shard.max_over_ranks(elapsed_ms)
     job_bytes = shard.sum_over_ranks(step_bytes)
     job_flops = shard.sum_over_ranks(step_flops)
     value = job_bytes * args.steps / (max_elapsed / 1e3) / 1e9
     gflops = job_flops * args.steps / (max_elapsed / 1e3) / 1e9
 
-    # End to end through the C ABI: pinned host batch -> device -> conv -> host,
-    # pipelined in chunks over three streams, copies inside the timed region.
     e2e = None
     if not args.no_e2e:
-        e2e = end_to_end(args, native, local_shape, units, xh, wh, torch, api, shard)
-
+        e2e = end_to_end(args, native, local_shape, units, xh, wh, torch)
+    pk = peaks()
+    roof = roofline_of(plan, step_bytes, step_flops, max(1, launches), kernel_ms, pk) if launches else None
+    if roof is not None and roof['bound'] == 'hbm' and rank == 0 and sets > 1:
+        # Context for launch-sized transfers: a device copy x -> y of the
+        # same bytes per launch, same rotating sets, back to back.
+        copy_ms = copy_same_bytes_ms(torch, stream, xs, ys, args.steps)
+        copy_gbs = 2 * xs[0].numel() * 4 / (copy_ms / 1e3) / 1e9
+        roof['same_size_copy'] = {'gbs': copy_gbs, 'ms': copy_ms, 'frac_of_it': roof['achieved'] / copy_gbs,
+                                  'what': 'torch copy_ of x into y (read + write bytes), same rotating sets, '
+                                          'K back-to-back copies'}
     cudnn = None
-    if not args.no_cudnn and rank == 0:
-        cudnn = cudnn_baseline(args, torch, local_shape, xs, dw, sets,
-                               (elapsed_ms / args.steps, graph_kernel_ms * launches_per_step))
-
+    if not args.no_cudnn and rank == 0 and launches:
+        cudnn = cudnn_fresh_process(args, local_shape, local, sets,
+                                    (elapsed_ms / args.steps, graph_kernel_ms * launches))
     cpu = None
     if not args.no_cpu_baseline and rank == 0 and world == 1:
-        cpu = cpu_baseline(args.workload, local_shape.n, args.cpu_seconds)
-
+        cpu = cpu_baseline(name, local_shape.n, args.cpu_seconds if primary else args.cpu_seconds / 2)
     status = native.device_status(clear=True)
     if status:
         raise SystemExit(f'device status word set during timing: {status:#x}')
-    peaks, peak_kind = measured_peaks()
-    achieved = (step_bytes / launches_per_step) / (kernel_ms / 1e3) / 1e9
-    fp32_tflops = (step_flops / launches_per_step) / (kernel_ms / 1e3) / 1e12
-    if plan.startswith('kernel=tf32x3'):
-        # Tensor-bound: FP32 work against the 3xTF32 ceiling = measured bf16
-        # GEMM rate / 2 (TF32 issues at half the bf16 rate) / 3 (products).
-        peak_tensor = peaks['bf16_tflops'] / 2 / 3
-        roofline = {'bound': 'tensor', 'achieved': fp32_tflops, 'peak': peak_tensor, 'unit': 'TFLOP/s',
-                    'frac': fp32_tflops / peak_tensor,
-                    'peak_source': f'{peak_kind} bf16 dense GEMM / 2 (TF32 rate) / 3 (3xTF32 products)',
-                    'hbm_achieved_gbs': achieved, 'hbm_frac': achieved / peaks['hbm_gbs']}
-    else:
-        roofline = {'bound': 'hbm', 'achieved': achieved, 'peak': peaks['hbm_gbs'], 'unit': 'GB/s',
-                    'frac': achieved / peaks['hbm_gbs'], 'peak_source': f'{peak_kind} copy bandwidth'}
-        if rank == 0 and xs[0].numel() == ys[0].numel():
-            # Context for launch-sized transfers: a device copy x -> y of the
-            # same bytes per launch, same rotating sets, back to back.
-            copy_ms = copy_same_bytes_ms(torch, stream, xs, ys, args.steps)
-            copy_gbs = 2 * xs[0].numel() * 4 / (copy_ms / 1e3) / 1e9
-            roofline['same_size_copy'] = {'gbs': copy_gbs, 'ms': copy_ms, 'frac_of_it': achieved / copy_gbs,
-                                          'what': 'torch copy_ of x into y (read + write bytes), '
-                                                  'same rotating sets, K back-to-back copies'}
-    traffic = recorded_traffic(args.workload)
     clocks = sampler.summary()
     if world > 1:
         import torch.distributed as dist
         gathered = [None] * world
         dist.all_gather_object(gathered, clocks)
         clocks = gathered[0] | {'per_rank_reasons': [g.get('reasons') for g in gathered]}
+    if roof is not None:
+        roof.update({'traffic': recorded_traffic(name), 'kernel_ms': kernel_ms,
+                     'kernel_ms_timing': 'CUDA events bracketing the timed region on the launch stream / launches',
+                     'graph_kernel_ms': graph_kernel_ms,
+                     'algorithmic_bytes_per_launch': step_bytes / launches,
+                     'algorithmic_flops_per_launch': step_flops / launches})
+    del calls, xs, ys
+    torch.cuda.empty_cache()
+    return {'workload': name, 'value': value, 'unit': UNIT, 'gflops': gflops, 'ms_per_step': max_elapsed / args.steps,
+            'scaling': scaling, 'config': workload_config(name, full.shape),
+            'run': {'implementation': 3, 'kernel_plan': plan, 'images_this_rank': local_n if units else 0,
+                    'units_this_rank': len(units), 'launches_per_step': launches,
+                    'rotating_sets': sets,
+                    'parallelism': f'{scaling} scaling over {world} GPU(s): '
+                                   + ('each rank its own batch' if scaling == 'weak'
+                                      else 'shard.units_for_rank (batch ranges, group blocks when N < ranks)')
+                                   + ', no collective on the data path'},
+            'roofline': roof, 'e2e': e2e, 'gpu_launches': args.steps * launches, 'clocks': clocks,
+            'cudnn': cudnn, 'cpu_baseline': cpu}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from groupconv_atlas_b200 import api
+
+    rank, world, local = dist_setup()
+    torch.cuda.set_device(local)
+    if world > 1:
+        # NCCL's own log lines go to stderr unless the caller chose a file:
+        # stdout carries only the JSON line
+        os.environ.setdefault('NCCL_DEBUG_FILE', '/dev/stderr')
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=180),
+                                device_id=torch.device('cuda', local))
+    ctx = {'native': api.Native(), 'rank': rank, 'world': world, 'local': local}
+    main_result = measure_workload(args, args.workload, args.scaling, ctx, primary=True)
+    blocks = [measure_workload(args, b, default_scaling(b), ctx, primary=False) for b in args.block_list]
     if rank == 0:
+        m = main_result
         line = {
-            'metric': METRIC, 'value': value, 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
-            'warmup': args.warmup, 'ms_per_step': max_elapsed / args.steps, 'higher_is_better': True,
-            'scaling': args.scaling, 'vs_baseline': None, 'dtype': 'f32',
+            'metric': METRIC, 'value': m['value'], 'unit': UNIT, 'n_gpus': world, 'steps': args.steps,
+            'warmup': args.warmup, 'ms_per_step': m['ms_per_step'], 'higher_is_better': True,
+            'scaling': m['scaling'], 'vs_baseline': None, 'dtype': 'f32',
             'data': 'synthetic (seeded per-image generators, distributions of the workload definition)',
-            'gflops': gflops,
-            'config': {'workload': args.workload, 'shape': dataclasses.asdict(full.shape),
-                       'images_per_step': job_images, 'implementation': 3, 'kernel_plan': plan,
-                       'l2': f'{sets} rotating input/output sets per rank, {sets * set_bytes / 2**20:.0f} MiB '
-                             f'> L2 {L2_BYTES / 2**20:.0f} MiB',
-                       'parallelism': f'{args.scaling} batch sharding over {world} GPU(s), no collective'},
-            'roofline': {**roofline, 'traffic': traffic, 'kernel_ms': kernel_ms,
-                         'kernel_ms_timing': 'CUDA events bracketing the timed region on the launch stream / launches',
-                         'graph_kernel_ms': graph_kernel_ms,
-                         'algorithmic_bytes_per_launch': step_bytes / launches_per_step,
-                         'algorithmic_flops_per_launch': step_flops / launches_per_step,
-                         'fp32_tflops': fp32_tflops},
-            'e2e': e2e, 'gpu_launches': args.steps * launches_per_step, 'clocks': clocks,
-            'cudnn': cudnn, 'cpu_baseline': cpu,
+            'gflops': m['gflops'], 'config': m['config'], 'run': m['run'], 'roofline': m['roofline'],
+            'e2e': m['e2e'], 'gpu_launches': m['gpu_launches'], 'clocks': m['clocks'], 'cudnn': m['cudnn'],
+            'cpu_baseline': m['cpu_baseline'],
+            'blocks': blocks,
         }
         print(json.dumps(line), flush=True)
-    del calls
     if world > 1:
         dist.destroy_process_group()
     return 0
 
 
-def end_to_end(args, native, shape, units, xh, wh, torch, api, shard):
-    """Same metric, through the C ABI with host buffers: per step the batch is
-    copied host->device in chunks (pinned), convolved chunk by chunk as soon
-    as its copy lands, and copied back; three streams overlap the two copy
-    directions with compute, and two device buffer sets alternate between
-    steps, so the copies of step k+1 never wait for the convolutions of
-    step k."""
-    import dataclasses
-    n = shape.n
-    chunks = max(1, min(8, n))
-    bounds = [(i * n // chunks, (i + 1) * n // chunks) for i in range(chunks)]
-    bounds = [b for b in bounds if b[1] > b[0]]
+def end_to_end(args, native, shape, units, xh, wh, torch):
+    """Same metric, through the C ABI with host buffers: per step each piece
+    of the rank's units (batch units in up to 8 image chunks) is copied
+    host->device (pinned), convolved as soon as its copy lands, and copied
+    back; three streams overlap the two copy directions with compute, and two
+    device buffer sets alternate between steps, so the copies of step k+1
+    never wait for the convolutions of step k."""
+    from groupconv_atlas_b200 import shard
+    pieces = pieces_of(units, shape, chunks=8)
+    if not pieces:  # a rank without work still takes every collective step of the others
+        barrier()
+        barrier()
+        shard.max_over_ranks(0.0)
+        shard.sum_over_ranks(0.0)
+        return None
     dws = [torch.empty(shape.weight, device='cuda') for _ in range(2)]
     dxs = [torch.empty(shape.input, device='cuda') for _ in range(2)]
     dys = [torch.empty(shape.output, device='cuda') for _ in range(2)]
     yh = torch.empty(shape.output, pin_memory=True)
     s_in, s_cmp, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
-    calls = [[Call(native, dataclasses.replace(shape, n=hi - lo), dxs[b][lo:hi], dws[b], dys[b][lo:hi],
-                   s_cmp.cuda_stream) for lo, hi in bounds] for b in range(2)]
-    ev_in = [[torch.cuda.Event() for _ in bounds] for _ in range(2)]
-    ev_cmp = [[torch.cuda.Event() for _ in bounds] for _ in range(2)]
-    ev_out = [[torch.cuda.Event() for _ in bounds] for _ in range(2)]
+
+    def flat(t, off, n):
+        return t.view(-1)[off:off + n]
+
+    calls = [[Call(native, p.shape, flat(dxs[b], p.x_off, p.x_len).view(p.shape.input),
+                   flat(dws[b], p.w_off, p.w_len).view(p.shape.weight),
+                   flat(dys[b], p.y_off, p.y_len).view(p.shape.output), s_cmp.cuda_stream) for p in pieces]
+             for b in range(2)]
+    ev_in = [[torch.cuda.Event() for _ in pieces] for _ in range(2)]
+    ev_cmp = [[torch.cuda.Event() for _ in pieces] for _ in range(2)]
+    ev_out = [[torch.cuda.Event() for _ in pieces] for _ in range(2)]
     used = [False, False]
 
     def step(k):
         b = k & 1
-        dx, dy = dxs[b], dys[b]
         with torch.cuda.stream(s_in):
             if used[b]:
                 s_in.wait_event(ev_cmp[b][-1])  # step k-2 finished reading these weights
             dws[b].copy_(wh, non_blocking=True)
-            for j, (lo, hi) in enumerate(bounds):
+            for j, p in enumerate(pieces):
                 if used[b]:
-                    s_in.wait_event(ev_cmp[b][j])  # step k-2 finished reading this dx chunk
-                dx[lo:hi].copy_(xh[lo:hi], non_blocking=True)
+                    s_in.wait_event(ev_cmp[b][j])  # step k-2 finished reading this x piece
+                flat(dxs[b], p.x_off, p.x_len).copy_(flat(xh, p.x_off, p.x_len), non_blocking=True)
                 ev_in[b][j].record(s_in)
-        for j in range(len(bounds)):
+        for j in range(len(pieces)):
             s_cmp.wait_event(ev_in[b][j])
             if used[b]:
-                s_cmp.wait_event(ev_out[b][j])  # step k-2 finished reading this dy chunk
+                s_cmp.wait_event(ev_out[b][j])  # step k-2 finished reading this y piece
             calls[b][j]()
             ev_cmp[b][j].record(s_cmp)
         with torch.cuda.stream(s_out):
-            for j, (lo, hi) in enumerate(bounds):
+            for j, p in enumerate(pieces):
                 s_out.wait_event(ev_cmp[b][j])
-                yh[lo:hi].copy_(dy[lo:hi], non_blocking=True)
+                flat(yh, p.y_off, p.y_len).copy_(flat(dys[b], p.y_off, p.y_len), non_blocking=True)
                 ev_out[b][j].record(s_out)
         used[b] = True
 
@@ -536,40 +619,86 @@ def end_to_end(args, native, shape, units, xh, wh, torch, api, shard):
     for i in range(args.e2e_steps):
         step(3 + i)
     t1.record(s_out)
+    s_in.wait_stream(s_out)
     torch.cuda.synchronize()
     barrier()
     ms = shard.max_over_ranks(t0.elapsed_time(t1))
-    # the host result of the last step equals that step's device output
-    consistent = bool(torch.equal(yh, dys[(2 + args.e2e_steps) & 1].cpu()))
-    step_bytes = 4 * (math.prod(shape.input) + math.prod(shape.weight) + math.prod(shape.output))
+    last = dys[(2 + args.e2e_steps) & 1]
+    consistent = all(torch.equal(flat(yh, p.y_off, p.y_len), flat(last, p.y_off, p.y_len).cpu()) for p in pieces)
+    step_bytes = sum(p.bytes for p in pieces)
     job_bytes = shard.sum_over_ranks(step_bytes)
-    # The link's bound: the same bytes copied in both directions at once
-    # (the step's input host->device while its output goes device->host),
-    # with no convolution.
-    c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    c0.record(s_in)
-    for _ in range(5):
-        s_out.wait_event(c0)
-        with torch.cuda.stream(s_in):
-            dxs[0].copy_(xh, non_blocking=True)
-        with torch.cuda.stream(s_out):
-            yh.copy_(dys[0], non_blocking=True)
-        s_in.wait_stream(s_out)
-    c1.record(s_in)
-    torch.cuda.synchronize()
-    link_ms = shard.max_over_ranks(c0.elapsed_time(c1) / 5)
-    bound = job_bytes / (link_ms / 1e3) / 1e9
     e2e_value = job_bytes * args.e2e_steps / (ms / 1e3) / 1e9
+    del calls, dxs, dys, dws
+    torch.cuda.empty_cache()
     return {'value': e2e_value, 'unit': UNIT,
-            'link_bound': {'value': bound, 'unit': UNIT, 'frac': e2e_value / bound, 'ms_per_step': link_ms,
-                           'what': 'the step\'s input host->device and output device->host copied at once '
-                                   '(pinned), no convolution'},
-            'h2d_bytes_per_step': 4 * (math.prod(shape.input) + math.prod(shape.weight)),
-            'd2h_bytes_per_step': 4 * math.prod(shape.output), 'steps': args.e2e_steps,
-            'ms_per_step': ms / args.e2e_steps, 'chunks': len(bounds),
-            'path': 'pinned host -> gc_cuda_conv per chunk (C ABI via ctypes) -> pinned host',
-            'host_matches_device': consistent}
+            'h2d_bytes_per_step': sum(4 * p.x_len for p in pieces) + 4 * math.prod(shape.weight),
+            'd2h_bytes_per_step': sum(4 * p.y_len for p in pieces), 'steps': args.e2e_steps,
+            'ms_per_step': ms / args.e2e_steps, 'pieces_per_step': len(pieces),
+            'path': 'pinned host -> gc_cuda_conv per piece (C ABI via ctypes) -> pinned host, '
+                    'copies and calls overlapped on three streams',
+            'host_matches_device': bool(consistent)}
+
+
+def cudnn_fresh_process(args, shape, device, sets, ours):
+    """torch.nn.functional.conv2d on the same shape in a fresh process (so
+    cuDNN's benchmark search is not hidden by a cache warmed in this one, as
+    the reference's bench/cuda_run.py:124-156 does): TF32 off and read back,
+    cudnn.benchmark, device time of back-to-back calls (eager) and of
+    CUDA-graph replay, rotating inputs as large as ours."""
+    spec = json.dumps({'shape': dataclasses.asdict(shape), 'device': device, 'sets': sets,
+                       'steps': max(20, min(args.steps, 200))})
+    env = dict(os.environ)
+    for k in ('RANK', 'WORLD_SIZE', 'LOCAL_RANK', 'MASTER_ADDR', 'MASTER_PORT', 'LOCAL_WORLD_SIZE',
+              'GROUP_RANK', 'TORCHELASTIC_RUN_ID'):
+        env.pop(k, None)
+    proc = subprocess.run([sys.executable, str(ROOT / 'bench.py'), '--cudnn-leg', spec], capture_output=True,
+                          text=True, env=env, timeout=600)
+    if proc.returncode != 0:
+        return {'error': (proc.stderr or proc.stdout)[-400:]}
+    res = json.loads(proc.stdout.strip().splitlines()[-1])
+    res.update({'ours_ms_per_step': ours[0], 'ours_graph_ms_per_step': ours[1],
+                'speedup_vs_cudnn': res['ms_per_step'] / ours[0],
+                'speedup_vs_cudnn_graph': res['graph_ms_per_step'] / ours[1]})
+    return res
+
+
+def cudnn_leg(spec):
+    """The fresh cuDNN process (see cudnn_fresh_process)."""
+    import torch
+    import torch.nn.functional as F
+    from groupconv_atlas_b200.api import Shape
+    cfg = json.loads(spec)
+    shape = Shape(**cfg['shape'])
+    torch.cuda.set_device(cfg['device'])
+    set_fp32_precision(torch)
+    torch.backends.cudnn.benchmark = True
+    sets, steps = cfg['sets'], cfg['steps']
+    g = torch.Generator(device='cuda').manual_seed(3)
+    stream = torch.cuda.Stream()
+    with torch.inference_mode(), torch.cuda.stream(stream):
+        xs = [torch.rand(shape.input, device='cuda', generator=g) * 2 - 1 for _ in range(sets)]
+        w = torch.rand(shape.weight, device='cuda', generator=g) * 2 - 1
+        conv = lambda k: F.conv2d(xs[k % sets], w, padding=1, groups=shape.groups)
+        for k in range(10):
+            conv(k)
+        stream.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for k in range(steps):
+            conv(k)
+        b.record(stream)
+        stream.synchronize()
+        eager_ms = a.elapsed_time(b) / steps
+        outs = [None] * sets
+
+        def step(k):
+            outs[k % sets] = conv(k)
+        graph_ms = graph_step_ms(torch, stream, step, min(steps, 50))
+    print(json.dumps({'ms_per_step': eager_ms, 'graph_ms_per_step': graph_ms,
+                      'timing': 'fresh process; back-to-back calls on one stream (eager) and CUDA-graph replay',
+                      'api': 'torch.nn.functional.conv2d', 'tf32': False, 'benchmark': True,
+                      'cudnn_version': torch.backends.cudnn.version()}))
+    return 0
 
 
 def copy_same_bytes_ms(torch, stream, xs, ys, steps):
@@ -607,48 +736,6 @@ def graph_step_ms(torch, stream, step, count, replays=3):
     ms = a.elapsed_time(b) / (replays * count)
     del graph
     return ms
-
-
-def cudnn_baseline(args, torch, shape, xs, dw, sets, our_step_ms):
-    """torch.nn.functional.conv2d on the same device buffers: TF32 off and read
-    back, cudnn.benchmark on, device time of back-to-back calls."""
-    import torch.nn.functional as F
-    if hasattr(torch.backends, 'fp32_precision'):
-        for target in (torch.backends, torch.backends.cuda.matmul, torch.backends.cudnn,
-                       torch.backends.cudnn.conv):
-            target.fp32_precision = 'ieee'
-        tf32 = torch.backends.cudnn.conv.fp32_precision != 'ieee'
-    else:
-        torch.backends.cuda.matmul.allow_tf32 = False
-        torch.backends.cudnn.allow_tf32 = False
-        tf32 = torch.backends.cudnn.allow_tf32
-    if tf32:
-        raise SystemExit('could not disable TF32 for the cuDNN baseline')
-    torch.backends.cudnn.benchmark = True
-    stream = torch.cuda.Stream()
-    steps = max(20, min(args.steps, 200))
-    with torch.inference_mode(), torch.cuda.stream(stream):
-        for k in range(10):
-            F.conv2d(xs[k % sets], dw, padding=1, groups=shape.groups)
-        stream.synchronize()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        for k in range(steps):
-            F.conv2d(xs[k % sets], dw, padding=1, groups=shape.groups)
-        b.record(stream)
-        stream.synchronize()
-        eager_ms = a.elapsed_time(b) / steps
-        outs = [None] * sets
-
-        def step(k):
-            outs[k % sets] = F.conv2d(xs[k % sets], dw, padding=1, groups=shape.groups)
-        graph_ms = graph_step_ms(torch, stream, step, min(steps, 50))
-    return {'ms_per_step': eager_ms, 'graph_ms_per_step': graph_ms, 'ours_ms_per_step': our_step_ms[0],
-            'ours_graph_ms_per_step': our_step_ms[1], 'speedup_vs_cudnn': eager_ms / our_step_ms[0],
-            'speedup_vs_cudnn_graph': graph_ms / our_step_ms[1],
-            'timing': 'back-to-back calls on one stream (eager) and CUDA-graph replay, both sides',
-            'api': 'torch.nn.functional.conv2d', 'tf32': False, 'benchmark': True,
-            'cudnn_version': torch.backends.cudnn.version()}
 
 
 def set_fp32_precision(torch):
@@ -768,10 +855,8 @@ def run_sweep(args):
     set_fp32_precision(torch)
     torch.backends.cudnn.benchmark = True
     native = api.Native()
-    peaks, peak_kind = measured_peaks()
-    props = torch.cuda.get_device_properties(local)
-    ffma_peak = props.multi_processor_count * 128 * 2 * 1.965e9 / 1e12  # TFLOP/s at max SM clock
-    tensor_peak = peaks['bf16_tflops'] / 6
+    pk = peaks()
+    ffma_peak, tensor_peak = pk['ffma_tflops'], pk['tf32x3_tflops']
     stream = torch.cuda.Stream()
     rows = []
     for s in workloads.sweep_shapes():
@@ -801,9 +886,9 @@ def run_sweep(args):
         if plan.startswith('kernel=tf32x3'):
             bound, frac = 'tensor', tflops / tensor_peak
         elif s.cpg >= 4:
-            bound, frac = 'fp32', max(tflops / ffma_peak, gbs / peaks['hbm_gbs'])
+            bound, frac = 'fp32', max(tflops / ffma_peak, gbs / pk['hbm_gbs'])
         else:
-            bound, frac = 'hbm', gbs / peaks['hbm_gbs']
+            bound, frac = 'hbm', gbs / pk['hbm_gbs']
         rows.append({'shape': [s.n, s.cin, s.h, s.w, s.cpg], 'us': ours * 1e3, 'cudnn_us': theirs * 1e3,
                      'speedup_vs_cudnn': theirs / ours, 'gbs': gbs, 'tflops': tflops, 'bound': bound,
                      'frac': frac, 'points_ok': check['passed'], 'kernel': plan.split()[0].split('=')[1]})
@@ -819,8 +904,7 @@ def run_sweep(args):
             'losses': sum(r['speedup_vs_cudnn'] < 1 / 1.05 for r in rows),
             'all_points_ok': all(r['points_ok'] for r in rows),
             'geomean_roofline_frac': geo(r['frac'] for r in rows),
-            'peaks': {'hbm_gbs': peaks['hbm_gbs'], 'ffma_tflops': ffma_peak, 'tf32x3_tflops': tensor_peak,
-                      'source': peak_kind},
+            'peaks': pk,
             'rows': rows}
     print(json.dumps(line), flush=True)
     return 0 if line['all_points_ok'] else 1
@@ -972,6 +1056,8 @@ def run_model_layers(args):
 
 def main(argv=None):
     args = parse_args(argv)
+    if args.cudnn_leg:
+        return cudnn_leg(args.cudnn_leg)
     if args.impl == 'reference':
         return run_reference(args)
     if args.workload == 'config4_block':

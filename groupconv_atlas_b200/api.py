@@ -184,6 +184,13 @@ class Native:
         lib.gc_b200_last_plan.restype = ct.c_char_p
         lib.gc_b200_device_status.argtypes = [ct.POINTER(ct.c_uint32), ct.c_int]
         lib.gc_b200_selftest_wait_timeout.argtypes = [ct.c_uint32, ct.c_void_p]
+        lib.gc_b200_probe_ffma.argtypes = [ct.c_void_p, ct.c_int, ct.c_int, ct.c_void_p]
+        lib.gc_b200_probe_ffma_flops.argtypes = [ct.c_int, ct.c_int]
+        lib.gc_b200_probe_ffma_flops.restype = ct.c_longlong
+        lib.gc_b200_probe_tf32_mma.argtypes = [ct.c_void_p, ct.c_int, ct.c_int, ct.c_void_p]
+        lib.gc_b200_probe_tf32_mma_flops.argtypes = [ct.c_int, ct.c_int]
+        lib.gc_b200_probe_tf32_mma_flops.restype = ct.c_longlong
+        lib.gc_b200_probe_copy.argtypes = [ct.c_void_p, ct.c_void_p, ct.c_uint64, ct.c_int, ct.c_void_p]
 
     def check(self, status):
         if status:
@@ -230,6 +237,27 @@ class Native:
 
     def selftest_wait_timeout(self, limit_us, stream=0):
         self.check(self.lib.gc_b200_selftest_wait_timeout(native_int(limit_us, 33), self._stream(stream)))
+
+    # Peak-rate probes: each launches one kernel into caller-owned device
+    # buffers (torch tensors here) and returns the work it does.
+    def probe_ffma(self, out, blocks, iters, stream=0):
+        """FFMA chains; returns the FLOPs of the launch."""
+        self.check(self.lib.gc_b200_probe_ffma(ct.c_void_p(out.data_ptr()), native_int(blocks),
+                                               native_int(iters), self._stream(stream)))
+        return self.lib.gc_b200_probe_ffma_flops(native_int(blocks), native_int(iters))
+
+    def probe_tf32_mma(self, status, blocks, iters, stream=0):
+        """Back-to-back tcgen05 TF32 MMAs; returns the FLOPs of the launch."""
+        self.check(self.lib.gc_b200_probe_tf32_mma(ct.c_void_p(status.data_ptr()), native_int(blocks),
+                                                   native_int(iters), self._stream(stream)))
+        return self.lib.gc_b200_probe_tf32_mma_flops(native_int(blocks), native_int(iters))
+
+    def probe_copy(self, src, dst, blocks, stream=0):
+        """Device copy src -> dst; returns the bytes moved (read + write)."""
+        nbytes = src.numel() * src.element_size()
+        self.check(self.lib.gc_b200_probe_copy(ct.c_void_p(src.data_ptr()), ct.c_void_p(dst.data_ptr()),
+                                               nbytes, native_int(blocks), self._stream(stream)))
+        return 2 * nbytes
 
 
 def inputs(shape, seed=20260908):

@@ -30,6 +30,7 @@
 #include "kernel_wide.cuh"
 #include "kernel_tf32x3.cuh"
 #include "kernel_small.cuh"
+#include "kernel_probe.cuh"
 
 namespace {
 
@@ -1386,6 +1387,72 @@ int gc_b200_selftest_wait_timeout(uint32_t limit_us, void *stream) {
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
     return gc_error(GC_OK, "");
+}
+
+// ---- peak-rate probes (the roofline denominators) -------------------------------------
+static int probe_launched() {
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? gc_error(GC_OK, "") : gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+}
+
+static int probe_device_pointer(const void *p) {
+    int current = -1;
+    cudaError_t e = cudaGetDevice(&current);
+    if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+    cudaPointerAttributes attr;
+    std::memset(&attr, 0, sizeof(attr));
+    e = cudaPointerGetAttributes(&attr, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+    }
+    if (attr.type != cudaMemoryTypeDevice || attr.device != current)
+        return gc_error(GC_INVALID, "probe buffers must be device memory of the current device");
+    return GC_OK;
+}
+
+int gc_b200_probe_ffma(float *out, int blocks, int iters, void *stream) {
+    if (out == nullptr || blocks < 1 || blocks > (1 << 20) || iters < 1 || iters > (1 << 24))
+        return gc_error(GC_INVALID, "probe_ffma: out must be non-null, blocks in 1..2^20, iters in 1..2^24");
+    int st = probe_device_pointer(out);
+    if (st != GC_OK) return st;
+    gcb::ffma_probe_kernel<<<blocks, gcb::kProbeThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        out, 1.0f, iters);
+    return probe_launched();
+}
+
+long long gc_b200_probe_ffma_flops(int blocks, int iters) {
+    return 2LL * blocks * gcb::kProbeThreads * iters * gcb::kProbeUnroll * gcb::kProbeChains;
+}
+
+int gc_b200_probe_tf32_mma(uint32_t *status, int blocks, int iters, void *stream) {
+    if (status == nullptr || blocks < 1 || blocks > (1 << 16) || iters < 1 || iters > (1 << 20))
+        return gc_error(GC_INVALID, "probe_tf32_mma: status must be non-null, blocks in 1..65536, "
+                                    "iters in 1..2^20");
+    int st = probe_device_pointer(status);
+    if (st != GC_OK) return st;
+    gcb::tf32_mma_probe_kernel<<<blocks, 128, 0, reinterpret_cast<cudaStream_t>(stream)>>>(status, iters);
+    return probe_launched();
+}
+
+long long gc_b200_probe_tf32_mma_flops(int blocks, int iters) {
+    return 2LL * gcb::kProbeM * gcb::kProbeN * 8 * static_cast<long long>(blocks) * iters;
+}
+
+int gc_b200_probe_copy(const void *src, void *dst, uint64_t bytes, int blocks, void *stream) {
+    if (src == nullptr || dst == nullptr || bytes == 0 || bytes % 16 != 0 || !aligned16(src) || !aligned16(dst) ||
+        blocks < 1 || blocks > (1 << 20))
+        return gc_error(GC_INVALID, "probe_copy: 16-byte aligned non-null buffers, bytes a non-zero multiple "
+                                    "of 16, blocks in 1..2^20");
+    const char *s = static_cast<const char *>(src);
+    const char *d = static_cast<const char *>(dst);
+    if (s < d + bytes && d < s + bytes) return gc_error(GC_INVALID, "probe_copy: buffers overlap");
+    int st = probe_device_pointer(src);
+    if (st == GC_OK) st = probe_device_pointer(dst);
+    if (st != GC_OK) return st;
+    gcb::copy_probe_kernel<<<blocks, gcb::kProbeThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+        static_cast<const float4 *>(src), static_cast<float4 *>(dst), static_cast<long long>(bytes / 16));
+    return probe_launched();
 }
 
 }  // extern "C"

@@ -463,10 +463,12 @@ __global__ void __launch_bounds__(kWsMaxThreads) direct_ws_kernel(const __grid_c
         }
         // Before the CTA's shared memory is released, the copies still in
         // flight must land: the last STAGES items (all earlier ones were
-        // consumed before their stage was refilled).  Bounded.
-        if (!ok)
-            for (int i = max(0, issued - STAGES); i < issued; ++i)
-                mbar_wait_bounded(&full[i % STAGES], static_cast<uint32_t>((i / STAGES) & 1));
+        // consumed before their stage was refilled).  Always, not only when
+        // this warp gave up: the compute or weight warps may have given up
+        // while its last copies were still arriving.  Bounded.
+        (void)ok;
+        for (int i = max(0, issued - STAGES); i < issued; ++i)
+            mbar_wait_bounded(&full[i % STAGES], static_cast<uint32_t>((i / STAGES) & 1));
         return;
     }
 

@@ -7,6 +7,7 @@
 // Errors come back as gc_status values with the library's thread-local
 // message; nothing here computes a convolution.
 #include <torch/extension.h>
+#include <c10/cuda/CUDAGuard.h>
 #include <c10/cuda/CUDAStream.h>
 
 #include <stdexcept>
@@ -40,6 +41,10 @@ at::Tensor conv(const at::Tensor &x, const at::Tensor &w, int64_t cout, int64_t 
     int64_t ho = 0, wo = 0;
     int st = gc_validate_shape(&p, &ho, &wo);
     if (st != GC_OK) throw std::runtime_error("gc_status " + std::to_string(st) + ": " + gc_last_error());
+    // gc_cuda_conv requires the tensors' device to be the current device (as
+    // nn.Conv2d runs on its input's device whatever the current one is).
+    c10::OptionalDeviceGuard guard;
+    if (x.is_cuda()) guard.reset_device(x.device());
     at::Tensor y = at::empty({p.n, cout, ho, wo}, x.options());
     const gc_tensor xd = describe(x), wd = describe(w);
     gc_tensor yd = describe(y);

@@ -65,10 +65,11 @@ class B200Conv2d(torch.nn.Module):
             (lambda dev: torch.cuda.current_stream(dev).cuda_stream)
 
     def _descriptors(self, x: torch.Tensor):
-        """Per input geometry and device: the convolution's Shape, its output
-        size, the ctypes descriptors (only their data pointers change per
-        call) and their addresses."""
-        key = (x.shape, x.get_device())
+        """Per input geometry, device and dtype (input and weight): the
+        convolution's Shape, its output size, the ctypes descriptors (only
+        their data pointers change per call; their dtype and byte counts are
+        part of the key) and their addresses."""
+        key = (x.shape, x.get_device(), x.dtype, self.weight.dtype)
         entry = self._cache.get(key)
         if entry is None:
             shape = api.Shape(n=x.shape[0], h=x.shape[2], w=x.shape[3], **self.geometry)
@@ -90,6 +91,11 @@ class B200Conv2d(torch.nn.Module):
                     status, _, message = text[len('gc_status '):].partition(': ')
                     raise api.NativeError(int(status), message) from None
                 raise
+        if x.is_cuda and x.get_device() != torch.cuda.current_device():
+            # gc_cuda_conv runs on the current device, which must hold the
+            # tensors (nn.Conv2d runs on its input's device)
+            with torch.cuda.device(x.device):
+                return self.forward(x)
         _, out_shape, (_, xd, wd, yd), (pa, xa, wa, ya) = self._descriptors(x)
         y = x.new_empty(out_shape)
         xd.data = x.data_ptr()

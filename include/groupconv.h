@@ -140,6 +140,29 @@ int gc_b200_device_status(uint32_t *status, int clear);
  * test check the timeout path without faulting or hanging the GPU. */
 int gc_b200_selftest_wait_timeout(uint32_t limit_us, void *stream);
 
+/* Peak-rate probes: the denominators of the roofline fractions, measured on
+ * the GPU itself (the reference's equivalent for its RTX 4090 is
+ * csrc/cuda/microbench.cu:15-29, a logical copy and eight FMA chains).  Each
+ * launches one kernel on `stream` into caller-owned device buffers of the
+ * current device and returns at once; the caller times it with events.
+ *   gc_b200_probe_ffma      `blocks` x 256 threads, 8 independent FFMA
+ *                           chains each; out holds blocks * 256 floats.
+ *                           FLOPs = gc_b200_probe_ffma_flops(blocks, iters).
+ *   gc_b200_probe_tf32_mma  `blocks` CTAs (one per SM), each issuing `iters`
+ *                           back-to-back tcgen05.mma.kind::tf32 of
+ *                           M = 128, N = 256, K = 8 into TMEM; status holds
+ *                           `blocks` words, 0 = completed, 1 = the bounded
+ *                           wait for the commit gave up.
+ *                           FLOPs = gc_b200_probe_tf32_mma_flops(blocks, iters).
+ *   gc_b200_probe_copy      16-byte grid-stride copy src -> dst of `bytes`
+ *                           (a multiple of 16; 16-byte aligned buffers that
+ *                           do not overlap); bytes moved = 2 * bytes. */
+int gc_b200_probe_ffma(float *out, int blocks, int iters, void *stream);
+long long gc_b200_probe_ffma_flops(int blocks, int iters);
+int gc_b200_probe_tf32_mma(uint32_t *status, int blocks, int iters, void *stream);
+long long gc_b200_probe_tf32_mma_flops(int blocks, int iters);
+int gc_b200_probe_copy(const void *src, void *dst, uint64_t bytes, int blocks, void *stream);
+
 #ifdef __cplusplus
 }
 /* Internal shared error helper; returns the supplied status

@@ -3,7 +3,7 @@
 Run in a checkout where the reference tree is available (it is read, never
 copied):
 
-    python tests/golden/make_atlas.py --reference /root/reference
+    python tests/golden/make_atlas.py --reference <reference checkout>
 
 It writes ``atlas_fixture.json`` next to this script:
 

@@ -3,8 +3,8 @@
 Run in a checkout where the reference tree is available (it is read, never
 copied):
 
-    make -C oracle ref                       # compile the reference CPU library
-    python tests/golden/make_golden.py --reference /root/reference
+    make -C oracle ref REF=<reference checkout>   # compile the reference CPU library
+    GC_REFERENCE_TREE=<reference checkout> python tests/golden/make_golden.py
 
 It writes, next to this script:
 
@@ -23,6 +23,7 @@ B-geometry matrix subset and general-geometry sweep (tests/native_cuda.cu:
 """
 from __future__ import annotations
 
+import os
 import argparse
 import ctypes as ct
 import dataclasses
@@ -38,8 +39,11 @@ REPO = HERE.parents[1]
 
 def main():
     parser = argparse.ArgumentParser()
-    parser.add_argument('--reference', default='/root/reference')
+    parser.add_argument('--reference', default=os.environ.get('GC_REFERENCE_TREE'),
+                        help='the reference checkout (default: $GC_REFERENCE_TREE)')
     args = parser.parse_args()
+    if not args.reference:
+        raise SystemExit('name the reference checkout: --reference PATH or GC_REFERENCE_TREE')
     sys.path.insert(0, args.reference)
     sys.path.insert(0, str(REPO))
     from bench.api import Shape, inputs  # the reference's own Python

@@ -81,3 +81,34 @@ def test_cpp_front_end_matches_ctypes_path(native, torch_cuda, geo):
     torch.cuda.synchronize()
     assert torch.equal(a, b)
     assert orc.error_metrics(a.cpu().numpy(), ref.cpu().numpy())['passed']
+
+
+def test_ctypes_descriptor_cache_is_keyed_by_dtype(native):
+    """A float64 input after a float32 one must not reuse float32 descriptors:
+    the call is rejected (GC_INVALID: the CUDA backend computes FP32 only)
+    instead of running on stale dtype and byte counts."""
+    from groupconv_atlas_b200 import api
+    conv = torch.nn.Conv2d(4, 4, 3, padding=1, groups=4, bias=False)
+    mod = torch_module.B200Conv2d(conv, native, cpp=False)
+    a = mod._descriptors(torch.zeros(1, 4, 6, 6))
+    b = mod._descriptors(torch.zeros(1, 4, 6, 6, dtype=torch.float64))
+    assert a is not b and b[2][1].dtype == api.tensor(torch.zeros(1, dtype=torch.float64)).dtype
+    with pytest.raises(api.NativeError) as err:
+        mod(torch.zeros(1, 4, 6, 6, dtype=torch.float64))
+    assert err.value.status == 1
+
+
+@pytest.mark.gpu
+def test_input_on_a_device_other_than_the_current_one(native, torch_cuda):
+    if torch.cuda.device_count() < 2:
+        pytest.skip('needs two CUDA devices')
+    conv = torch.nn.Conv2d(16, 16, 3, padding=1, groups=4, bias=False).to('cuda:1')
+    x = torch.randn(2, 16, 12, 12, device='cuda:1')
+    torch.cuda.set_device(0)
+    with torch.inference_mode():
+        ref = torch.nn.functional.conv2d(x, conv.weight, padding=1, groups=4)
+        for cpp in (True, False):
+            y = torch_module.B200Conv2d(conv, native, cpp=cpp)(x)
+            assert y.device == x.device
+            torch.cuda.synchronize(1)
+            assert orc.error_metrics(y.cpu().numpy(), ref.cpu().numpy())['passed']
