@@ -39,6 +39,7 @@ def config5_inputs():
 def _device_run(native, torch, shape, dx, dw, impl=3, sentinel=True):
     dy = torch.full(shape.output, float('nan') if sentinel else 0.0, device='cuda')
     stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())  # the inputs' copies and the NaN fill come first
     with torch.cuda.stream(stream):
         native.cuda(shape, dx, dw, dy, impl, stream.cuda_stream)
         plan = native.last_plan()
@@ -55,6 +56,7 @@ def test_config5_full_batch_one_call(native, torch_cuda, config5_inputs, groups)
     dw = torch.from_numpy(wl.w).cuda()
     dy, plan = _device_run(native, torch, s, dx, dw)
     assert native.device_status(clear=True) == 0
+    assert not torch.isnan(dy).any().item(), f'unwritten outputs [{plan}]'
     one = dataclasses.replace(s, n=1)
     for img in (0, 511, 1023):
         y = dy[img:img + 1].cpu().numpy()
@@ -78,6 +80,7 @@ def test_config5_units_of_eight_ranks_on_one_gpu(native, torch_cuda, config5_inp
     whole, plan = _device_run(native, torch, s, dx, dw)
     dy = torch.full(s.output, float('nan'), device='cuda')
     stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
     firsts = []
     with torch.cuda.stream(stream):
         for rank in range(8):
@@ -113,6 +116,7 @@ def test_group_block_units_on_one_gpu(native, torch_cuda, n, groups, world):
     dx, dw = torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda()
     dy = torch.full(s.output, float('nan'), device='cuda')
     stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
     count = 0
     with torch.cuda.stream(stream):
         for rank in range(world):
