@@ -937,6 +937,9 @@ def paired_shape_rows(args, entries):
         # Cout) only; every other layer runs on implementation 0
         impl = 3 if (s.r, s.s, s.sh, s.sw, s.ph, s.pw, s.dh, s.dw, s.cin) == (3, 3, 1, 1, 1, 1, 1, 1, s.cout) else 0
         x_host, w_host = api.inputs(s)
+        with_bias = bool(extra.pop('with_bias', False))
+        b_host = (np.random.default_rng(int(s.id[3:11], 16)).uniform(-1, 1, s.cout).astype(np.float32)
+                  if with_bias else None)
         nbytes = 4 * (math.prod(s.input) + math.prod(s.output) + math.prod(s.weight))
         sets = int(max(1, min(8, math.ceil(3 * L2_BYTES / nbytes))))
         g = torch.Generator(device='cuda').manual_seed(int(s.id[3:11], 16))
@@ -945,10 +948,16 @@ def paired_shape_rows(args, entries):
                                                       for _ in range(sets - 1)]
             ys = [torch.empty(s.output, device='cuda') for _ in range(sets)]
             w = torch.from_numpy(w_host).cuda()
-            native.cuda(s, xs[0], w, ys[0], impl, stream.cuda_stream)
+            db = torch.from_numpy(b_host).cuda() if with_bias else None
+            if with_bias:
+                native.conv_ex(s, xs[0], w, ys[0], bias=db, stream=stream.cuda_stream)
+            else:
+                native.cuda(s, xs[0], w, ys[0], impl, stream.cuda_stream)
             plan = native.last_plan()
             stream.synchronize()
             y0 = ys[0].cpu().numpy()
+        if with_bias:  # the convolution part of the output is what the oracle checks
+            y0 = y0 - b_host[None, :, None, None]
         check = orc.check_points(s, x_host, w_host, y0)
         abs_sum = orc.oracle_points(s, np.abs(x_host), np.abs(w_host), check['points'])
         got = np.array([float(y0[p]) for p in check['points']])
@@ -956,8 +965,13 @@ def paired_shape_rows(args, entries):
         bound_ok = bool(np.all(np.abs(got - expected) <= orc.BOUND_FACTOR * abs_sum))
         del x_host, y0
         conv = dict(stride=(s.sh, s.sw), padding=(s.ph, s.pw), dilation=(s.dh, s.dw), groups=s.groups)
-        calls = {'ours': lambda k: native.cuda(s, xs[k % sets], w, ys[k % sets], impl, stream.cuda_stream),
-                 'cudnn': lambda k: F.conv2d(xs[k % sets], w, **conv)}
+        if with_bias:
+            calls = {'ours': lambda k: native.conv_ex(s, xs[k % sets], w, ys[k % sets], bias=db,
+                                                      stream=stream.cuda_stream),
+                     'cudnn': lambda k: F.conv2d(xs[k % sets], w, db, **conv)}
+        else:
+            calls = {'ours': lambda k: native.cuda(s, xs[k % sets], w, ys[k % sets], impl, stream.cuda_stream),
+                     'cudnn': lambda k: F.conv2d(xs[k % sets], w, **conv)}
         graphs, repeats = {}, {}
         with torch.cuda.stream(stream), torch.inference_mode():
             for name, call in calls.items():
@@ -987,7 +1001,8 @@ def paired_shape_rows(args, entries):
                     us = [ev[2 * i].elapsed_time(ev[2 * i + 1]) * 1e3 / repeats[name] for i in range(samples)]
                     medians[name].append(statistics.median(us))
         cmp = stats.compare_batches(medians['cudnn'], medians['ours'])
-        rows.append({**extra, 'shape': [s.n, s.cin, s.h, s.w, s.cpg], 'stride': s.sh, 'implementation': impl,
+        rows.append({**extra, 'shape': [s.n, s.cin, s.h, s.w, s.cpg], 'stride': s.sh,
+                     'implementation': 'gc_b200_conv_ex (bias)' if with_bias else impl,
                      'shape_id': s.id,
                      'kernel': plan.split()[0].split('=')[1], 'us': statistics.median(medians['ours']),
                      'cudnn_us': statistics.median(medians['cudnn']), 'speedup_vs_cudnn': cmp['speedup'],
@@ -1032,9 +1047,11 @@ def run_atlas(args):
 
 
 def run_model_layers(args):
-    """The reference's 12 frozen model-layer operations: the 8 without bias
-    measured like the Atlas; the 4 biased ConvNeXt layers reported as
-    unsupported (the ABI has no bias), as bench/model_run.py does."""
+    """The reference's 12 frozen model-layer operations measured like the
+    Atlas: the 8 without bias through gc_cuda_conv, the 4 biased ConvNeXt
+    7x7 depthwise layers (which the reference reports as unsupported,
+    bench/model_run.py:46-49) through gc_b200_conv_ex with their bias, against
+    torch's conv2d with the same bias."""
     import torch
     from groupconv_atlas_b200 import workloads
     rank, world, local = dist_setup()
@@ -1044,14 +1061,13 @@ def run_model_layers(args):
     set_fp32_precision(torch)
     torch.backends.cudnn.benchmark = True
     layers = workloads.model_layers()
-    rows = paired_shape_rows(args, [(l.shape, {'model': l.model, 'module_path': l.module_path})
-                                    for l in layers if not l.bias])
-    unsupported = [{'model': l.model, 'module_path': l.module_path, 'n': l.shape.n, 'status': 'UNSUPPORTED',
-                    'reason': 'bias not implemented'} for l in layers if l.bias]
-    return shape_set_line(args, 'model_layers', 'model layers: geomean speedup of gc_cuda_conv over torch/cuDNN '
-                          '(TF32 off), 8 no-bias layers', rows,
-                          'synthetic: the reference seeding per shape id, x, w ~U[-1,1)',
-                          {'unsupported': unsupported})
+    rows = paired_shape_rows(args, [(l.shape, {'model': l.model, 'module_path': l.module_path,
+                                               'bias': l.bias, 'with_bias': l.bias}) for l in layers])
+    return shape_set_line(args, 'model_layers', 'model layers: geomean speedup over torch/cuDNN (TF32 off), '
+                          '12 layers: 8 through gc_cuda_conv, the 4 biased ConvNeXt 7x7 depthwise layers '
+                          'through gc_b200_conv_ex', rows,
+                          'synthetic: the reference seeding per shape id, x, w ~U[-1,1), bias ~U[-1,1) seeded per '
+                          'shape id')
 
 
 def main(argv=None):

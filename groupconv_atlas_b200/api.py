@@ -34,6 +34,9 @@ GC_OK, GC_INVALID, GC_UNSUPPORTED, GC_DEVICE_ERROR, GC_UNAVAILABLE = range(5)
 AUTO, GENERAL, DIRECT_LDG, DIRECT_TMA, TF32X3, SMALL, KSTREAM = range(7)
 KERNELS = {'auto': AUTO, 'general': GENERAL, 'direct_ldg': DIRECT_LDG,
            'direct_tma': DIRECT_TMA, 'tf32x3': TF32X3, 'small': SMALL, 'kstream': KSTREAM}
+# Layouts of gc_b200_conv_ex.
+NCHW, NHWC = 0, 1
+LAYOUTS = {'nchw': NCHW, 'nhwc': NHWC}
 STATUS_TMA_TIMEOUT = 0x1
 STATUS_MMA_TIMEOUT = 0x2
 
@@ -184,6 +187,7 @@ class Native:
         lib.gc_b200_last_plan.restype = ct.c_char_p
         lib.gc_b200_device_status.argtypes = [ct.POINTER(ct.c_uint32), ct.c_int]
         lib.gc_b200_selftest_wait_timeout.argtypes = [ct.c_uint32, ct.c_void_p]
+        lib.gc_b200_conv_ex.argtypes = [ct.POINTER(CShape)] + [ct.POINTER(Tensor)] * 4 + [ct.c_int, ct.c_void_p]
         lib.gc_b200_probe_ffma.argtypes = [ct.c_void_p, ct.c_int, ct.c_int, ct.c_void_p]
         lib.gc_b200_probe_ffma_flops.argtypes = [ct.c_int, ct.c_int]
         lib.gc_b200_probe_ffma_flops.restype = ct.c_longlong
@@ -224,6 +228,17 @@ class Native:
         stream = self._stream(stream)
         self.check(self.lib.gc_b200_conv(ct.byref(p), ct.byref(xd), ct.byref(wd), ct.byref(yd),
                                          native_int(kernel), stream))
+        return y
+
+    def conv_ex(self, shape, x, w, y, bias=None, layout='nchw', stream=0):
+        """gc_b200_conv_ex: optional bias (rank-1, Cout) and layout 'nchw' or
+        'nhwc' (x and y channels-last, e.g. torch.channels_last tensors)."""
+        lay = LAYOUTS.get(layout, layout) if isinstance(layout, str) else layout
+        p, xd, wd, yd = cshape(shape), tensor(x), tensor(w), tensor(y)
+        bd = tensor(bias) if bias is not None else None
+        self.check(self.lib.gc_b200_conv_ex(ct.byref(p), ct.byref(xd), ct.byref(wd),
+                                            ct.byref(bd) if bd is not None else None, ct.byref(yd),
+                                            native_int(lay), self._stream(stream)))
         return y
 
     def last_plan(self):

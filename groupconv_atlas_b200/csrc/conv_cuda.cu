@@ -31,6 +31,7 @@
 #include "kernel_tf32x3.cuh"
 #include "kernel_small.cuh"
 #include "kernel_kstream.cuh"
+#include "kernel_nhwc.cuh"
 #include "kernel_probe.cuh"
 
 namespace {
@@ -44,7 +45,7 @@ constexpr int kStages = 3;
 // when gc_b200_last_plan asks for it (formatting costs about a third of a
 // microsecond, a tenth of the host time of a call).
 struct PlanRecord {
-    enum Kind { kNone, kDirect, kWide, kTf32, kSmall, kGeneral, kDw, kDwS2, kKstream } kind = kNone;
+    enum Kind { kNone, kDirect, kWide, kTf32, kSmall, kGeneral, kDw, kDwS2, kKstream, kNhwc } kind = kNone;
     const char *name = "";  // variant name, static storage
     bool tma = false;
     long long v[14] = {};
@@ -101,6 +102,10 @@ std::string format_plan(const PlanRecord &r) {
                       "kernel=kstream engine=group8 grid=%lld block=%lld smem=%lld gi=%lld items=%lld stages=%lld "
                       "band=8 cell=8x2x7 vec_store=%lld",
                       v[0], v[1], v[2], v[3], v[4], v[5], v[6]);
+        break;
+    case PlanRecord::kNhwc:
+        std::snprintf(buf, sizeof(buf), "kernel=nhwc engine=%s grid=%lld block=256 cpg=%lld bias=%lld", r.name, v[0],
+                      v[1], v[2]);
         break;
     case PlanRecord::kGeneral:
         std::snprintf(buf, sizeof(buf), "kernel=general grid=%lld block=%lld run=%lld cob=%lld index=%s runs=%lld",
@@ -1127,7 +1132,7 @@ bool dw_eligible(const gc_shape *p, int64_t ho, int64_t wo) {
 }
 
 int launch_dw(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const float *w, float *y, int dev,
-              cudaStream_t stream) {
+              cudaStream_t stream, const float *bias = nullptr) {
     DeviceFacts facts;
     int st = device_facts(dev, facts);
     if (st != GC_OK) return st;
@@ -1143,6 +1148,7 @@ int launch_dw(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const f
     P.x = x;
     P.w = w;
     P.y = y;
+    P.bias = bias;
     P.n = static_cast<int>(p->n);
     P.c = static_cast<int>(p->cin);
     P.h = static_cast<int>(p->h);
@@ -1190,7 +1196,7 @@ bool dw_s2_eligible(const gc_shape *p) {
 }
 
 int launch_dw_s2(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const float *w, float *y, int dev,
-                 cudaStream_t stream) {
+                 cudaStream_t stream, const float *bias = nullptr) {
     DeviceFacts facts;
     int st = device_facts(dev, facts);
     if (st != GC_OK) return st;
@@ -1198,6 +1204,7 @@ int launch_dw_s2(const gc_shape *p, int64_t ho, int64_t wo, const float *x, cons
     P.x = x;
     P.w = w;
     P.y = y;
+    P.bias = bias;
     P.n = static_cast<int>(p->n);
     P.c = static_cast<int>(p->cin);
     P.h = static_cast<int>(p->h);
@@ -1235,9 +1242,9 @@ const void *general_kernel_for(bool narrow) {
 }
 
 int launch_general(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const float *w,
-                   float *y, int dev, cudaStream_t stream) {
-    if (dw_s2_eligible(p)) return launch_dw_s2(p, ho, wo, x, w, y, dev, stream);
-    if (dw_eligible(p, ho, wo)) return launch_dw(p, ho, wo, x, w, y, dev, stream);
+                   float *y, int dev, cudaStream_t stream, const float *bias = nullptr) {
+    if (dw_s2_eligible(p)) return launch_dw_s2(p, ho, wo, x, w, y, dev, stream, bias);
+    if (dw_eligible(p, ho, wo)) return launch_dw(p, ho, wo, x, w, y, dev, stream, bias);
     DeviceFacts facts;
     int st = device_facts(dev, facts);
     if (st != GC_OK) return st;
@@ -1245,6 +1252,7 @@ int launch_general(const gc_shape *p, int64_t ho, int64_t wo, const float *x, co
     P.xp = x;
     P.wp = w;
     P.yp = y;
+    P.bias = bias;
     P.n = p->n;
     P.cin = p->cin;
     P.cout = p->cout;
@@ -1286,6 +1294,92 @@ int launch_general(const gc_shape *p, int64_t ho, int64_t wo, const float *x, co
     cudaError_t e = launch_pdl(fn, dim3(static_cast<unsigned>(blocks)), dim3(threads), args, 0, stream);
     if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
     record_plan(PlanRecord::kGeneral, "", false, blocks, threads, kGeneralRun, cob, narrow ? 1 : 0, P.total_runs);
+    return GC_OK;
+}
+
+// ---- channels-last (NHWC) tensors (kernel_nhwc.cuh) --------------------------------------
+bool channels_last_strides(const gc_tensor *t) {
+    return t->rank == 4 && t->strides[1] == 1 && t->strides[3] == t->dims[1] &&
+           t->strides[2] == t->dims[3] * t->dims[1] && t->strides[0] == t->dims[2] * t->dims[3] * t->dims[1];
+}
+
+int launch_nhwc(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const float *w, const float *bias,
+                float *y, int dev, cudaStream_t stream) {
+    DeviceFacts facts;
+    int st = device_facts(dev, facts);
+    if (st != GC_OK) return st;
+    const long long cpg = p->cin / p->groups;
+    const bool b = p->cin == p->cout && p->r == 3 && p->s == 3 && p->sh == 1 && p->sw == 1 && p->ph == 1 &&
+                   p->pw == 1 && p->dh == 1 && p->dw == 1;
+    const bool vec = b && p->cin % 4 == 0 && aligned16(x) && aligned16(y) && (cpg == 1 || cpg == 2 || cpg % 4 == 0) &&
+                     p->h < (1LL << 30) && p->w < (1LL << 30) && p->cin < (1LL << 30);
+    cudaError_t e;
+    if (vec) {
+        gcb::NhwcParams P{};
+        P.x = x;
+        P.w = w;
+        P.bias = bias;
+        P.y = y;
+        P.n = static_cast<int>(std::min<long long>(p->n, 1LL << 30));
+        P.c = static_cast<int>(p->cin);
+        P.h = static_cast<int>(p->h);
+        P.wd = static_cast<int>(p->w);
+        P.cpg = static_cast<int>(cpg);
+        P.qcols = static_cast<int>(ceil_div(p->w, gcb::kNhwcPx));
+        P.cquads = static_cast<int>(p->cin / 4);
+        P.cells = p->n * p->h * P.qcols * P.cquads;
+        const void *fn = cpg == 1   ? reinterpret_cast<const void *>(&gcb::nhwc_conv_kernel<1>)
+                         : cpg == 2 ? reinterpret_cast<const void *>(&gcb::nhwc_conv_kernel<2>)
+                                    : reinterpret_cast<const void *>(&gcb::nhwc_conv_kernel<0>);
+        const long long blocks = std::min<long long>(ceil_div(P.cells, 256), static_cast<long long>(facts.sms) * 8);
+        void *args[] = {&P};
+        e = launch_pdl(fn, dim3(static_cast<unsigned>(blocks)), dim3(256), args, 0, stream);
+        if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+        record_plan(PlanRecord::kNhwc, "vector4x4", false, blocks, cpg, bias != nullptr ? 1 : 0);
+        return GC_OK;
+    }
+    gcb::NhwcScalarParams P{};
+    P.x = x;
+    P.wt = w;
+    P.bias = bias;
+    P.y = y;
+    P.n = p->n;
+    P.cin = p->cin;
+    P.cout = p->cout;
+    P.h = p->h;
+    P.w = p->w;
+    P.r = p->r;
+    P.s = p->s;
+    P.groups = p->groups;
+    P.sh = p->sh;
+    P.sw = p->sw;
+    P.ph = p->ph;
+    P.pw = p->pw;
+    P.dh = p->dh;
+    P.dw = p->dw;
+    P.ho = ho;
+    P.wo = wo;
+    P.total = p->n * ho * wo * p->cout;
+    const long long blocks = std::min<long long>(ceil_div(P.total, 256), static_cast<long long>(facts.sms) * 8);
+    void *args[] = {&P};
+    e = launch_pdl(reinterpret_cast<const void *>(&gcb::nhwc_scalar_kernel), dim3(static_cast<unsigned>(blocks)),
+                   dim3(256), args, 0, stream);
+    if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+    record_plan(PlanRecord::kNhwc, "scalar", false, blocks, cpg, bias != nullptr ? 1 : 0);
+    return GC_OK;
+}
+
+// Structure of an optional bias descriptor: rank 1, Cout dense FP32 elements
+// on the CUDA device of the data tensors.
+int check_bias_descriptor(const gc_tensor *b, const gc_shape *p, const gc_tensor *x) {
+    if (b->data == nullptr) return gc_error(GC_INVALID, "bias data pointer is null");
+    if (b->dtype != GC_F32) return gc_error(GC_INVALID, "bias dtype must be F32");
+    if (b->device != GC_CUDA || b->device_index != x->device_index)
+        return gc_error(GC_INVALID, "bias must be CUDA memory on the tensors' device");
+    if (b->rank != 1 || b->dims[0] != p->cout) return gc_error(GC_INVALID, "bias must be a rank-1 tensor of Cout");
+    if (b->bytes < static_cast<uint64_t>(p->cout) * 4u) return gc_error(GC_INVALID, "bias buffer too small");
+    if ((reinterpret_cast<uintptr_t>(b->data) & 3u) != 0) return gc_error(GC_INVALID, "bias is not 4-byte aligned");
+    if (b->strides[0] != 1) return gc_error(GC_UNSUPPORTED, "bias must be dense");
     return GC_OK;
 }
 
@@ -1468,6 +1562,51 @@ int gc_b200_conv(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_t
     if (st != GC_OK) return st;
     if (kernel == GC_B200_AUTO) kernel = b ? auto_kernel(p, x, w, dev) : GC_B200_GENERAL;
     return run_kernel(p, x, w, y, kernel, dev, stream);
+}
+
+int gc_b200_conv_ex(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, const gc_tensor *bias,
+                    gc_tensor *y, int layout, void *stream) {
+    if (p == nullptr || x == nullptr || w == nullptr || y == nullptr)
+        return gc_error(GC_INVALID, "null shape or tensor descriptor");
+    if (layout != GC_B200_NCHW && layout != GC_B200_NHWC) return gc_error(GC_UNSUPPORTED, "unknown layout");
+    int st = GC_OK;
+    if (layout == GC_B200_NCHW) {
+        st = gc_validate_tensors(p, x, w, y, GC_CUDA, GC_F32);
+    } else {
+        // every GC_INVALID condition first (checked on dense-NCHW views of the
+        // same sizes), then the channels-last layout of x and y
+        gc_tensor xd = *x, yd = *y;
+        for (gc_tensor *t : {&xd, &yd}) {
+            t->strides[3] = 1;
+            t->strides[2] = t->dims[3];
+            t->strides[1] = t->dims[2] * t->dims[3];
+            t->strides[0] = t->dims[1] * t->dims[2] * t->dims[3];
+        }
+        st = gc_validate_tensors(p, &xd, w, &yd, GC_CUDA, GC_F32);
+        if (st == GC_OK && (!channels_last_strides(x) || !channels_last_strides(y)))
+            st = gc_error(GC_UNSUPPORTED, "NHWC layout needs channels-last strides (H*W*C, 1, W*C, C) for x and y");
+    }
+    if (st != GC_OK) return st;
+    if (bias != nullptr && (st = check_bias_descriptor(bias, p, x)) != GC_OK) return st;
+    int dev = -1;
+    st = device_and_stream_checks(x, w, y, stream, dev);
+    if (st != GC_OK) return st;
+    if (bias != nullptr && (st = check_pointer(bias, dev)) != GC_OK) return st;
+    const bool b = b_geometry(p);
+    if (layout == GC_B200_NCHW && bias == nullptr)
+        return run_kernel(p, x, w, y, b ? auto_kernel(p, x, w, dev) : GC_B200_GENERAL, dev, stream, true);
+    int64_t ho = 0, wo = 0;
+    st = gc_validate_shape(p, &ho, &wo);
+    if (st != GC_OK) return st;
+    const float *xp = static_cast<const float *>(x->data), *wp = static_cast<const float *>(w->data);
+    const float *bp = bias != nullptr ? static_cast<const float *>(bias->data) : nullptr;
+    float *yp = static_cast<float *>(y->data);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    st = layout == GC_B200_NCHW ? launch_general(p, ho, wo, xp, wp, yp, dev, s, bp)
+                                : launch_nhwc(p, ho, wo, xp, wp, bp, yp, dev, s);
+    if (st != GC_OK) return st;
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? gc_error(GC_OK, "") : gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
 }
 
 const char *gc_b200_last_plan(void) {

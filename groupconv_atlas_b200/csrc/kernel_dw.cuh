@@ -14,7 +14,7 @@
 // (coalesced stores).  Two stages alternate: the copies of a CTA's next item
 // are in flight while it computes the current one.  The per-output sum runs
 // over (r, s) in row-major order with fused multiply-adds from zero, as the
-// reference's k0 does.
+// reference's k0 does; an optional per-channel bias is added after the sum.
 #pragma once
 #include <cstdint>
 
@@ -26,6 +26,7 @@ struct DwParams {
     const float *x;
     const float *w;
     float *y;
+    const float *bias;           // nullable: per-channel bias added after the sum
     int n, c, h, wd;             // input
     int sh, sw, ph, pw, dh, dw;  // geometry (kernel size is the template K)
     int ho, wo;                  // output
@@ -83,6 +84,8 @@ __global__ void __launch_bounds__(256) dw_conv_kernel(const __grid_constant__ Dw
         float wr[K * K];
 #pragma unroll
         for (int q = 0; q < K * K; ++q) wr[q] = __ldg(P.w + static_cast<long long>(c) * (K * K) + q);
+        const bool has_bias = P.bias != nullptr;
+        const float bv = has_bias ? __ldg(P.bias + c) : 0.0f;
         const float *st = tile + (k & 1) * stage_floats;
         float *yp = P.y + plane * plane_out + static_cast<long long>(oh0) * P.wo;
         if constexpr (UNIT) {
@@ -105,6 +108,9 @@ __global__ void __launch_bounds__(256) dw_conv_kernel(const __grid_constant__ Dw
                         for (int s = 0; s < K; ++s) acc[j] = fmaf(v[j + s], wr[r * K + s], acc[j]);
                 }
                 float *yr = yp + static_cast<long long>(orow) * P.wo + ow0;
+                if (has_bias)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) acc[j] += bv;
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
                     if (ow0 + j < P.wo) yr[j] = acc[j];
@@ -119,7 +125,7 @@ __global__ void __launch_bounds__(256) dw_conv_kernel(const __grid_constant__ Dw
                 for (int r = 0; r < K; ++r)
 #pragma unroll
                     for (int s = 0; s < K; ++s) acc = fmaf(t0[r * P.dh * P.pitch + s * P.dw], wr[r * K + s], acc);
-                yp[o] = acc;
+                yp[o] = has_bias ? acc + bv : acc;
             }
         }
         __syncthreads();  // every thread is done with this stage before it is refilled
@@ -144,6 +150,7 @@ struct DwS2Params {
     const float *x;
     const float *w;
     float *y;
+    const float *bias;  // nullable: per-channel bias added after the sum
     int n, c, h, wd, ho, wo;
     int qcols;        // ceil(wo / 4)
     int prows;        // ceil(ho / 2)
@@ -219,6 +226,11 @@ __global__ void __launch_bounds__(256) dw_s2_conv_kernel(const __grid_constant__
 #pragma unroll
                     for (int s = 0; s < K; ++s) acc = fmaf(v[S * rr + r][S * q + s], wr[r * K + s], acc);
                 o[q] = acc;
+            }
+            if (P.bias != nullptr) {
+                const float bv = __ldg(P.bias + c);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) o[q] += bv;
             }
             float *yr = yp + static_cast<long long>(oh) * P.wo + ow0;
             if (P.vec_out && ow0 + 3 < P.wo) {

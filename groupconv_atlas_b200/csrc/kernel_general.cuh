@@ -9,7 +9,8 @@
 // Consecutive threads take consecutive runs of a row, so input loads are
 // coalesced (at the layer's stride) and the threads of a warp share weights
 // (L1 broadcast).  Grid-stride over runs; index arithmetic in 32 bits when
-// every tensor has fewer than 2^31 elements, else 64 bits.
+// every tensor has fewer than 2^31 elements, else 64 bits.  An optional
+// per-output-channel bias is added after the sum.
 #pragma once
 #include <cstdint>
 
@@ -21,6 +22,7 @@ struct GeneralParams {
     const float *xp;
     const float *wp;
     float *yp;
+    const float *bias;  // nullable: per-output-channel bias added after the sum
     long long n, cin, cout, h, w, r, s, groups, sh, sw, ph, pw, dh, dw;
     long long ho, wo;
     long long runs_per_row;  // ceil(wo / RUN)
@@ -81,6 +83,13 @@ __global__ void __launch_bounds__(256) general_conv_kernel(const __grid_constant
             }
         }
         float *out = P.yp + ((n * static_cast<I>(P.cout) + co0) * HO + oh) * WO + ow0;
+        if (P.bias != nullptr)
+#pragma unroll
+            for (int c = 0; c < COB; ++c) {
+                const float b = __ldg(P.bias + co0 + c);
+#pragma unroll
+                for (int j = 0; j < RUN; ++j) acc[c][j] += b;
+            }
 #pragma unroll
         for (int c = 0; c < COB; ++c)
 #pragma unroll

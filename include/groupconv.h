@@ -122,6 +122,34 @@ typedef enum {
 int gc_b200_conv(const gc_shape *p, const gc_tensor *x, const gc_tensor *w,
                  gc_tensor *y, int kernel, void *stream);
 
+/* Layouts of x and y for gc_b200_conv_ex. */
+typedef enum {
+    GC_B200_NCHW = 0, /* dense NCHW, as gc_cuda_conv                                  */
+    GC_B200_NHWC = 1  /* channels last: element strides (H*W*C, 1, W*C, C) for the
+                         descriptor dims (N, C, H, W), PyTorch's channels_last format */
+} gc_b200_layout;
+
+/* Convolution with an optional bias and a choice of layout.  Same contract as
+ * gc_cuda_conv (validation, current device, caller's stream, no allocation,
+ * no synchronization); weights are always dense [Cout][Cin/groups][R][S].
+ *   bias    NULL for none, else a rank-1 dense FP32 CUDA tensor of Cout
+ *           elements on the same device; y = conv(x, w) + bias[c], the bias
+ *           added after the FP32 sum.  (The reference has no bias: its model
+ *           runner reports biased layers, e.g. ConvNeXt's 7x7 depthwise ones,
+ *           as unsupported - bench/model_run.py:46-49.)
+ *   layout  GC_B200_NCHW: without a bias the production choice of
+ *           gc_cuda_conv implementation 3 (or the general kernel outside B
+ *           geometry); with a bias the depthwise engines or the general
+ *           kernel, any geometry.
+ *           GC_B200_NHWC: x and y channels-last (the reference times this
+ *           layout only through cuDNN, bench/cuda_boundaries.py:17, and its
+ *           ABI rejects it, csrc/common/common.cpp:48): a vectorized kernel
+ *           for 3x3/s1/p1 with C % 4 == 0 and 16-byte aligned x and y, a
+ *           scalar kernel for every other geometry.  Strides that are neither
+ *           -> GC_UNSUPPORTED. */
+int gc_b200_conv_ex(const gc_shape *p, const gc_tensor *x, const gc_tensor *w,
+                    const gc_tensor *bias, gc_tensor *y, int layout, void *stream);
+
 /* Launch plan chosen by the last successful gc_cuda_conv / gc_b200_conv call
  * on the calling thread: kernel family name, grid, block, shared memory and
  * work split, as one line of text.  Empty before the first launch. */
