@@ -31,9 +31,9 @@ FIELDS = ('n', 'cin', 'cout', 'h', 'w', 'r', 's', 'groups', 'sh', 'sw', 'ph', 'p
 # Status codes (include/groupconv.h, reference csrc/common/groupconv.h:10-11).
 GC_OK, GC_INVALID, GC_UNSUPPORTED, GC_DEVICE_ERROR, GC_UNAVAILABLE = range(5)
 # Kernel families of gc_b200_conv.
-AUTO, GENERAL, DIRECT_LDG, DIRECT_TMA, TF32X3, SMALL, KSTREAM = range(7)
+AUTO, GENERAL, DIRECT_LDG, DIRECT_TMA, TF32X3, SMALL = range(6)
 KERNELS = {'auto': AUTO, 'general': GENERAL, 'direct_ldg': DIRECT_LDG,
-           'direct_tma': DIRECT_TMA, 'tf32x3': TF32X3, 'small': SMALL, 'kstream': KSTREAM}
+           'direct_tma': DIRECT_TMA, 'tf32x3': TF32X3, 'small': SMALL}
 # Layouts of gc_b200_conv_ex.
 NCHW, NHWC = 0, 1
 LAYOUTS = {'nchw': NCHW, 'nhwc': NHWC}

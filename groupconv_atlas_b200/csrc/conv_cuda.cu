@@ -30,7 +30,6 @@
 #include "kernel_wide.cuh"
 #include "kernel_tf32x3.cuh"
 #include "kernel_small.cuh"
-#include "kernel_kstream.cuh"
 #include "kernel_nhwc.cuh"
 #include "kernel_probe.cuh"
 
@@ -45,7 +44,7 @@ constexpr int kStages = 3;
 // when gc_b200_last_plan asks for it (formatting costs about a third of a
 // microsecond, a tenth of the host time of a call).
 struct PlanRecord {
-    enum Kind { kNone, kDirect, kWide, kTf32, kSmall, kGeneral, kDw, kDwS2, kKstream, kNhwc } kind = kNone;
+    enum Kind { kNone, kDirect, kWide, kTf32, kSmall, kGeneral, kDw, kDwS2, kNhwc } kind = kNone;
     const char *name = "";  // variant name, static storage
     bool tma = false;
     long long v[14] = {};
@@ -96,12 +95,6 @@ std::string format_plan(const PlanRecord &r) {
                       "kernel=general engine=depthwise_cells k=%lld stride=%lld grid=%lld block=256 cells=%lld "
                       "vec_in=%lld vec_out=%lld",
                       v[0], v[5], v[1], v[2], v[3], v[4]);
-        break;
-    case PlanRecord::kKstream:
-        std::snprintf(buf, sizeof(buf),
-                      "kernel=kstream engine=group8 grid=%lld block=%lld smem=%lld gi=%lld items=%lld stages=%lld "
-                      "band=8 cell=8x2x7 vec_store=%lld",
-                      v[0], v[1], v[2], v[3], v[4], v[5], v[6]);
         break;
     case PlanRecord::kNhwc:
         std::snprintf(buf, sizeof(buf), "kernel=nhwc engine=%s grid=%lld block=256 cpg=%lld bias=%lld", r.name, v[0],
@@ -259,27 +252,6 @@ int encode_rows_map(CUtensorMap &map, const float *base, long long rows, long lo
     cuuint32_t box[2] = {static_cast<cuuint32_t>(bw), static_cast<cuuint32_t>(bh)};
     cuuint32_t estride[2] = {1, 1};
     CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box,
-                        estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return gc_error(GC_DEVICE_ERROR, "cuTensorMapEncodeTiled failed");
-    return GC_OK;
-}
-
-// 5-D map over an NCHW float tensor with the channels split into (channel in
-// group, group): dims (W, H, cpg, groups, N), box (bw, bh, 1, bg, 1).
-int encode_group_map(CUtensorMap &map, const float *base, long long n, long long groups, long long cpg,
-                     long long h, long long w, int bw, int bh, int bg) {
-    PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
-    int st = tensor_map_encoder(encode);
-    if (st != GC_OK) return st;
-    cuuint64_t dims[5] = {static_cast<cuuint64_t>(w), static_cast<cuuint64_t>(h), static_cast<cuuint64_t>(cpg),
-                          static_cast<cuuint64_t>(groups), static_cast<cuuint64_t>(n)};
-    cuuint64_t strides[4] = {static_cast<cuuint64_t>(w) * 4, static_cast<cuuint64_t>(h * w) * 4,
-                             static_cast<cuuint64_t>(cpg * h * w) * 4, static_cast<cuuint64_t>(groups * cpg * h * w) * 4};
-    cuuint32_t box[5] = {static_cast<cuuint32_t>(bw), static_cast<cuuint32_t>(bh), 1u, static_cast<cuuint32_t>(bg),
-                         1u};
-    cuuint32_t estride[5] = {1, 1, 1, 1, 1};
-    CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 5, const_cast<float *>(base), dims, strides, box,
                         estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return gc_error(GC_DEVICE_ERROR, "cuTensorMapEncodeTiled failed");
@@ -961,70 +933,6 @@ int launch_tf32(const gc_shape *p, const float *x, const float *w, float *y, int
     return GC_OK;
 }
 
-// ---- 8-channel groups with streamed input channels (kernel_kstream.cuh) ---------------------
-// Groups per item: the largest divisor of the group count up to 8 (one
-// compute warp per group).
-int ks_groups_per_item(long long groups) {
-    for (int gi = gcb::kKsMaxGroups; gi > 1; --gi)
-        if (groups % gi == 0) return gi;
-    return 1;
-}
-
-// B geometry, 8 channels per group, rows of 52 or 56 pixels (8 cells of 7
-// columns; width % 4 == 0 for the TMA strides), 16-byte aligned input and
-// weights, and item counts within 32-bit indices.
-bool kstream_eligible(const gc_shape *p, const void *x, const void *w) {
-    if (p->cin / p->groups != gcb::kKsCpg || p->w % 4 != 0 || (p->w + gcb::kKsCw - 1) / gcb::kKsCw != gcb::kKsQc)
-        return false;
-    if (!aligned16(x) || !aligned16(w) || p->h >= (1LL << 30) || p->n >= (1LL << 30) || p->cin >= (1LL << 30))
-        return false;
-    const long long items = (p->groups / ks_groups_per_item(p->groups)) * p->n * ceil_div(p->h, gcb::kKsBand);
-    return items < (1LL << 31);
-}
-
-int launch_kstream(const gc_shape *p, const float *x, const float *w, float *y, int dev, cudaStream_t stream) {
-    DeviceFacts facts;
-    int st = device_facts(dev, facts);
-    if (st != GC_OK) return st;
-    gcb::KsParams P{};
-    P.w = w;
-    P.y = y;
-    P.n = static_cast<int>(p->n);
-    P.c = static_cast<int>(p->cin);
-    P.h = static_cast<int>(p->h);
-    P.wd = static_cast<int>(p->w);
-    P.groups = static_cast<int>(p->groups);
-    P.gi = ks_groups_per_item(p->groups);
-    P.gblocks = P.groups / P.gi;
-    P.bands = static_cast<int>(ceil_div(p->h, gcb::kKsBand));
-    P.items = static_cast<int>(static_cast<long long>(P.gblocks) * P.n * P.bands);
-    P.box_bytes = static_cast<unsigned>(P.gi * gcb::kKsRows * gcb::kKsPitch * 4);
-    P.stage_bytes = static_cast<unsigned>(round_up(P.box_bytes, 128));
-    P.wraw_bytes = static_cast<unsigned>(P.gi * gcb::kKsWFloats * 4);
-    P.vec_store = aligned16(y) ? 1 : 0;  // width % 4 == 0: every row of a plane starts 16-byte aligned
-    const size_t fixed = gcb::ks_fixed_bytes(P.gi);
-    const long long room = static_cast<long long>(facts.smem_optin) - static_cast<long long>(fixed);
-    P.stages = static_cast<int>(std::min<long long>(gcb::kKsMaxStages, room / P.stage_bytes));
-    if (P.stages < 2) return gc_error(GC_UNSUPPORTED, "kstream kernel: ring does not fit in shared memory");
-    const size_t smem = static_cast<size_t>(P.stages) * P.stage_bytes + fixed;
-    const int threads = P.gi * 32 + 32;
-    const void *fn = reinterpret_cast<const void *>(&gcb::kstream_conv_kernel);
-    int ctas = 0;
-    st = kernel_occupancy(dev, fn, threads, smem, facts.smem_optin, ctas);
-    if (st != GC_OK) return st;
-    if (ctas < 1) return gc_error(GC_UNSUPPORTED, "kstream kernel: does not fit on an SM");
-    CUtensorMap map;
-    std::memset(&map, 0, sizeof(map));
-    st = encode_group_map(map, x, p->n, p->groups, gcb::kKsCpg, p->h, p->w, gcb::kKsPitch, gcb::kKsRows, P.gi);
-    if (st != GC_OK) return st;
-    const int grid = static_cast<int>(std::min<long long>(P.items, static_cast<long long>(facts.sms) * ctas));
-    void *args[] = {&P, &map};
-    cudaError_t e = launch_pdl(fn, dim3(grid), dim3(threads), args, smem, stream);
-    if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
-    record_plan(PlanRecord::kKstream, "", true, grid, threads, smem, P.gi, P.items, P.stages, P.vec_store);
-    return GC_OK;
-}
-
 // ---- small-image kernel ----------------------------------------------------------------------
 constexpr long long kSmallMaxPixels = 512;  // one thread per pixel: at most 512 threads
 
@@ -1450,9 +1358,6 @@ int run_kernel(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_ten
     case GC_B200_SMALL:
         st = launch_small(p, xp, wp, yp, dev, s);
         break;
-    case GC_B200_KSTREAM:
-        st = launch_kstream(p, xp, wp, yp, dev, s);
-        break;
     default:
         return gc_error(GC_UNSUPPORTED, "unknown B200 kernel family");
     }
@@ -1469,15 +1374,6 @@ int run_kernel(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_ten
 int auto_kernel(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, int dev) {
     const long long cpg = p->cin / p->groups;
     if (cpg >= 16 && tf32_eligible(p, x->data, w->data)) return GC_B200_TF32X3;
-    // 8-channel groups on 52/56-pixel rows: the channel-streaming kernel when
-    // its items (8 groups x 8 rows of one image each, one CTA per SM) give
-    // every SM at least four.
-    if (cpg == 8 && kstream_eligible(p, x->data, w->data)) {
-        DeviceFacts facts;
-        const long long items =
-            (p->groups / ks_groups_per_item(p->groups)) * p->n * ceil_div(p->h, gcb::kKsBand);
-        if (device_facts(dev, facts) == GC_OK && items >= 4LL * facts.sms) return GC_B200_KSTREAM;
-    }
     // Depthwise layers of little work - planes of at most 256 pixels, or at
     // most 256K outputs in all, but not the very smallest (under 32K outputs,
     // where the small-image kernel's launch is cheaper) - run on the
@@ -1539,7 +1435,7 @@ int gc_b200_conv(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_t
                  int kernel, void *stream) {
     int st = gc_validate_tensors(p, x, w, y, GC_CUDA, GC_F32);
     if (st != GC_OK) return st;
-    if (kernel < GC_B200_AUTO || kernel > GC_B200_KSTREAM)
+    if (kernel < GC_B200_AUTO || kernel > GC_B200_SMALL)
         return gc_error(GC_UNSUPPORTED, "unknown B200 kernel family");
     const bool b = b_geometry(p);
     if (kernel != GC_B200_GENERAL && kernel != GC_B200_AUTO && !b)
@@ -1553,10 +1449,6 @@ int gc_b200_conv(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_t
         return gc_error(GC_UNSUPPORTED,
                         "3xTF32 path needs a multiple of 8 channels per group, 16-byte aligned weights and "
                         "a 256-pixel strip plus halo within 1024 rows and shared memory");
-    if (kernel == GC_B200_KSTREAM && !kstream_eligible(p, x->data, w->data))
-        return gc_error(GC_UNSUPPORTED,
-                        "kstream kernel needs 8 channels per group, a width of 52 or 56 and 16-byte aligned "
-                        "input and weights");
     int dev = -1;
     st = device_and_stream_checks(x, w, y, stream, dev);
     if (st != GC_OK) return st;

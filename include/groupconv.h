@@ -111,9 +111,7 @@ typedef enum {
     GC_B200_DIRECT_TMA = 3, /* B geometry, smem band staged by TMA tensor loads */
     GC_B200_TF32X3 = 4,     /* B geometry, a multiple of 8 channels per group (dense
                                layers too): tcgen05 3xTF32 implicit GEMM */
-    GC_B200_SMALL = 5,      /* B geometry, small images (whole planes per CTA, any width) */
-    GC_B200_KSTREAM = 6     /* B geometry, 8 channels per group, width 52 or 56: input channels
-                               streamed through a TMA ring, a whole group per warp */
+    GC_B200_SMALL = 5       /* B geometry, small images (whole planes per CTA, any width) */
 } gc_b200_kernel;
 
 /* Same contract as gc_cuda_conv (validation, stream, no allocation, no sync),

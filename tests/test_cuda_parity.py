@@ -60,13 +60,7 @@ def tf32_eligible(s):
 TF32_WIDEST_CPG16 = max(w for w in range(1, 1024) if tf32_fits(16, w))
 
 
-def kstream_eligible(s):
-    """The channel-streaming kernel: 8 channels per group, rows of 52 or 56
-    pixels (8 cells of 7 columns; width % 4 == 0)."""
-    return s.b_geometry and s.cpg == 8 and s.w % 4 == 0 and -(-s.w // 7) == 8
-
-
-@pytest.mark.parametrize('kernel', ['general', 'direct_ldg', 'direct_tma', 'tf32x3', 'small', 'kstream'])
+@pytest.mark.parametrize('kernel', ['general', 'direct_ldg', 'direct_tma', 'tf32x3', 'small'])
 def test_golden_kernel_families(native, torch_cuda, golden_cases, kernel):
     """Each kernel family on every golden case it serves; the others must be
     refused with GC_UNSUPPORTED, never silently rerouted."""
@@ -79,8 +73,6 @@ def test_golden_kernel_families(native, torch_cuda, golden_cases, kernel):
             eligible = tf32_eligible(c.shape)
         if kernel == 'small':
             eligible = c.shape.b_geometry and c.shape.h * c.shape.w <= 512
-        if kernel == 'kstream':
-            eligible = kstream_eligible(c.shape)
         if not eligible:
             with pytest.raises(NativeError) as err:
                 run(native, torch_cuda, c.shape, c.x, c.w, kernel=kernel)
@@ -90,7 +82,7 @@ def test_golden_kernel_families(native, torch_cuda, golden_cases, kernel):
         assert plan.startswith(f'kernel={kernel}'), plan
         assert_matches(c.shape, c.x, c.w, y, c.y32, label=f'{c.name} {kernel}')
         ran += 1
-    assert ran > 0 or kernel == 'kstream'  # its shapes: test_kstream_kernel below
+    assert ran > 0
 
 
 SMALL_B = [
@@ -276,73 +268,3 @@ def test_depthwise_engine_leaves_other_kernel_sizes_to_the_general_kernel(native
     y, plan = run(native, torch_cuda, s, x, w, impl=0)
     assert plan.startswith('kernel=general grid='), plan
     assert_matches(s, x, w, y, label='9x9 depthwise')
-
-
-# The channel-streaming kernel for 8-channel groups: group blocks of 1-8
-# groups per CTA (divisors of the group count), partial last bands, one-row
-# images, widths 52 and 56.
-KSTREAM_SHAPES = [(1, 8, 56, 56), (2, 24, 9, 52), (3, 64, 57, 56), (1, 40, 1, 56), (2, 256, 56, 56),
-                  (1, 512, 16, 52), (5, 128, 8, 56), (1, 72, 100, 56), (4, 16, 23, 52), (33, 64, 12, 56)]
-
-
-@pytest.mark.parametrize('n,c,h,w', KSTREAM_SHAPES)
-def test_kstream_kernel(native, torch_cuda, n, c, h, w):
-    """Against the FP64 oracle, and bitwise against the TMA-staged direct
-    kernel (both sum every output over ci, then the 9 taps in order)."""
-    s = Shape(n=n, cin=c, cout=c, h=h, w=w, groups=c // 8)
-    x, wt = inputs(s, 9)
-    y, plan = run(native, torch_cuda, s, x, wt, kernel='kstream')
-    assert plan.startswith('kernel=kstream'), plan
-    assert_matches(s, x, wt, y, label=f'{s} {plan}')
-    y_tma, plan_tma = run(native, torch_cuda, s, x, wt, kernel='direct_tma')
-    assert np.array_equal(y, y_tma), f'{plan} vs {plan_tma}'
-    assert native.device_status(clear=True) == 0
-
-
-def test_kstream_unaligned_output_and_refusals(native, torch_cuda):
-    """An output that is not 16-byte aligned takes the scalar store path; an
-    input or weights that are not 16-byte aligned, or other widths and group
-    sizes, are refused by the family and served by another kernel under
-    implementation 3."""
-    torch = torch_cuda
-    s = Shape(n=2, cin=64, cout=64, h=17, w=56, groups=8)
-    x, wt = inputs(s, 4)
-    y64, bound = orc.conv_f64_bound(s, x, wt)
-    stream = torch.cuda.Stream()
-    with torch.cuda.stream(stream):
-        dx, dw = torch.from_numpy(x).cuda(), torch.from_numpy(wt).cuda()
-        buf = torch.full((int(np.prod(s.output)) + 1,), float('nan'), device='cuda')
-        dy = buf[1:].view(s.output)
-        native.b200(s, dx, dw, dy, 'kstream', stream.cuda_stream)
-        plan = native.last_plan()
-        stream.synchronize()
-    assert plan.startswith('kernel=kstream') and 'vec_store=0' in plan, plan
-    assert orc.bound_check(dy.cpu().numpy(), y64, bound)['passed']
-    with torch.cuda.stream(stream):
-        xbuf = torch.empty(int(np.prod(s.input)) + 1, device='cuda')
-        xbuf[1:].copy_(torch.from_numpy(x).reshape(-1))
-        dxu = xbuf[1:].view(s.input)
-        dy2 = torch.full(s.output, float('nan'), device='cuda')
-        with pytest.raises(NativeError) as err:
-            native.b200(s, dxu, dw, dy2, 'kstream', stream.cuda_stream)
-        assert err.value.status == GC_UNSUPPORTED
-        native.cuda(s, dxu, dw, dy2, 3, stream.cuda_stream)
-        plan = native.last_plan()
-        stream.synchronize()
-    assert not plan.startswith('kernel=kstream'), plan
-    assert orc.bound_check(dy2.cpu().numpy(), y64, bound)['passed']
-    for bad in (Shape(n=1, cin=64, cout=64, h=8, w=48, groups=8), Shape(n=1, cin=64, cout=64, h=8, w=56, groups=16),
-                Shape(n=1, cin=64, cout=64, h=8, w=54, groups=8)):
-        xb, wb = inputs(bad, 1)
-        with pytest.raises(NativeError) as err:
-            run(native, torch, bad, xb, wb, kernel='kstream')
-        assert err.value.status == GC_UNSUPPORTED
-
-
-def test_kstream_is_the_production_choice_for_large_batches(native, torch_cuda):
-    s = Shape(n=32, cin=256, cout=256, h=56, w=56, groups=32)
-    x, wt = inputs(s, 2)
-    y, plan = run(native, torch_cuda, s, x, wt, impl=3)
-    assert plan.startswith('kernel=kstream'), plan
-    p = orc.check_points(s, x, wt, y)
-    assert p['passed']
