@@ -91,6 +91,8 @@ SMALL_B = [
     (1, 48, 19, 28, 16), (1, 64, 14, 16, 32), (1, 128, 9, 12, 64), (2, 6, 33, 17, 3),
     (1, 10, 70, 72, 5), (1, 24, 112, 112, 1), (1, 16, 112, 112, 4), (1, 8, 7, 7, 8),
     (5, 4, 14, 14, 2), (1, 2, 200, 248, 1), (1, 4, 5, 252, 2),
+    # 16-channel groups on the warp-specialized direct kernel: tails, several groups per item
+    (2, 64, 30, 56, 16), (1, 32, 9, 12, 16), (3, 128, 17, 28, 16), (1, 16, 112, 112, 16),
 ]
 
 
