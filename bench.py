@@ -54,7 +54,7 @@ UNIT = 'GB/s'
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_PEAKS = {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0}
 WORKLOADS = ['config1', 'config2', 'config4_leaf', 'config5_g32', 'config5_g4', 'config4_block', 'config3', 'atlas',
-             'model_layers']
+             'model_layers', 'kernels']
 DEFAULT_BLOCKS = 'config5_g4,config2'
 
 
@@ -82,6 +82,10 @@ def parse_args(argv=None):
     ap.add_argument('--cpu-seconds', type=float, default=10.0, help='CPU baseline sample budget')
     ap.add_argument('--atlas-batches', type=int, default=10, help='atlas: paired batches per shape')
     ap.add_argument('--atlas-samples', type=int, default=30, help='atlas: samples per batch and implementation')
+    ap.add_argument('--shapes', default='16,512,112,112,16;32,256,56,56,16;32,256,56,56,32',
+                    help='kernels workload: N,C,H,W,CPG shapes separated by ";"')
+    ap.add_argument('--families', default='tf32x3,direct_tma',
+                    help='kernels workload: gc_b200_conv kernel families to compare')
     ap.add_argument('--cudnn-leg', default=None, help=argparse.SUPPRESS)  # internal: the fresh cuDNN process
     args = ap.parse_args(argv)
     if args.warmup < 3:
@@ -1070,6 +1074,62 @@ def run_model_layers(args):
                           'shape id')
 
 
+def run_kernels(args):
+    """Per shape and kernel family (gc_b200_conv), the device time of K
+    back-to-back calls between CUDA events on the launching stream, after W
+    warm-up calls; uniform inputs generated on the device.  The evidence for
+    the production choice between kernel families."""
+    import torch
+    from groupconv_atlas_b200 import api
+    from groupconv_atlas_b200.api import Shape
+    rank, world, local = dist_setup()
+    if rank != 0:
+        return 0
+    torch.cuda.set_device(local)
+    native = api.Native()
+    pk = peaks()
+    stream = torch.cuda.Stream()
+    rows = []
+    for spec in args.shapes.split(';'):
+        n, c, h, w, cpg = (int(v) for v in spec.split(','))
+        s = Shape(n=n, cin=c, cout=c, h=h, w=w, groups=c // cpg)
+        flops = 2 * n * c * h * w * cpg * 9
+        nbytes = 4 * (2 * n * c * h * w + c * cpg * 9)
+        with torch.cuda.stream(stream):
+            x = torch.rand(s.input, device='cuda') * 2 - 1
+            wt = (torch.rand(s.weight, device='cuda') * 2 - 1) / math.sqrt(9 * cpg)
+            y = torch.empty(s.output, device='cuda')
+            row = {'shape': [n, c, h, w, cpg]}
+            for fam in args.families.split(','):
+                try:
+                    native.b200(s, x, wt, y, fam, stream.cuda_stream)
+                except api.NativeError as e:
+                    row[fam] = {'status': e.status, 'error': str(e)}
+                    continue
+                plan = native.last_plan()
+                for _ in range(args.warmup):
+                    native.b200(s, x, wt, y, fam, stream.cuda_stream)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                for _ in range(args.steps):
+                    native.b200(s, x, wt, y, fam, stream.cuda_stream)
+                b.record(stream)
+                stream.synchronize()
+                ms = a.elapsed_time(b) / args.steps
+                row[fam] = {'us': ms * 1e3, 'tflops': flops / (ms / 1e3) / 1e12, 'gbs': nbytes / (ms / 1e3) / 1e9,
+                            'plan': plan}
+            times = {f: v['us'] for f, v in row.items() if isinstance(v, dict) and 'us' in v}
+            row['fastest'] = min(times, key=times.get) if times else None
+            rows.append(row)
+        del x, y
+        torch.cuda.empty_cache()
+    print(json.dumps({'metric': 'device time per call of gc_b200_conv kernel families', 'unit': 'us',
+                      'n_gpus': 1, 'steps': args.steps, 'warmup': args.warmup, 'dtype': 'f32',
+                      'data': 'synthetic uniform inputs on the device', 'peaks': pk,
+                      'config': {'workload': 'kernels', 'families': args.families}, 'rows': rows}), flush=True)
+    return 0
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.cudnn_leg:
@@ -1084,6 +1144,8 @@ def main(argv=None):
         return run_atlas(args)
     if args.workload == 'model_layers':
         return run_model_layers(args)
+    if args.workload == 'kernels':
+        return run_kernels(args)
     return run_ours(args)
 
 
