@@ -760,15 +760,22 @@ GRAPH_STEPS, GRAPH_REPLAYS = 50, 3  # the block's graph timing: calls captured, 
 
 def run_block(args):
     """Config 4: torchvision MobileNetV2 features[3] (random Kaiming-normal
-    init, seed 2, eval), N4 input N(0,1); the reference block runs every conv
-    on cuDNN, the candidate replaces only the depthwise 3x3 by gc_cuda_conv
-    (implementation 3), as the reference's bench/module_run.py:215-235 does.
-    Reports block latency from CUDA-graph replay (device) and synchronized
-    per-call wall time (API), both blocks, same inputs."""
+    init, seed 2, eval; batch-norm running statistics drawn from a seeded
+    distribution so that they are not the identity), N4 input N(0,1).  Three
+    blocks on the same input: the reference block (every layer on
+    PyTorch/cuDNN); the candidate with only the depthwise 3x3 replaced by
+    gc_cuda_conv (implementation 3), as the reference's
+    bench/module_run.py:215-235 does; and the fused candidate, whose
+    depthwise conv + batch norm + ReLU6 run as one gc_b200_conv_ex call (the
+    normalisation folded into the weights and a bias, ReLU6 in the epilogue).
+    Reported per block: latency from CUDA-graph replay (device) and the
+    synchronized per-call wall time (API); the API speed-up of each candidate
+    over the reference block with the reference's paired batch-median
+    bootstrap (bench/stats.py) over alternating rounds."""
     import copy
     import torch
     import torchvision
-    from groupconv_atlas_b200 import api, torch_module
+    from groupconv_atlas_b200 import api, stats, torch_module
     from oracle import oracle as orc
     rank, world, local = dist_setup()
     if rank != 0:
@@ -777,67 +784,88 @@ def run_block(args):
     set_fp32_precision(torch)
     torch.backends.cudnn.benchmark = True
     torch.manual_seed(2)
-    block = torchvision.models.mobilenet_v2(weights=None).features[3].eval().cuda()
+    block = torchvision.models.mobilenet_v2(weights=None).features[3].eval()
+    g = torch.Generator().manual_seed(2)
+    for m in block.modules():
+        if isinstance(m, torch.nn.BatchNorm2d):
+            m.running_mean.copy_(torch.randn(m.num_features, generator=g) * 0.1)
+            m.running_var.copy_(torch.rand(m.num_features, generator=g) * 0.5 + 0.75)
+            m.weight.data.copy_(torch.rand(m.num_features, generator=g) * 0.5 + 0.75)
+            m.bias.data.copy_(torch.randn(m.num_features, generator=g) * 0.1)
+    block = block.cuda()
     cand = copy.deepcopy(block)
+    fused = copy.deepcopy(block)
     native = api.Native()
     replaced = torch_module.substitute(cand, torch_module.is_depthwise_3x3, native)
+    fused_names = torch_module.fuse_conv_bn_act(fused, torch_module.is_depthwise, native)
     x = torch.randn((4, 24, 56, 56), generator=torch.Generator().manual_seed(2)).cuda()
     stream = torch.cuda.Stream()
+    mods = (('ours', cand), ('fused', fused), ('cudnn', block))
     with torch.inference_mode(), torch.cuda.stream(stream):
         ref = block(x)
-        out = cand(x)
-        stream.synchronize()
-        check = orc.error_metrics(out.cpu().numpy(), ref.cpu().numpy())
-        if not check['passed']:
-            raise SystemExit(f'substituted block does not match the cuDNN block: {check}')
-        plan = native.last_plan()
+        checks, plans = {}, {}
+        for name, mod in mods[:2]:
+            out = mod(x)
+            plans[name] = native.last_plan()
+            stream.synchronize()
+            checks[name] = orc.error_metrics(out.cpu().numpy(), ref.cpu().numpy())
+            if not checks[name]['passed']:
+                raise SystemExit(f'{name} block does not match the cuDNN block: {checks[name]}')
         results = {}
-        mods = (('ours', cand), ('cudnn', block))
         for name, mod in mods:
             for _ in range(20):
                 mod(x)
             results[name + '_graph_us'] = graph_step_ms(torch, stream, lambda k, m=mod: m(x), GRAPH_STEPS,
                                                         GRAPH_REPLAYS) * 1e3
-        # Synchronized API time: rounds alternate between the two blocks (host
-        # timing drifts over seconds); per block the median over rounds.
-        rounds, per_round = 10, max(1, args.steps // 10)
+        # Synchronized API time: rounds alternate the order of the blocks
+        # (host timing drifts over seconds); per round the median call.
+        rounds, per_round = 10, max(3, args.steps // 10)
         api_rounds = {name: [] for name, _ in mods}
         for r in range(rounds):
-            for name, mod in (mods if r % 2 == 0 else mods[::-1]):
-                stream.synchronize()
-                t0 = time.perf_counter()
+            order = list(mods) if r % 2 == 0 else list(mods)[::-1]
+            for name, mod in order:
+                samples = []
                 for _ in range(per_round):
+                    stream.synchronize()
+                    t0 = time.perf_counter()
                     mod(x)
                     stream.synchronize()
-                api_rounds[name].append((time.perf_counter() - t0) / per_round * 1e6)
+                    samples.append((time.perf_counter() - t0) * 1e6)
+                api_rounds[name].append(statistics.median(samples))
         for name, _ in mods:
             results[name + '_api_us'] = statistics.median(api_rounds[name])
             results[name + '_api_rounds_us'] = api_rounds[name]
-        # end to end: pinned host input -> block -> pinned host output
+        api_cmp = {name: stats.compare_batches(api_rounds['cudnn'], api_rounds[name]) for name in ('ours', 'fused')}
+        # end to end: pinned host input -> fused block -> pinned host output
         xh = x.cpu().pin_memory()
-        yh = torch.empty(tuple(out.shape), pin_memory=True)
+        yh = torch.empty(tuple(ref.shape), pin_memory=True)
         xd = torch.empty_like(x)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
         for _ in range(args.e2e_steps):
             xd.copy_(xh, non_blocking=True)
-            yh.copy_(cand(xd), non_blocking=True)
+            yh.copy_(fused(xd), non_blocking=True)
         b.record(stream)
         stream.synchronize()
         e2e_us = a.elapsed_time(b) / args.e2e_steps * 1e3
-    line = {'metric': 'MobileNetV2 features[3] block latency, depthwise 3x3 on gc_cuda_conv (config 4)',
-            'value': results['ours_graph_us'], 'unit': 'us', 'n_gpus': 1, 'steps': args.steps,
-            'warmup': 20, 'ms_per_step': results['ours_graph_us'] / 1e3, 'higher_is_better': False,
-            'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32', 'data': 'synthetic N(0,1) input, seed 2',
-            'config': {'workload': 'config4_block', 'replaced': replaced, 'kernel_plan': plan,
-                       'input': [4, 24, 56, 56]},
-            'block': results, 'speedup_graph': results['cudnn_graph_us'] / results['ours_graph_us'],
-            'speedup_api': results['cudnn_api_us'] / results['ours_api_us'], 'check': check,
+    line = {'metric': 'MobileNetV2 features[3] block latency with the depthwise conv on this library (config 4)',
+            'value': results['fused_graph_us'], 'unit': 'us', 'n_gpus': 1, 'steps': args.steps,
+            'warmup': 20, 'ms_per_step': results['fused_graph_us'] / 1e3, 'higher_is_better': False,
+            'scaling': 'weak', 'vs_baseline': None, 'dtype': 'f32',
+            'data': 'synthetic N(0,1) input, seed 2; Kaiming-normal weights, seeded batch-norm statistics',
+            'config': {'workload': 'config4_block', 'replaced': replaced, 'fused': fused_names,
+                       'kernel_plans': plans, 'input': [4, 24, 56, 56]},
+            'block': results,
+            'speedup_graph': {n: results['cudnn_graph_us'] / results[n + '_graph_us'] for n in ('ours', 'fused')},
+            'speedup_api': {n: api_cmp[n]['speedup'] for n in ('ours', 'fused')},
+            'api_classification': {n: api_cmp[n]['classification'] for n in ('ours', 'fused')},
+            'api_ci95': {n: api_cmp[n]['ci95'] for n in ('ours', 'fused')},
+            'check': checks,
             'e2e': {'value': e2e_us, 'unit': 'us', 'h2d_bytes_per_step': x.numel() * 4,
-                    'd2h_bytes_per_step': out.numel() * 4},
+                    'd2h_bytes_per_step': ref.numel() * 4, 'block': 'fused'},
             # the timed region of `value`: GRAPH_REPLAYS replays of GRAPH_STEPS
-            # block calls, one gc_cuda_conv launch each
-            'gpu_launches': GRAPH_STEPS * GRAPH_REPLAYS * len(replaced)}
+            # fused-block calls, one gc_b200_conv_ex launch each
+            'gpu_launches': GRAPH_STEPS * GRAPH_REPLAYS * len(fused_names)}
     print(json.dumps(line), flush=True)
     return 0
 

@@ -37,6 +37,9 @@ KERNELS = {'auto': AUTO, 'general': GENERAL, 'direct_ldg': DIRECT_LDG,
 # Layouts of gc_b200_conv_ex.
 NCHW, NHWC = 0, 1
 LAYOUTS = {'nchw': NCHW, 'nhwc': NHWC}
+# Activations of gc_b200_conv_ex.
+ACT_NONE, ACT_RELU, ACT_RELU6 = 0, 1, 2
+ACTIVATIONS = {'none': ACT_NONE, 'relu': ACT_RELU, 'relu6': ACT_RELU6}
 STATUS_TMA_TIMEOUT = 0x1
 STATUS_MMA_TIMEOUT = 0x2
 
@@ -187,7 +190,8 @@ class Native:
         lib.gc_b200_last_plan.restype = ct.c_char_p
         lib.gc_b200_device_status.argtypes = [ct.POINTER(ct.c_uint32), ct.c_int]
         lib.gc_b200_selftest_wait_timeout.argtypes = [ct.c_uint32, ct.c_void_p]
-        lib.gc_b200_conv_ex.argtypes = [ct.POINTER(CShape)] + [ct.POINTER(Tensor)] * 4 + [ct.c_int, ct.c_void_p]
+        lib.gc_b200_conv_ex.argtypes = [ct.POINTER(CShape)] + [ct.POINTER(Tensor)] * 4 + [ct.c_int, ct.c_int,
+                                                                                              ct.c_void_p]
         lib.gc_b200_probe_ffma.argtypes = [ct.c_void_p, ct.c_int, ct.c_int, ct.c_void_p]
         lib.gc_b200_probe_ffma_flops.argtypes = [ct.c_int, ct.c_int]
         lib.gc_b200_probe_ffma_flops.restype = ct.c_longlong
@@ -230,15 +234,17 @@ class Native:
                                          native_int(kernel), stream))
         return y
 
-    def conv_ex(self, shape, x, w, y, bias=None, layout='nchw', stream=0):
-        """gc_b200_conv_ex: optional bias (rank-1, Cout) and layout 'nchw' or
-        'nhwc' (x and y channels-last, e.g. torch.channels_last tensors)."""
+    def conv_ex(self, shape, x, w, y, bias=None, layout='nchw', activation='none', stream=0):
+        """gc_b200_conv_ex: optional bias (rank-1, Cout), activation ('none',
+        'relu', 'relu6') and layout 'nchw' or 'nhwc' (x and y channels-last,
+        e.g. torch.channels_last tensors)."""
         lay = LAYOUTS.get(layout, layout) if isinstance(layout, str) else layout
+        act = ACTIVATIONS.get(activation, activation) if isinstance(activation, str) else activation
         p, xd, wd, yd = cshape(shape), tensor(x), tensor(w), tensor(y)
         bd = tensor(bias) if bias is not None else None
         self.check(self.lib.gc_b200_conv_ex(ct.byref(p), ct.byref(xd), ct.byref(wd),
                                             ct.byref(bd) if bd is not None else None, ct.byref(yd),
-                                            native_int(lay), self._stream(stream)))
+                                            native_int(lay), native_int(act), self._stream(stream)))
         return y
 
     def last_plan(self):

@@ -700,10 +700,12 @@ int plan_engine(const gc_shape *p, const float *w, const float *y, bool tma, int
 }
 
 int launch_direct(const gc_shape *p, const float *x, const float *w, float *y, bool tma, int dev,
-                  cudaStream_t stream) {
+                  cudaStream_t stream, const float *bias = nullptr, int act = gcb::kActNone) {
     EnginePlan plan;
     int st = plan_engine(p, w, y, tma, dev, plan);
     if (st != GC_OK) return st;
+    if (plan.wide && (bias != nullptr || act != gcb::kActNone))
+        return gc_error(GC_UNSUPPORTED, "channel-chunked kernel: no bias or activation epilogue");
     CUtensorMap map;
     std::memset(&map, 0, sizeof(map));
     void *args[2];
@@ -711,6 +713,8 @@ int launch_direct(const gc_shape *p, const float *x, const float *w, float *y, b
         plan.D.x = x;
         plan.D.w = w;
         plan.D.y = y;
+        plan.D.bias = bias;
+        plan.D.act = act;
         if (tma) {
             st = encode_nchw_map(map, x, p->n, p->cin, p->h, p->w, plan.D.pitch, plan.D.rows, plan.D.cb);
             if (st != GC_OK) return st;
@@ -1044,7 +1048,7 @@ bool dw_eligible(const gc_shape *p, int64_t ho, int64_t wo) {
 }
 
 int launch_dw(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const float *w, float *y, int dev,
-              cudaStream_t stream, const float *bias = nullptr) {
+              cudaStream_t stream, const float *bias = nullptr, int act = gcb::kActNone) {
     DeviceFacts facts;
     int st = device_facts(dev, facts);
     if (st != GC_OK) return st;
@@ -1061,6 +1065,7 @@ int launch_dw(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const f
     P.w = w;
     P.y = y;
     P.bias = bias;
+    P.act = act;
     P.n = static_cast<int>(p->n);
     P.c = static_cast<int>(p->cin);
     P.h = static_cast<int>(p->h);
@@ -1108,7 +1113,7 @@ bool dw_s2_eligible(const gc_shape *p) {
 }
 
 int launch_dw_s2(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const float *w, float *y, int dev,
-                 cudaStream_t stream, const float *bias = nullptr) {
+                 cudaStream_t stream, const float *bias = nullptr, int act = gcb::kActNone) {
     DeviceFacts facts;
     int st = device_facts(dev, facts);
     if (st != GC_OK) return st;
@@ -1117,6 +1122,7 @@ int launch_dw_s2(const gc_shape *p, int64_t ho, int64_t wo, const float *x, cons
     P.w = w;
     P.y = y;
     P.bias = bias;
+    P.act = act;
     P.n = static_cast<int>(p->n);
     P.c = static_cast<int>(p->cin);
     P.h = static_cast<int>(p->h);
@@ -1154,9 +1160,9 @@ const void *general_kernel_for(bool narrow) {
 }
 
 int launch_general(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const float *w,
-                   float *y, int dev, cudaStream_t stream, const float *bias = nullptr) {
-    if (dw_s2_eligible(p)) return launch_dw_s2(p, ho, wo, x, w, y, dev, stream, bias);
-    if (dw_eligible(p, ho, wo)) return launch_dw(p, ho, wo, x, w, y, dev, stream, bias);
+                   float *y, int dev, cudaStream_t stream, const float *bias = nullptr, int act = gcb::kActNone) {
+    if (dw_s2_eligible(p)) return launch_dw_s2(p, ho, wo, x, w, y, dev, stream, bias, act);
+    if (dw_eligible(p, ho, wo)) return launch_dw(p, ho, wo, x, w, y, dev, stream, bias, act);
     DeviceFacts facts;
     int st = device_facts(dev, facts);
     if (st != GC_OK) return st;
@@ -1165,6 +1171,7 @@ int launch_general(const gc_shape *p, int64_t ho, int64_t wo, const float *x, co
     P.wp = w;
     P.yp = y;
     P.bias = bias;
+    P.act = act;
     P.n = p->n;
     P.cin = p->cin;
     P.cout = p->cout;
@@ -1216,7 +1223,7 @@ bool channels_last_strides(const gc_tensor *t) {
 }
 
 int launch_nhwc(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const float *w, const float *bias,
-                float *y, int dev, cudaStream_t stream) {
+                int act, float *y, int dev, cudaStream_t stream) {
     DeviceFacts facts;
     int st = device_facts(dev, facts);
     if (st != GC_OK) return st;
@@ -1232,6 +1239,7 @@ int launch_nhwc(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const
         P.w = w;
         P.bias = bias;
         P.y = y;
+        P.act = act;
         P.n = static_cast<int>(std::min<long long>(p->n, 1LL << 30));
         P.c = static_cast<int>(p->cin);
         P.h = static_cast<int>(p->h);
@@ -1255,6 +1263,7 @@ int launch_nhwc(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const
     P.wt = w;
     P.bias = bias;
     P.y = y;
+    P.act = act;
     P.n = p->n;
     P.cin = p->cin;
     P.cout = p->cout;
@@ -1467,10 +1476,12 @@ int gc_b200_conv(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_t
 }
 
 int gc_b200_conv_ex(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, const gc_tensor *bias,
-                    gc_tensor *y, int layout, void *stream) {
+                    gc_tensor *y, int layout, int activation, void *stream) {
     if (p == nullptr || x == nullptr || w == nullptr || y == nullptr)
         return gc_error(GC_INVALID, "null shape or tensor descriptor");
     if (layout != GC_B200_NCHW && layout != GC_B200_NHWC) return gc_error(GC_UNSUPPORTED, "unknown layout");
+    if (activation != GC_B200_ACT_NONE && activation != GC_B200_ACT_RELU && activation != GC_B200_ACT_RELU6)
+        return gc_error(GC_UNSUPPORTED, "unknown activation");
     int st = GC_OK;
     if (layout == GC_B200_NCHW) {
         st = gc_validate_tensors(p, x, w, y, GC_CUDA, GC_F32);
@@ -1495,8 +1506,9 @@ int gc_b200_conv_ex(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, c
     if (st != GC_OK) return st;
     if (bias != nullptr && (st = check_pointer(bias, dev)) != GC_OK) return st;
     const bool b = b_geometry(p);
-    if (layout == GC_B200_NCHW && bias == nullptr)
-        return run_kernel(p, x, w, y, b ? auto_kernel(p, x, w, dev) : GC_B200_GENERAL, dev, stream, true);
+    const int kernel = b ? auto_kernel(p, x, w, dev) : GC_B200_GENERAL;
+    if (layout == GC_B200_NCHW && bias == nullptr && activation == GC_B200_ACT_NONE)
+        return run_kernel(p, x, w, y, kernel, dev, stream, true);
     int64_t ho = 0, wo = 0;
     st = gc_validate_shape(p, &ho, &wo);
     if (st != GC_OK) return st;
@@ -1504,8 +1516,16 @@ int gc_b200_conv_ex(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, c
     const float *bp = bias != nullptr ? static_cast<const float *>(bias->data) : nullptr;
     float *yp = static_cast<float *>(y->data);
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    st = layout == GC_B200_NCHW ? launch_general(p, ho, wo, xp, wp, yp, dev, s, bp)
-                                : launch_nhwc(p, ho, wo, xp, wp, bp, yp, dev, s);
+    if (layout == GC_B200_NHWC) {
+        st = launch_nhwc(p, ho, wo, xp, wp, bp, activation, yp, dev, s);
+    } else {
+        // The production kernel when it has the epilogue (the direct
+        // engines), else the depthwise engines or the general kernel.
+        st = GC_UNSUPPORTED;
+        if (kernel == GC_B200_DIRECT_TMA || kernel == GC_B200_DIRECT_LDG)
+            st = launch_direct(p, xp, wp, yp, kernel == GC_B200_DIRECT_TMA, dev, s, bp, activation);
+        if (st == GC_UNSUPPORTED) st = launch_general(p, ho, wo, xp, wp, yp, dev, s, bp, activation);
+    }
     if (st != GC_OK) return st;
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? gc_error(GC_OK, "") : gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));

@@ -172,6 +172,21 @@ __device__ __forceinline__ float lds_over(const float *p, bool pred, float v) {
     return v;
 }
 
+// ---- output epilogue -------------------------------------------------------------
+// Activations gc_b200_conv_ex can apply after the (optional) bias: the values
+// of GC_B200_ACT_* in groupconv.h.
+constexpr int kActNone = 0, kActRelu = 1, kActRelu6 = 2;
+
+// y = act(v + b): the bias only when there is one and the activation only
+// when one is asked for, so that without either the stored value is the sum
+// itself (bit for bit, signed zeros included).
+__device__ __forceinline__ float epilogue(float v, bool has_bias, float b, int act) {
+    if (has_bias) v += b;
+    if (act == kActRelu) v = fmaxf(v, 0.0f);
+    if (act == kActRelu6) v = fminf(fmaxf(v, 0.0f), 6.0f);
+    return v;
+}
+
 // ---- stores -----------------------------------------------------------------------
 // Streaming 16-byte store: the output is not re-read by this kernel, so it is
 // marked evict-first to keep the input halo rows resident in L2.

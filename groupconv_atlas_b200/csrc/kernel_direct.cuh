@@ -69,7 +69,19 @@ struct DirectParams {
     int bulk_w;          // TMA staging: weights by bulk copy (else plain loads)
     unsigned x_bytes;    // bytes one TMA box delivers
     unsigned w_bytes;    // raw weight bytes per item
+    const float *bias;   // nullable: per-output-channel bias added after the sum
+    int act;             // kActNone / kActRelu / kActRelu6, applied after the bias
 };
+
+// The epilogue of a row segment of CW outputs of one channel, in place.
+template <int CW>
+__device__ __forceinline__ void finish_row(float (&a)[CW], const DirectParams &P, int channel) {
+    if (P.bias == nullptr && P.act == kActNone) return;
+    const bool hb = P.bias != nullptr;
+    const float b = hb ? __ldg(P.bias + channel) : 0.0f;
+#pragma unroll
+    for (int u = 0; u < CW; ++u) a[u] = epilogue(a[u], hb, b, P.act);
+}
 
 __device__ __forceinline__ void decode_item(const DirectParams &P, int item, int &n, int &c0,
                                             int &h0) {
@@ -310,7 +322,10 @@ __device__ __forceinline__ void compute_item(const DirectParams &P, const Cell &
                     acc[v % 3][u] = a;
                 }
             }
-            if (rr >= 2 && rr - 2 < rows_valid) store_row<CW>(ybase + (rr - 2) * P.wd, acc[(rr - 2) % 3], c, P.wd);
+            if (rr >= 2 && rr - 2 < rows_valid) {
+                finish_row<CW>(acc[(rr - 2) % 3], P, c0 + c.co_item);
+                store_row<CW>(ybase + (rr - 2) * P.wd, acc[(rr - 2) % 3], c, P.wd);
+            }
         }
     } else {
         const int chan_floats = P.rows * P.pitch;
@@ -365,7 +380,10 @@ __device__ __forceinline__ void compute_item(const DirectParams &P, const Cell &
         for (int j = 0; j < COB; ++j)
 #pragma unroll
             for (int v = 0; v < VR; ++v)
-                if (v < rows_valid) store_row<CW>(ybase + j * plane_floats + v * P.wd, acc[j][v], c, P.wd);
+                if (v < rows_valid) {
+                    finish_row<CW>(acc[j][v], P, c0 + c.co_item + j);
+                    store_row<CW>(ybase + j * plane_floats + v * P.wd, acc[j][v], c, P.wd);
+                }
     }
 }
 

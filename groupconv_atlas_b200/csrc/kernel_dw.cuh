@@ -14,7 +14,8 @@
 // (coalesced stores).  Two stages alternate: the copies of a CTA's next item
 // are in flight while it computes the current one.  The per-output sum runs
 // over (r, s) in row-major order with fused multiply-adds from zero, as the
-// reference's k0 does; an optional per-channel bias is added after the sum.
+// reference's k0 does; an optional per-channel bias and activation are
+// applied after the sum.
 #pragma once
 #include <cstdint>
 
@@ -27,6 +28,7 @@ struct DwParams {
     const float *w;
     float *y;
     const float *bias;           // nullable: per-channel bias added after the sum
+    int act;                     // kActNone / kActRelu / kActRelu6, applied after the bias
     int n, c, h, wd;             // input
     int sh, sw, ph, pw, dh, dw;  // geometry (kernel size is the template K)
     int ho, wo;                  // output
@@ -108,9 +110,9 @@ __global__ void __launch_bounds__(256) dw_conv_kernel(const __grid_constant__ Dw
                         for (int s = 0; s < K; ++s) acc[j] = fmaf(v[j + s], wr[r * K + s], acc[j]);
                 }
                 float *yr = yp + static_cast<long long>(orow) * P.wo + ow0;
-                if (has_bias)
+                if (has_bias || P.act != kActNone)
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) acc[j] += bv;
+                    for (int j = 0; j < 4; ++j) acc[j] = epilogue(acc[j], has_bias, bv, P.act);
 #pragma unroll
                 for (int j = 0; j < 4; ++j)
                     if (ow0 + j < P.wo) yr[j] = acc[j];
@@ -125,7 +127,7 @@ __global__ void __launch_bounds__(256) dw_conv_kernel(const __grid_constant__ Dw
                 for (int r = 0; r < K; ++r)
 #pragma unroll
                     for (int s = 0; s < K; ++s) acc = fmaf(t0[r * P.dh * P.pitch + s * P.dw], wr[r * K + s], acc);
-                yp[o] = has_bias ? acc + bv : acc;
+                yp[o] = epilogue(acc, has_bias, bv, P.act);
             }
         }
         __syncthreads();  // every thread is done with this stage before it is refilled
@@ -151,6 +153,7 @@ struct DwS2Params {
     const float *w;
     float *y;
     const float *bias;  // nullable: per-channel bias added after the sum
+    int act;            // kActNone / kActRelu / kActRelu6, applied after the bias
     int n, c, h, wd, ho, wo;
     int qcols;        // ceil(wo / 4)
     int prows;        // ceil(ho / 2)
@@ -227,10 +230,11 @@ __global__ void __launch_bounds__(256) dw_s2_conv_kernel(const __grid_constant__
                     for (int s = 0; s < K; ++s) acc = fmaf(v[S * rr + r][S * q + s], wr[r * K + s], acc);
                 o[q] = acc;
             }
-            if (P.bias != nullptr) {
-                const float bv = __ldg(P.bias + c);
+            if (P.bias != nullptr || P.act != kActNone) {
+                const bool hb = P.bias != nullptr;
+                const float bv = hb ? __ldg(P.bias + c) : 0.0f;
 #pragma unroll
-                for (int q = 0; q < 4; ++q) o[q] += bv;
+                for (int q = 0; q < 4; ++q) o[q] = epilogue(o[q], hb, bv, P.act);
             }
             float *yr = yp + static_cast<long long>(oh) * P.wo + ow0;
             if (P.vec_out && ow0 + 3 < P.wo) {

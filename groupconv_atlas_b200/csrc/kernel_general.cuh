@@ -10,7 +10,7 @@
 // coalesced (at the layer's stride) and the threads of a warp share weights
 // (L1 broadcast).  Grid-stride over runs; index arithmetic in 32 bits when
 // every tensor has fewer than 2^31 elements, else 64 bits.  An optional
-// per-output-channel bias is added after the sum.
+// per-output-channel bias and activation are applied after the sum.
 #pragma once
 #include <cstdint>
 
@@ -23,6 +23,7 @@ struct GeneralParams {
     const float *wp;
     float *yp;
     const float *bias;  // nullable: per-output-channel bias added after the sum
+    int act;            // kActNone / kActRelu / kActRelu6, applied after the bias
     long long n, cin, cout, h, w, r, s, groups, sh, sw, ph, pw, dh, dw;
     long long ho, wo;
     long long runs_per_row;  // ceil(wo / RUN)
@@ -83,12 +84,13 @@ __global__ void __launch_bounds__(256) general_conv_kernel(const __grid_constant
             }
         }
         float *out = P.yp + ((n * static_cast<I>(P.cout) + co0) * HO + oh) * WO + ow0;
-        if (P.bias != nullptr)
+        if (P.bias != nullptr || P.act != kActNone)
 #pragma unroll
             for (int c = 0; c < COB; ++c) {
-                const float b = __ldg(P.bias + co0 + c);
+                const bool hb = P.bias != nullptr;
+                const float b = hb ? __ldg(P.bias + co0 + c) : 0.0f;
 #pragma unroll
-                for (int j = 0; j < RUN; ++j) acc[c][j] += b;
+                for (int j = 0; j < RUN; ++j) acc[c][j] = epilogue(acc[c][j], hb, b, P.act);
             }
 #pragma unroll
         for (int c = 0; c < COB; ++c)

@@ -22,7 +22,7 @@
 //                           per thread, consecutive threads on consecutive
 //                           channels of a pixel.
 // Every output sums in FP32 from zero; the bias is added last, as a
-// framework's convolution with bias does.
+// framework's convolution with bias does, then the optional activation.
 #pragma once
 #include "device_util.cuh"
 
@@ -35,6 +35,7 @@ struct NhwcParams {
     const float *w;
     const float *bias;  // nullable
     float *y;
+    int act;            // kActNone / kActRelu / kActRelu6, applied after the bias
     int n, c, h, wd, cpg;
     int qcols;         // ceil(wd / kNhwcPx)
     int cquads;        // c / 4
@@ -124,8 +125,9 @@ __global__ void __launch_bounds__(256) nhwc_conv_kernel(const __grid_constant__ 
 #pragma unroll
         for (int p = 0; p < kNhwcPx; ++p) {
             if (w0 + p >= P.wd) break;
-            float4 v = make_float4(acc[0][p], acc[1][p], acc[2][p], acc[3][p]);
-            if (P.bias != nullptr) v = make_float4(v.x + b[0], v.y + b[1], v.z + b[2], v.w + b[3]);
+            const bool hb = P.bias != nullptr;
+            const float4 v = make_float4(epilogue(acc[0][p], hb, b[0], P.act), epilogue(acc[1][p], hb, b[1], P.act),
+                                         epilogue(acc[2][p], hb, b[2], P.act), epilogue(acc[3][p], hb, b[3], P.act));
             *reinterpret_cast<float4 *>(out + p * C) = v;
         }
     }
@@ -136,6 +138,7 @@ struct NhwcScalarParams {
     const float *wt;    // weights
     const float *bias;  // nullable
     float *y;
+    int act;            // kActNone / kActRelu / kActRelu6, applied after the bias
     long long n, cin, cout, h, w, r, s, groups, sh, sw, ph, pw, dh, dw, ho, wo;
     long long total;    // n * ho * wo * cout
 };
@@ -166,8 +169,8 @@ __global__ void __launch_bounds__(256) nhwc_scalar_kernel(const __grid_constant_
                                __ldg(P.wt + ((co * cpg + ci) * P.r + r) * P.s + s), acc);
                 }
             }
-        if (P.bias != nullptr) acc += __ldg(P.bias + co);
-        P.y[o] = acc;
+        const bool hb = P.bias != nullptr;
+        P.y[o] = epilogue(acc, hb, hb ? __ldg(P.bias + co) : 0.0f, P.act);
     }
 }
 

@@ -127,17 +127,27 @@ typedef enum {
                          descriptor dims (N, C, H, W), PyTorch's channels_last format */
 } gc_b200_layout;
 
-/* Convolution with an optional bias and a choice of layout.  Same contract as
- * gc_cuda_conv (validation, current device, caller's stream, no allocation,
- * no synchronization); weights are always dense [Cout][Cin/groups][R][S].
+/* Activation applied after the bias by gc_b200_conv_ex. */
+#define GC_B200_ACT_NONE 0
+#define GC_B200_ACT_RELU 1  /* max(y, 0)          */
+#define GC_B200_ACT_RELU6 2 /* min(max(y, 0), 6)  */
+
+/* Convolution with an optional bias, an optional activation and a choice of
+ * layout.  Same contract as gc_cuda_conv (validation, current device,
+ * caller's stream, no allocation, no synchronization); weights are always
+ * dense [Cout][Cin/groups][R][S].
  *   bias    NULL for none, else a rank-1 dense FP32 CUDA tensor of Cout
  *           elements on the same device; y = conv(x, w) + bias[c], the bias
  *           added after the FP32 sum.  (The reference has no bias: its model
  *           runner reports biased layers, e.g. ConvNeXt's 7x7 depthwise ones,
- *           as unsupported - bench/model_run.py:46-49.)
- *   layout  GC_B200_NCHW: without a bias the production choice of
- *           gc_cuda_conv implementation 3 (or the general kernel outside B
- *           geometry); with a bias the depthwise engines or the general
+ *           as unsupported - bench/model_run.py:46-49.)  With a convolution's
+ *           batch normalisation folded into w and bias, conv + BN + ReLU6 of
+ *           an inference network is one call.
+ *   activation  GC_B200_ACT_NONE, _RELU or _RELU6, applied after the bias.
+ *   layout  GC_B200_NCHW: without bias and activation the production choice
+ *           of gc_cuda_conv implementation 3 (or the general kernel outside
+ *           B geometry); with either, the same kernel when it is one of the
+ *           direct engines, else the depthwise engines or the general
  *           kernel, any geometry.
  *           GC_B200_NHWC: x and y channels-last (the reference times this
  *           layout only through cuDNN, bench/cuda_boundaries.py:17, and its
@@ -146,7 +156,8 @@ typedef enum {
  *           scalar kernel for every other geometry.  Strides that are neither
  *           -> GC_UNSUPPORTED. */
 int gc_b200_conv_ex(const gc_shape *p, const gc_tensor *x, const gc_tensor *w,
-                    const gc_tensor *bias, gc_tensor *y, int layout, void *stream);
+                    const gc_tensor *bias, gc_tensor *y, int layout,
+                    int activation, void *stream);
 
 /* Launch plan chosen by the last successful gc_cuda_conv / gc_b200_conv call
  * on the calling thread: kernel family name, grid, block, shared memory and

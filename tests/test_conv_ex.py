@@ -31,9 +31,9 @@ def _cl(dims):
     return (h * w * c, 1, w * c, c)
 
 
-def _call(native, s, x, w, b, y, layout):
+def _call(native, s, x, w, b, y, layout, act=0):
     return native.lib.gc_b200_conv_ex(ct.byref(api.cshape(s)), ct.byref(x), ct.byref(w),
-                                      ct.byref(b) if b is not None else None, ct.byref(y), layout, None)
+                                      ct.byref(b) if b is not None else None, ct.byref(y), layout, act, None)
 
 
 def test_validation_without_a_device(native):
@@ -55,6 +55,7 @@ def test_validation_without_a_device(native):
     assert _call(native, s, xn, w, good_b, y, 1) == GC_UNSUPPORTED  # NCHW strides under the NHWC layout
     assert b'channels-last' in native.lib.gc_last_error()
     assert _call(native, s, x, w, good_b, y, 7) == GC_UNSUPPORTED
+    assert _call(native, s, x, w, good_b, y, 1, act=5) == GC_UNSUPPORTED
     short = _desc(s.input, _cl(s.input))
     short.bytes = 8
     assert _call(native, s, short, w, None, y, 1) == GC_INVALID  # too small, before the layout check
@@ -193,3 +194,64 @@ def test_nhwc_unaligned_takes_the_scalar_kernel(native, torch_cuda):
     assert 'engine=scalar' in plan, plan
     y64, bound = orc.conv_f64_bound(s, x, w)
     assert orc.bound_check(dy.contiguous().cpu().numpy(), y64, bound)['passed']
+
+
+EPI_SHAPES = [
+    # B geometry on the direct engines (depthwise TMA kernel, grouped warp-specialized kernel,
+    # cp.async staging for an odd width), the register-cell depthwise kernel, the general kernel
+    dict(n=4, cin=144, cout=144, h=56, w=56, groups=144),
+    dict(n=2, cin=64, cout=64, h=28, w=28, groups=16),
+    dict(n=2, cin=32, cout=32, h=13, w=15, groups=8),
+    dict(n=2, cin=16, cout=16, h=14, w=14, groups=16),
+    dict(n=1, cin=64, cout=64, h=10, w=12, groups=2),
+    dict(n=1, cin=96, cout=96, h=23, w=21, groups=96, sh=2, sw=2),
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize('act', ['relu', 'relu6'])
+@pytest.mark.parametrize('geo', EPI_SHAPES, ids=lambda g: '-'.join(f'{k}{v}' for k, v in g.items()))
+def test_bias_and_activation_epilogue(native, torch_cuda, geo, act):
+    """act(conv + b) against the FP64 oracle with the same bias and clamp
+    (the clamp can only shrink the error), on whichever kernel serves it."""
+    torch = torch_cuda
+    s = Shape(**geo)
+    x, w = inputs(s, 12)
+    x = x * 4.0  # outputs spread beyond 6 so that ReLU6 clamps both ends
+    b = np.linspace(-1.5, 1.5, s.cout).astype(np.float32)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        dx, dw, db = (torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in (x, w, b))
+        dy = torch.full(s.output, float('nan'), device='cuda')
+        native.conv_ex(s, dx, dw, dy, bias=db, activation=act, stream=stream.cuda_stream)
+        plan = native.last_plan()
+        stream.synchronize()
+    y64, bound = orc.conv_f64_bound(s, x, w)
+    bb = np.broadcast_to(b.astype(np.float64)[None, :, None, None], y64.shape)
+    hi = 6.0 if act == 'relu6' else np.inf
+    expected = np.clip(y64 + bb, 0.0, hi)
+    y = dy.cpu().numpy()
+    res = orc.bound_check(y, expected, bound + np.abs(bb))
+    assert res['passed'], (plan, res)
+    assert (y >= 0).all() and (y <= hi).all()
+    if act == 'relu6':
+        assert (y == 6.0).any() and (y == 0.0).any()
+
+
+@pytest.mark.gpu
+def test_activation_without_bias_on_the_production_kernel(native, torch_cuda):
+    torch = torch_cuda
+    s = Shape(n=2, cin=64, cout=64, h=28, w=28, groups=8)
+    x, w = inputs(s, 13)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        dx, dw = torch.from_numpy(x).cuda(), torch.from_numpy(w).cuda()
+        plain = torch.empty(s.output, device='cuda')
+        relu = torch.empty(s.output, device='cuda')
+        native.cuda(s, dx, dw, plain, 3, stream.cuda_stream)
+        production = native.last_plan().split()[0]
+        native.conv_ex(s, dx, dw, relu, activation='relu', stream=stream.cuda_stream)
+        plan = native.last_plan()
+        stream.synchronize()
+    assert plan.split()[0] == production, (plan, production)
+    assert torch.equal(relu, torch.clamp_min(plain, 0.0))

@@ -112,3 +112,43 @@ def test_input_on_a_device_other_than_the_current_one(native, torch_cuda):
             assert y.device == x.device
             torch.cuda.synchronize(1)
             assert orc.error_metrics(y.cpu().numpy(), ref.cpu().numpy())['passed']
+
+
+@pytest.mark.gpu
+def test_fused_conv_bn_relu6_block(native, torch_cuda):
+    """MobileNetV2 features[3] with its depthwise Conv2dNormActivation fused
+    into one gc_b200_conv_ex call (batch norm folded, ReLU6 in the epilogue)
+    matches the cuDNN block, with non-trivial batch-norm statistics."""
+    torchvision = pytest.importorskip('torchvision')
+    torch.backends.cudnn.allow_tf32 = False
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.manual_seed(2)
+    block = torchvision.models.mobilenet_v2(weights=None).features[3].eval()
+    g = torch.Generator().manual_seed(5)
+    for m in block.modules():
+        if isinstance(m, torch.nn.BatchNorm2d):
+            m.running_mean.copy_(torch.randn(m.num_features, generator=g) * 0.2)
+            m.running_var.copy_(torch.rand(m.num_features, generator=g) + 0.5)
+            m.weight.data.copy_(torch.rand(m.num_features, generator=g) + 0.5)
+            m.bias.data.copy_(torch.randn(m.num_features, generator=g) * 0.2)
+    block = block.cuda()
+    fused = copy.deepcopy(block)
+    names = torch_module.fuse_conv_bn_act(fused, torch_module.is_depthwise, native)
+    assert names == ['conv.1']
+    x = torch.randn((4, 24, 56, 56), generator=torch.Generator().manual_seed(2)).cuda()
+    with torch.inference_mode():
+        ref, out = block(x), fused(x)
+        again = fused(x)
+    torch.cuda.synchronize()
+    assert orc.error_metrics(out.cpu().numpy(), ref.cpu().numpy())['passed']
+    assert torch.equal(out, again)
+    for cpp in (True, False):  # the ctypes path gives the same result
+        mod = fused.conv[1]
+        op = mod._op
+        if not cpp:
+            mod._op = None
+        with torch.inference_mode():
+            got = fused(x)
+        mod._op = op
+        torch.cuda.synchronize()
+        assert torch.equal(got, out)
