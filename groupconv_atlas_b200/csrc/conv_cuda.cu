@@ -86,9 +86,9 @@ std::string format_plan(const PlanRecord &r) {
         break;
     case PlanRecord::kDw:
         std::snprintf(buf, sizeof(buf),
-                      "kernel=general engine=depthwise k=%lld grid=%lld block=256 smem=%lld bh=%lld bands=%lld "
+                      "kernel=general engine=depthwise k=%lld grid=%lld block=%lld smem=%lld bh=%lld bands=%lld "
                       "pitch=%lld items=%lld",
-                      v[0], v[1], v[2], v[3], v[4], v[5], v[6]);
+                      v[0], v[1], v[7], v[2], v[3], v[4], v[5], v[6]);
         break;
     case PlanRecord::kDwS2:
         std::snprintf(buf, sizeof(buf),
@@ -1090,15 +1090,21 @@ int launch_dw(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const f
                                          : reinterpret_cast<const void *>(&gcb::dw_conv_kernel<5, false>))
                                  : (unit ? reinterpret_cast<const void *>(&gcb::dw_conv_kernel<7, true>)
                                          : reinterpret_cast<const void *>(&gcb::dw_conv_kernel<7, false>));
+    // Threads per CTA: an item's outputs (quads of 4 for stride 1 and
+    // dilation 1), in whole warps, 64 to 256: small bands of small planes get
+    // small CTAs, so that more of them are resident per SM instead of most
+    // threads of a 256-thread CTA idling.
+    const long long work = bh * (unit ? ceil_div(wo, 4) : wo);
+    const int threads = static_cast<int>(std::min<long long>(256, std::max<long long>(64, round_up(work, 32))));
     int ctas = 0;
-    st = kernel_occupancy(dev, fn, 256, smem, facts.smem_optin, ctas);
+    st = kernel_occupancy(dev, fn, threads, smem, facts.smem_optin, ctas);
     if (st != GC_OK) return st;
     if (ctas < 1) return gc_error(GC_UNSUPPORTED, "depthwise kernel: does not fit on an SM");
     const int grid = static_cast<int>(std::min<long long>(P.items, static_cast<long long>(facts.sms) * ctas));
     void *args[] = {&P};
-    cudaError_t e = launch_pdl(fn, dim3(grid), dim3(256), args, smem, stream);
+    cudaError_t e = launch_pdl(fn, dim3(grid), dim3(threads), args, smem, stream);
     if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
-    record_plan(PlanRecord::kDw, "", false, p->r, grid, smem, bh, P.bands, P.pitch, P.items);
+    record_plan(PlanRecord::kDw, "", false, p->r, grid, smem, bh, P.bands, P.pitch, P.items, threads);
     return GC_OK;
 }
 
