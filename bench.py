@@ -79,6 +79,9 @@ def parse_args(argv=None):
     ap.add_argument('--no-e2e', action='store_true')
     ap.add_argument('--no-cudnn', action='store_true')
     ap.add_argument('--no-cpu-baseline', action='store_true')
+    ap.add_argument('--no-autotune', action='store_true',
+                    help='skip gc_b200_autotune (the library\'s benchmark mode, run once per shape before timing, '
+                         'as cuDNN runs with cudnn.benchmark)')
     ap.add_argument('--cpu-seconds', type=float, default=10.0, help='CPU baseline sample budget')
     ap.add_argument('--atlas-batches', type=int, default=10, help='atlas: paired batches per shape')
     ap.add_argument('--atlas-samples', type=int, default=30, help='atlas: samples per batch and implementation')
@@ -419,6 +422,14 @@ def measure_workload(args, name, scaling, ctx, primary):
     step_bytes = sum(p.bytes for p in pieces)
     step_flops = sum(p.flops for p in pieces)
 
+    # Benchmark mode once per piece shape (the library's own plan search, as
+    # the cuDNN baseline runs with cudnn.benchmark), outside the timed region.
+    if not args.no_autotune:
+        with torch.cuda.stream(stream):
+            for p in pieces:
+                native.autotune(p.shape, view(xs[0], p.x_off, p.shape.input), view(dw, p.w_off, p.shape.weight),
+                                view(ys[0], p.y_off, p.shape.output), stream=stream.cuda_stream)
+        stream.synchronize()
     # Correctness gate before timing: 64 FP64 points of every piece's output
     # (each unit's own sub-shape and views).
     plan = ''
@@ -900,6 +911,8 @@ def run_sweep(args):
             xs = [torch.rand(s.input, device='cuda', generator=g) * 2 - 1 for _ in range(sets)]
             ys = [torch.empty(s.output, device='cuda') for _ in range(sets)]
             w = torch.from_numpy(w_host).cuda()
+            if not args.no_autotune:
+                native.autotune(s, xs[0], w, ys[0], stream=stream.cuda_stream)
             native.cuda(s, xs[0], w, ys[0], 3, stream.cuda_stream)
             plan = native.last_plan()
             stream.synchronize()
@@ -981,6 +994,8 @@ def paired_shape_rows(args, entries):
             ys = [torch.empty(s.output, device='cuda') for _ in range(sets)]
             w = torch.from_numpy(w_host).cuda()
             db = torch.from_numpy(b_host).cuda() if with_bias else None
+            if not args.no_autotune and not with_bias:
+                native.autotune(s, xs[0], w, ys[0], stream=stream.cuda_stream)
             if with_bias:
                 native.conv_ex(s, xs[0], w, ys[0], bias=db, stream=stream.cuda_stream)
             else:

@@ -192,6 +192,7 @@ class Native:
         lib.gc_b200_selftest_wait_timeout.argtypes = [ct.c_uint32, ct.c_void_p]
         lib.gc_b200_conv_ex.argtypes = [ct.POINTER(CShape)] + [ct.POINTER(Tensor)] * 4 + [ct.c_int, ct.c_int,
                                                                                               ct.c_void_p]
+        lib.gc_b200_autotune.argtypes = [ct.POINTER(CShape)] + [ct.POINTER(Tensor)] * 3 + [ct.c_int, ct.c_void_p]
         lib.gc_b200_probe_ffma.argtypes = [ct.c_void_p, ct.c_int, ct.c_int, ct.c_void_p]
         lib.gc_b200_probe_ffma_flops.argtypes = [ct.c_int, ct.c_int]
         lib.gc_b200_probe_ffma_flops.restype = ct.c_longlong
@@ -245,6 +246,14 @@ class Native:
         self.check(self.lib.gc_b200_conv_ex(ct.byref(p), ct.byref(xd), ct.byref(wd),
                                             ct.byref(bd) if bd is not None else None, ct.byref(yd),
                                             native_int(lay), native_int(act), self._stream(stream)))
+        return y
+
+    def autotune(self, shape, x, w, y, candidates=8, stream=0):
+        """gc_b200_autotune: time the planner's best candidates on these
+        buffers once (synchronizing) and cache the fastest plan."""
+        p, xd, wd, yd = cshape(shape), tensor(x), tensor(w), tensor(y)
+        self.check(self.lib.gc_b200_autotune(ct.byref(p), ct.byref(xd), ct.byref(wd), ct.byref(yd),
+                                             native_int(candidates), self._stream(stream)))
         return y
 
     def last_plan(self):

@@ -461,7 +461,8 @@ int choose_pitch(int W, int qcols, int cw, int rblocks, int vr, int rows, int ce
 // Every CTA thread owns one cell, so a candidate needs cells <= 256; the
 // block is the cells rounded up to whole warps.
 int plan_small(const gc_shape *p, bool tma, bool w_aligned, bool y_aligned, int dev,
-               const DeviceFacts &facts, EnginePlan &out, bool &found) {
+               const DeviceFacts &facts, EnginePlan &out, bool &found,
+               std::vector<std::pair<double, EnginePlan>> *cands = nullptr) {
     const long long N = p->n, C = p->cin, H = p->h, W = p->w, cpg = p->cin / p->groups;
     const long long groups = p->groups;
     const bool compute_bound = cpg >= 4;
@@ -538,10 +539,8 @@ int plan_small(const gc_shape *p, bool tma, bool w_aligned, bool y_aligned, int 
                         const double inflight = ctas * (stages - 1) * (xf + wf) * 4.0;
                         score *= std::min(1.0, 0.7 + 0.3 * inflight / (64.0 * 1024));
                     }
-                    if (score <= best + 1e-9) continue;
-                    best = score;
-                    found = true;
-                    DirectParams &P = out.D;
+                    EnginePlan cand;
+                    DirectParams &P = cand.D;
                     std::memset(&P, 0, sizeof(P));
                     P.n = static_cast<int>(N);
                     P.c = static_cast<int>(C);
@@ -567,13 +566,18 @@ int plan_small(const gc_shape *p, bool tma, bool w_aligned, bool y_aligned, int 
                     P.bulk_w = bulk_w;
                     P.x_bytes = static_cast<unsigned>(pitch * rows * cb * 4);
                     P.w_bytes = static_cast<unsigned>(cb * cpg * 9 * 4);
-                    out.wide = false;
-                    out.var = &var;
-                    out.tma = tma;
-                    out.threads = threads;
-                    out.smem = smem;
-                    out.ctas_per_sm = ctas;
-                    out.grid = static_cast<int>(std::min<long long>(items, slots));
+                    cand.wide = false;
+                    cand.var = &var;
+                    cand.tma = tma;
+                    cand.threads = threads;
+                    cand.smem = smem;
+                    cand.ctas_per_sm = ctas;
+                    cand.grid = static_cast<int>(std::min<long long>(items, slots));
+                    if (cands != nullptr) cands->emplace_back(score, cand);
+                    if (score <= best + 1e-9) continue;
+                    best = score;
+                    found = true;
+                    out = cand;
                 }
             }
         }
@@ -699,11 +703,11 @@ int plan_engine(const gc_shape *p, const float *w, const float *y, bool tma, int
     return GC_OK;
 }
 
-int launch_direct(const gc_shape *p, const float *x, const float *w, float *y, bool tma, int dev,
-                  cudaStream_t stream, const float *bias = nullptr, int act = gcb::kActNone) {
-    EnginePlan plan;
-    int st = plan_engine(p, w, y, tma, dev, plan);
-    if (st != GC_OK) return st;
+// Launches one planned direct-engine kernel (the plan is a copy; its data
+// pointers and epilogue are filled in here).
+int launch_plan(EnginePlan plan, const gc_shape *p, const float *x, const float *w, float *y, bool tma,
+                cudaStream_t stream, const float *bias, int act) {
+    int st = GC_OK;
     if (plan.wide && (bias != nullptr || act != gcb::kActNone))
         return gc_error(GC_UNSUPPORTED, "channel-chunked kernel: no bias or activation epilogue");
     CUtensorMap map;
@@ -743,6 +747,68 @@ int launch_direct(const gc_shape *p, const float *x, const float *w, float *y, b
                     plan.Wp.kc, plan.Wp.chunks, plan.Wp.co_item, plan.Wp.bh, plan.Wp.items, plan.Wp.cells,
                     plan.Wp.pitch, plan.Wp.rows, plan.Wp.vec_store);
     return GC_OK;
+}
+
+int launch_direct(const gc_shape *p, const float *x, const float *w, float *y, bool tma, int dev,
+                  cudaStream_t stream, const float *bias = nullptr, int act = gcb::kActNone) {
+    EnginePlan plan;
+    int st = plan_engine(p, w, y, tma, dev, plan);
+    if (st != GC_OK) return st;
+    return launch_plan(plan, p, x, w, y, tma, stream, bias, act);
+}
+
+// Benchmark mode for the direct engines: time the planner's best-scored
+// candidate tilings (up to `candidates`) on the caller's buffers and store
+// the fastest in the plan cache, where every later call of the shape finds
+// it.  Synchronizes the stream; y ends with the result of the chosen plan.
+int autotune_direct(const gc_shape *p, const float *x, const float *w, float *y, bool tma, int dev,
+                    cudaStream_t stream, int candidates) {
+    DeviceFacts facts;
+    int st = device_facts(dev, facts);
+    if (st != GC_OK) return st;
+    const long long cpg = p->cin / p->groups;
+    if (!(cpg < 16 || (cpg == 16 && tma))) return GC_OK;  // the channel-chunked kernel has no candidates
+    std::vector<std::pair<double, EnginePlan>> cands;
+    EnginePlan best_plan;
+    bool found = false;
+    st = plan_small(p, tma, aligned16(w), aligned16(y), dev, facts, best_plan, found, &cands);
+    if (st != GC_OK) return st;
+    if (!found) return GC_OK;
+    std::stable_sort(cands.begin(), cands.end(),
+                     [](const auto &a, const auto &b) { return a.first > b.first; });
+    if (static_cast<int>(cands.size()) > candidates) cands.resize(candidates);
+    cudaEvent_t ev[2];
+    cudaError_t e = cudaEventCreate(&ev[0]);
+    if (e == cudaSuccess) e = cudaEventCreate(&ev[1]);
+    if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+    float best_ms = -1.0f;
+    size_t best_i = 0;
+    for (size_t i = 0; i < cands.size() && st == GC_OK; ++i) {
+        st = launch_plan(cands[i].second, p, x, w, y, tma, stream, nullptr, gcb::kActNone);  // warm-up
+        if (st != GC_OK) break;
+        e = cudaEventRecord(ev[0], stream);
+        for (int r = 0; r < 3 && e == cudaSuccess && st == GC_OK; ++r)
+            st = launch_plan(cands[i].second, p, x, w, y, tma, stream, nullptr, gcb::kActNone);
+        if (e == cudaSuccess) e = cudaEventRecord(ev[1], stream);
+        if (e == cudaSuccess) e = cudaEventSynchronize(ev[1]);
+        float ms = 0.0f;
+        if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, ev[0], ev[1]);
+        if (e != cudaSuccess) st = gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+        if (st == GC_OK && (best_ms < 0.0f || ms < best_ms)) {
+            best_ms = ms;
+            best_i = i;
+        }
+    }
+    cudaEventDestroy(ev[0]);
+    cudaEventDestroy(ev[1]);
+    if (st != GC_OK) return st;
+    {
+        const PlanKey key{dev, p->n, p->cin, p->h, p->w, p->groups,
+                          (tma ? 1 : 0) | (aligned16(w) ? 2 : 0) | (aligned16(y) ? 4 : 0)};
+        std::lock_guard<std::mutex> lock(g_mutex);
+        g_plans[key] = cands[best_i].second;
+    }
+    return launch_plan(cands[best_i].second, p, x, w, y, tma, stream, nullptr, gcb::kActNone);
 }
 
 // ---- tcgen05 3xTF32 implicit GEMM ------------------------------------------------------
@@ -1534,6 +1600,30 @@ int gc_b200_conv_ex(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, c
     }
     if (st != GC_OK) return st;
     cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? gc_error(GC_OK, "") : gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+}
+
+int gc_b200_autotune(const gc_shape *p, const gc_tensor *x, const gc_tensor *w, gc_tensor *y, int candidates,
+                     void *stream) {
+    int st = gc_validate_tensors(p, x, w, y, GC_CUDA, GC_F32);
+    if (st != GC_OK) return st;
+    if (candidates < 1 || candidates > 64) return gc_error(GC_INVALID, "candidates must be in 1..64");
+    int dev = -1;
+    st = device_and_stream_checks(x, w, y, stream, dev);
+    if (st != GC_OK) return st;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaError_t e = cudaStreamIsCapturing(reinterpret_cast<cudaStream_t>(stream), &cs);
+    if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+    if (cs != cudaStreamCaptureStatusNone)
+        return gc_error(GC_UNSUPPORTED, "autotuning times kernels: not inside a stream capture");
+    if (!b_geometry(p)) return gc_error(GC_OK, "");  // the general kernel has one plan
+    const int kernel = auto_kernel(p, x, w, dev);
+    if (kernel != GC_B200_DIRECT_TMA && kernel != GC_B200_DIRECT_LDG) return gc_error(GC_OK, "");
+    st = autotune_direct(p, static_cast<const float *>(x->data), static_cast<const float *>(w->data),
+                         static_cast<float *>(y->data), kernel == GC_B200_DIRECT_TMA, dev,
+                         reinterpret_cast<cudaStream_t>(stream), candidates);
+    if (st != GC_OK) return st;
+    e = cudaGetLastError();
     return e == cudaSuccess ? gc_error(GC_OK, "") : gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
 }
 

@@ -159,6 +159,19 @@ int gc_b200_conv_ex(const gc_shape *p, const gc_tensor *x, const gc_tensor *w,
                     const gc_tensor *bias, gc_tensor *y, int layout,
                     int activation, void *stream);
 
+/* Benchmark mode (the counterpart of a framework's "benchmark" convolution
+ * search): for a shape that implementation 3 serves with a direct engine,
+ * time the planner's `candidates` best-scored tilings (1..64) on these
+ * buffers and keep the fastest in the library's plan cache, where every later
+ * gc_cuda_conv / gc_b200_conv / gc_b200_conv_ex call with the same device,
+ * shape and alignment finds it (for the life of the process).  Other shapes:
+ * GC_OK, nothing timed.  Unlike gc_cuda_conv it synchronizes `stream`,
+ * creates two CUDA events and must not be called inside a stream capture
+ * (GC_UNSUPPORTED); y is overwritten with the convolution's result.  Allocates
+ * no device memory. */
+int gc_b200_autotune(const gc_shape *p, const gc_tensor *x, const gc_tensor *w,
+                     gc_tensor *y, int candidates, void *stream);
+
 /* Launch plan chosen by the last successful gc_cuda_conv / gc_b200_conv call
  * on the calling thread: kernel family name, grid, block, shared memory and
  * work split, as one line of text.  Empty before the first launch. */

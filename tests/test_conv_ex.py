@@ -255,3 +255,17 @@ def test_activation_without_bias_on_the_production_kernel(native, torch_cuda):
         stream.synchronize()
     assert plan.split()[0] == production, (plan, production)
     assert torch.equal(relu, torch.clamp_min(plain, 0.0))
+
+
+def test_autotune_validation_without_a_device(native):
+    """gc_b200_autotune validates like gc_cuda_conv, then its own argument."""
+    s = Shape(n=2, cin=8, cout=8, h=5, w=6, groups=4)
+    x = _desc(s.input, _dense(s.input), data=1 << 20)
+    w = _desc(s.weight, _dense(s.weight), data=1 << 24)
+    y = _desc(s.output, _dense(s.output), data=1 << 28)
+    call = lambda cand, yy=y: native.lib.gc_b200_autotune(ct.byref(api.cshape(s)), ct.byref(x), ct.byref(w),
+                                                          ct.byref(yy), cand, None)
+    assert call(0) == GC_INVALID and b'candidates' in native.lib.gc_last_error()
+    assert call(65) == GC_INVALID
+    bad = _desc(s.output, _dense(s.output), dtype=1, data=1 << 28)
+    assert call(8, bad) == GC_INVALID

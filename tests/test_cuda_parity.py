@@ -270,3 +270,46 @@ def test_depthwise_engine_leaves_other_kernel_sizes_to_the_general_kernel(native
     y, plan = run(native, torch_cuda, s, x, w, impl=0)
     assert plan.startswith('kernel=general grid='), plan
     assert_matches(s, x, w, y, label='9x9 depthwise')
+
+
+AUTOTUNE_SHAPES = [(4, 64, 56, 56, 1), (8, 64, 28, 28, 2), (16, 128, 56, 56, 4), (8, 256, 56, 56, 8),
+                   (4, 64, 28, 28, 16), (2, 32, 30, 44, 4)]
+
+
+@pytest.mark.parametrize('n,c,h,w,cpg', AUTOTUNE_SHAPES)
+def test_autotune_keeps_results_and_caches_a_plan(native, torch_cuda, n, c, h, w, cpg):
+    """Benchmark mode times candidate tilings and caches the fastest; every
+    candidate sums each output over ci then the 9 taps in order, so the result
+    before, during and after tuning is the same bit for bit."""
+    torch = torch_cuda
+    s = Shape(n=n, cin=c, cout=c, h=h, w=w, groups=c // cpg)
+    x, wt = inputs(s, 21)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        dx, dw = torch.from_numpy(x).cuda(), torch.from_numpy(wt).cuda()
+        before = torch.full(s.output, float('nan'), device='cuda')
+        tuned = torch.full(s.output, float('nan'), device='cuda')
+        after = torch.full(s.output, float('nan'), device='cuda')
+        native.cuda(s, dx, dw, before, 3, stream.cuda_stream)
+        native.autotune(s, dx, dw, tuned, stream=stream.cuda_stream)
+        native.cuda(s, dx, dw, after, 3, stream.cuda_stream)
+        plan = native.last_plan()
+        stream.synchronize()
+    assert torch.equal(before, tuned) and torch.equal(before, after), plan
+    assert_matches(s, x, wt, after.cpu().numpy(), label=f'{s} {plan}')
+
+
+def test_autotune_refuses_inside_a_capture(native, torch_cuda):
+    torch = torch_cuda
+    s = Shape(n=2, cin=32, cout=32, h=28, w=28, groups=8)
+    x, wt = inputs(s, 22)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        dx, dw = torch.from_numpy(x).cuda(), torch.from_numpy(wt).cuda()
+        dy = torch.empty(s.output, device='cuda')
+    stream.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with pytest.raises(NativeError) as err:
+        with torch.cuda.graph(graph, stream=stream):
+            native.autotune(s, dx, dw, dy, stream=stream.cuda_stream)
+    assert err.value.status == GC_UNSUPPORTED
