@@ -54,7 +54,7 @@ UNIT = 'GB/s'
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_PEAKS = {'hbm_gbs': 6650.0, 'bf16_tflops': 1590.0}
 WORKLOADS = ['config1', 'config2', 'config4_leaf', 'config5_g32', 'config5_g4', 'config4_block', 'config3', 'atlas',
-             'model_layers', 'kernels']
+             'model_layers', 'kernels', 'nhwc']
 DEFAULT_BLOCKS = 'config5_g4,config2'
 
 
@@ -1173,6 +1173,71 @@ def run_kernels(args):
     return 0
 
 
+def run_nhwc(args):
+    """Channels-last layers: gc_b200_conv_ex with layout NHWC against
+    torch.nn.functional.conv2d on channels_last tensors (cuDNN, TF32 off,
+    benchmark mode) - the reference's torch_tuned_channels_last variant
+    (bench/cuda_boundaries.py:17) - and against this library's own NCHW path on
+    the same layer; device time of K back-to-back calls between CUDA events."""
+    import torch
+    import torch.nn.functional as F
+    from groupconv_atlas_b200 import api
+    from groupconv_atlas_b200.api import Shape
+    from oracle import oracle as orc
+    rank, world, local = dist_setup()
+    if rank != 0:
+        return 0
+    torch.cuda.set_device(local)
+    set_fp32_precision(torch)
+    torch.backends.cudnn.benchmark = True
+    native = api.Native()
+    stream = torch.cuda.Stream()
+    rows = []
+    for spec in args.shapes.split(';'):
+        n, c, h, w, cpg = (int(v) for v in spec.split(','))
+        s = Shape(n=n, cin=c, cout=c, h=h, w=w, groups=c // cpg)
+        with torch.cuda.stream(stream), torch.inference_mode():
+            g = torch.Generator(device='cuda').manual_seed(n * 7 + c)
+            x = torch.rand(s.input, device='cuda', generator=g) * 2 - 1
+            wt = (torch.rand(s.weight, device='cuda', generator=g) * 2 - 1) / math.sqrt(9 * cpg)
+            xcl = x.contiguous(memory_format=torch.channels_last)
+            ycl = torch.empty(s.output, device='cuda').contiguous(memory_format=torch.channels_last)
+            y = torch.empty(s.output, device='cuda')
+            calls = {
+                'ours_nhwc': lambda: native.conv_ex(s, xcl, wt, ycl, layout='nhwc', stream=stream.cuda_stream),
+                'ours_nchw': lambda: native.cuda(s, x, wt, y, 3, stream.cuda_stream),
+                'cudnn_channels_last': lambda: F.conv2d(xcl, wt.contiguous(memory_format=torch.channels_last),
+                                                        padding=1, groups=s.groups),
+                'cudnn_nchw': lambda: F.conv2d(x, wt, padding=1, groups=s.groups),
+            }
+            row = {'shape': [n, c, h, w, cpg]}
+            for name, call in calls.items():
+                for _ in range(max(3, args.warmup)):
+                    call()
+                plan = native.last_plan() if name.startswith('ours') else None
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                for _ in range(args.steps):
+                    call()
+                b.record(stream)
+                stream.synchronize()
+                row[name] = {'us': a.elapsed_time(b) / args.steps * 1e3, **({'plan': plan} if plan else {})}
+            # the NHWC result equals the NCHW production result within the FP32 acceptance gate
+            m = orc.error_metrics(ycl.contiguous().cpu().numpy(), y.cpu().numpy())
+            row['nhwc_matches_nchw'] = m['passed']
+            row['speedup_vs_cudnn_channels_last'] = row['cudnn_channels_last']['us'] / row['ours_nhwc']['us']
+            rows.append(row)
+        del x, xcl, y, ycl
+        torch.cuda.empty_cache()
+    geo = math.exp(statistics.fmean(math.log(r['speedup_vs_cudnn_channels_last']) for r in rows))
+    print(json.dumps({'metric': 'channels-last layers: speed-up of gc_b200_conv_ex (NHWC) over cuDNN channels_last',
+                      'value': geo, 'unit': 'x', 'n_gpus': 1, 'steps': args.steps, 'dtype': 'f32',
+                      'data': 'synthetic uniform inputs on the device', 'higher_is_better': True,
+                      'config': {'workload': 'nhwc'}, 'all_match': all(r['nhwc_matches_nchw'] for r in rows),
+                      'rows': rows}), flush=True)
+    return 0 if all(r['nhwc_matches_nchw'] for r in rows) else 1
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.cudnn_leg:
@@ -1189,6 +1254,8 @@ def main(argv=None):
         return run_model_layers(args)
     if args.workload == 'kernels':
         return run_kernels(args)
+    if args.workload == 'nhwc':
+        return run_nhwc(args)
     return run_ours(args)
 
 

@@ -75,8 +75,8 @@ std::string format_plan(const PlanRecord &r) {
     case PlanRecord::kTf32:
         std::snprintf(buf, sizeof(buf),
                       "kernel=tf32x3 engine=tcgen05 n_cta=%lld block=320 smem=%lld M=%lld N=%lld nb=%lld sp=%lld "
-                      "strips=%lld items=%lld chunks=%lld rows_b=%lld ks=%lld",
-                      v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7], v[8], v[9], v[10]);
+                      "strips=%lld items=%lld chunks=%lld rows_b=%lld ks=%lld layout=%s",
+                      v[0], v[1], v[2], v[3], v[4], v[5], v[6], v[7], v[8], v[9], v[10], r.name);
         break;
     case PlanRecord::kSmall:
         std::snprintf(buf, sizeof(buf),
@@ -861,21 +861,24 @@ struct Tf32Plan {
 // Kernel instance for an output-channel block width and the pixel rows per
 // step (two or four rows per converter thread).
 template <int CO>
-const void *tf32_instance(bool two) {
+const void *tf32_instance(bool two, bool nhwc) {
+    if (nhwc)
+        return two ? reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<CO, 2, true>)
+                   : reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<CO, 4, true>);
     return two ? reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<CO, 2>)
                : reinterpret_cast<const void *>(&gcb::tf32x3_conv_kernel<CO, 4>);
 }
-const void *tf32_kernel_for(long long co, long long rows_b) {
+const void *tf32_kernel_for(long long co, long long rows_b, bool nhwc) {
     const bool two = rows_b <= 2 * gcb::kConvThreads;
     switch (co) {
-    case 8: return tf32_instance<8>(two);
-    case 16: return tf32_instance<16>(two);
-    case 24: return tf32_instance<24>(two);
-    case 32: return tf32_instance<32>(two);
-    case 40: return tf32_instance<40>(two);
-    case 48: return tf32_instance<48>(two);
-    case 56: return tf32_instance<56>(two);
-    case 64: return tf32_instance<64>(two);
+    case 8: return tf32_instance<8>(two, nhwc);
+    case 16: return tf32_instance<16>(two, nhwc);
+    case 24: return tf32_instance<24>(two, nhwc);
+    case 32: return tf32_instance<32>(two, nhwc);
+    case 40: return tf32_instance<40>(two, nhwc);
+    case 48: return tf32_instance<48>(two, nhwc);
+    case 56: return tf32_instance<56>(two, nhwc);
+    case 64: return tf32_instance<64>(two, nhwc);
     default: return nullptr;
     }
 }
@@ -883,7 +886,7 @@ const void *tf32_kernel_for(long long co, long long rows_b) {
 // Work split of the tensor-core path: images stacked per block, 256-pixel
 // strips per item (one, or two for 64-channel groups of large planes), items
 // in waves over the SMs.
-int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
+int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out, bool nhwc = false) {
     DeviceFacts facts;
     int st = device_facts(dev, facts);
     if (st != GC_OK) return st;
@@ -961,7 +964,7 @@ int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
     P.a_bytes = static_cast<unsigned>(9 * P.m * 32);
     P.b_bytes = static_cast<unsigned>(rows_b * 32);
     P.wraw_bytes = static_cast<unsigned>(co * 72 * 4);
-    const void *fn = tf32_kernel_for(co, rows_b);
+    const void *fn = tf32_kernel_for(co, rows_b, nhwc);
     int ctas = 0;
     st = kernel_occupancy(dev, fn, gcb::kTf32Threads, smem, facts.smem_optin, ctas);
     if (st != GC_OK) return st;
@@ -973,9 +976,10 @@ int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out) {
     return GC_OK;
 }
 
-int launch_tf32(const gc_shape *p, const float *x, const float *w, float *y, int dev, cudaStream_t stream) {
+int launch_tf32(const gc_shape *p, const float *x, const float *w, float *y, int dev, cudaStream_t stream,
+                bool nhwc = false) {
     Tf32Plan plan;
-    int st = plan_tf32(p, dev, plan);
+    int st = plan_tf32(p, dev, plan, nhwc);
     if (st != GC_OK) return st;
     plan.P.x = x;
     plan.P.w = w;
@@ -1002,8 +1006,8 @@ int launch_tf32(const gc_shape *p, const float *x, const float *w, float *y, int
         }
     }
     if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
-    record_plan(PlanRecord::kTf32, "", false, plan.grid, plan.smem, plan.P.m, gcb::kTf32N, plan.P.nb, plan.P.sp,
-                plan.P.strips, plan.P.items, plan.P.chunks, plan.P.rows_b, plan.P.ksplit);
+    record_plan(PlanRecord::kTf32, nhwc ? "nhwc" : "nchw", false, plan.grid, plan.smem, plan.P.m, gcb::kTf32N,
+                plan.P.nb, plan.P.sp, plan.P.strips, plan.P.items, plan.P.chunks, plan.P.rows_b, plan.P.ksplit);
     return GC_OK;
 }
 
@@ -1305,6 +1309,16 @@ int launch_nhwc(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const
     const bool vec = b && p->cin % 4 == 0 && aligned16(x) && aligned16(y) && (cpg == 1 || cpg == 2 || cpg % 4 == 0) &&
                      p->h < (1LL << 30) && p->w < (1LL << 30) && p->cin < (1LL << 30);
     cudaError_t e;
+    // Groups of more than 16 channels (a multiple of 8): the tensor-core
+    // path reads channels-last pixels directly (each pixel's 8 channels of a
+    // step are 32 contiguous bytes) and stores channels-last outputs.
+    if (b && bias == nullptr && act == gcb::kActNone && cpg > 16 && p->cin % 8 == 0 && aligned16(x)) {
+        gc_shape q = *p;
+        if (tf32_eligible(&q, x, w)) {
+            st = launch_tf32(&q, x, w, y, dev, stream, true);
+            if (st != GC_UNSUPPORTED) return st;
+        }
+    }
     if (vec) {
         gcb::NhwcParams P{};
         P.x = x;

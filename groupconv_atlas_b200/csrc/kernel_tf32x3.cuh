@@ -259,7 +259,7 @@ struct RowGeom {
     unsigned valid;
 };
 
-template <int ROWS>
+template <int ROWS, bool NHWC>
 __device__ __forceinline__ RowGeom<ROWS> tf32_rows(const Tf32Params &P, int blk, int strip, int ctid) {
     RowGeom<ROWS> gm;
     gm.valid = 0;
@@ -275,18 +275,37 @@ __device__ __forceinline__ RowGeom<ROWS> tf32_rows(const Tf32Params &P, int blk,
         const int ih = vrow - k * hp2 - 1, iw = o - vrow * P.wp - 1;
         const int img = blk * P.nb + k;
         const bool in = i < P.rows_b && k < P.nb && img < P.n && ih >= 0 && ih < P.h && iw >= 0 && iw < P.wd;
-        gm.off[r] = in ? static_cast<long long>(img) * image_floats + ih * P.wd + iw : 0;
+        // element offset of the pixel: its plane position (NCHW), or the
+        // first channel of the pixel (channels last)
+        gm.off[r] = !in ? 0
+                    : NHWC ? ((static_cast<long long>(img) * P.h + ih) * P.wd + iw) * P.c
+                           : static_cast<long long>(img) * image_floats + ih * P.wd + iw;
         gm.valid |= in ? (1u << r) : 0u;
     }
     return gm;
 }
 
 // The 8 channels of the chunk at every pixel row of this thread (0 outside images).
-template <int ROWS>
+template <int ROWS, bool NHWC>
 __device__ __forceinline__ void tf32_load_rows(const Tf32Params &P, int gq, int chunk, const RowGeom<ROWS> &gm,
                                                float (&v)[ROWS][8]) {
     const long long hw = static_cast<long long>(P.h) * P.wd;
-    const float *base = P.x + (static_cast<long long>(gq / P.co_blocks) * P.cpg + chunk * 8) * hw;
+    const long long c0 = static_cast<long long>(gq / P.co_blocks) * P.cpg + chunk * 8;
+    if (NHWC) {
+        // channels last: a pixel's 8 channels of the chunk are 32 contiguous bytes
+        const float *base = P.x + c0;
+#pragma unroll
+        for (int r = 0; r < ROWS; ++r) {
+            const bool in = (gm.valid >> r) & 1u;
+            const float4 a = in ? __ldg(reinterpret_cast<const float4 *>(base + gm.off[r])) : make_float4(0, 0, 0, 0);
+            const float4 b =
+                in ? __ldg(reinterpret_cast<const float4 *>(base + gm.off[r] + 4)) : make_float4(0, 0, 0, 0);
+            v[r][0] = a.x, v[r][1] = a.y, v[r][2] = a.z, v[r][3] = a.w;
+            v[r][4] = b.x, v[r][5] = b.y, v[r][6] = b.z, v[r][7] = b.w;
+        }
+        return;
+    }
+    const float *base = P.x + c0 * hw;
 #pragma unroll
     for (int r = 0; r < ROWS; ++r) {
         const bool in = (gm.valid >> r) & 1u;
@@ -303,7 +322,7 @@ __device__ __forceinline__ void tf32_load_rows(const Tf32Params &P, int gq, int 
 // pixels 0-15 of the chunk, lane l + HALF pixels 16-31).  The sums go through
 // the warp's transpose buffer, so that the stores run with consecutive lanes
 // on consecutive pixels of one output channel.
-template <int M, int CO>
+template <int M, int CO, bool NHWC>
 __device__ __forceinline__ void tf32_epilogue(const Tf32Params &P, uint32_t acc, int item, int sub, int warp,
                                               int lane, float *ep) {
     constexpr int HALF = M / 8;  // output channels per lane quadrant
@@ -337,7 +356,27 @@ __device__ __forceinline__ void tf32_epilogue(const Tf32Params &P, uint32_t acc,
         const int vrow = o / P.wp, col = o - vrow * P.wp;
         const int k = vrow / hp2, hh = vrow - k * hp2;
         const int img = blk * P.nb + k;
-        if (o < out_px && hh < P.h && col < P.wd && img < P.n) {
+        const bool valid = o < out_px && hh < P.h && col < P.wd && img < P.n;
+        if (NHWC) {
+            // channels last: each store instruction writes the quadrant's
+            // channels of two pixels (16 lanes of consecutive channels each)
+            const long long poff =
+                valid ? ((static_cast<long long>(img) * P.h + hh) * P.wd + col) * P.c + static_cast<long long>(g) * CO +
+                            quad * HALF
+                      : -1;
+            const int j = lane & 15;
+#pragma unroll 4
+            for (int it = 0; it < 16; ++it) {
+                const int px = 2 * it + (lane >> 4);
+                const long long off = __shfl_sync(0xffffffffu, poff, px);
+                if (off >= 0 && j < nco) {
+                    if (P.ksplit == 1)
+                        st_stream(P.y + off + j, ep[j * 33 + px]);
+                    else
+                        atomicAdd(P.y + off + j, ep[j * 33 + px]);
+                }
+            }
+        } else if (valid) {
             float *yp = ych + img * image_floats + static_cast<long long>(hh) * P.wd + col;
             if (P.ksplit == 1) {
                 for (int j = 0; j < nco; ++j) st_stream(yp + j * hw, ep[j * 33 + lane]);
@@ -350,7 +389,7 @@ __device__ __forceinline__ void tf32_epilogue(const Tf32Params &P, uint32_t acc,
     }
 }
 
-template <int CO, int ROWS>
+template <int CO, int ROWS, bool NHWC = false>
 __global__ void __launch_bounds__(kTf32Threads, 1)
     tf32x3_conv_kernel(const __grid_constant__ Tf32Params P, const __grid_constant__ CUtensorMap wmap) {
     constexpr int M = CO * 2 > 64 ? 128 : 64;
@@ -496,7 +535,7 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
             tc_fence_after();
             for (int sub = 0; sub < P.sp; ++sub) {
                 const int buf = P.sp == 1 ? (it & 1) : sub;
-                tf32_epilogue<M, CO>(P, tmem_base + static_cast<uint32_t>(buf * kTf32N), first + it * stride, sub, warp,
+                tf32_epilogue<M, CO, NHWC>(P, tmem_base + static_cast<uint32_t>(buf * kTf32N), first + it * stride, sub, warp,
                                  lane, ep);
                 tc_fence_before();
                 __syncwarp();
@@ -513,10 +552,10 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
             if (item_j != load_item) {
                 int blk, strip;
                 tf32_decode(P, first + item_j * stride, load_g, blk, strip, load_split);
-                lgm = tf32_rows<ROWS>(P, blk, strip, ctid);
+                lgm = tf32_rows<ROWS, NHWC>(P, blk, strip, ctid);
                 load_item = item_j;
             }
-            tf32_load_rows<ROWS>(P, load_g, load_split * P.chunks + chunk_j, lgm, buf);
+            tf32_load_rows<ROWS, NHWC>(P, load_g, load_split * P.chunks + chunk_j, lgm, buf);
         };
         // One pipeline step: wait for the stage, convert the weights and the
         // rows held in buf, publish, refill buf with step k+2, and run a due

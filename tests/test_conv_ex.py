@@ -144,6 +144,13 @@ NHWC_SHAPES = [
     (dict(n=2, cin=6, cout=6, h=9, w=9, groups=2), True),                    # C % 4 != 0
     (dict(n=2, cin=96, cout=96, h=23, w=21, groups=96, sh=2, sw=2), False),  # strided depthwise
     (dict(n=1, cin=16, cout=32, h=11, w=10, r=5, s=5, groups=4, ph=2, pw=2), True),
+    # groups of more than 16 channels: the tensor-core path reading and writing channels-last
+    (dict(n=2, cin=64, cout=64, h=13, w=15, groups=2), False),     # 32 channels per group
+    (dict(n=1, cin=256, cout=256, h=12, w=14, groups=1), False),   # dense: output-channel blocks, split K
+    (dict(n=3, cin=128, cout=128, h=7, w=7, groups=2), False),     # 64 per group, images stacked in a strip
+    (dict(n=2, cin=96, cout=96, h=11, w=13, groups=2), False),     # 48 per group
+    (dict(n=4, cin=256, cout=256, h=28, w=28, groups=4), False),   # two strips per item
+    (dict(n=2, cin=64, cout=64, h=9, w=10, groups=2), True),       # bias: the FFMA kernel
 ]
 
 
@@ -164,9 +171,13 @@ def test_nhwc(native, torch_cuda, geo, with_bias):
         native.conv_ex(s, dx, dw, dy, bias=db, layout='nhwc', stream=stream.cuda_stream)
         plan = native.last_plan()
         stream.synchronize()
-    assert plan.startswith('kernel=nhwc'), plan
-    vector = s.b_geometry and s.cin % 4 == 0 and s.cpg in (1, 2) or (s.b_geometry and s.cin % 4 == 0 and s.cpg % 4 == 0)
-    assert ('engine=vector4x4' in plan) == vector, plan
+    tensor = s.b_geometry and s.cpg > 16 and s.cpg % 8 == 0 and not with_bias
+    if tensor:
+        assert plan.startswith('kernel=tf32x3') and 'layout=nhwc' in plan, plan
+    else:
+        assert plan.startswith('kernel=nhwc'), plan
+        vector = s.b_geometry and s.cin % 4 == 0 and (s.cpg in (1, 2) or s.cpg % 4 == 0)
+        assert ('engine=vector4x4' in plan) == vector, plan
     y = dy.contiguous().cpu().numpy()  # back to NCHW order
     if with_bias:
         _bias_bound_check(s, x, w, b, y)
