@@ -1178,7 +1178,9 @@ def run_nhwc(args):
     torch.nn.functional.conv2d on channels_last tensors (cuDNN, TF32 off,
     benchmark mode) - the reference's torch_tuned_channels_last variant
     (bench/cuda_boundaries.py:17) - and against this library's own NCHW path on
-    the same layer; device time of K back-to-back calls between CUDA events."""
+    the same layer.  Device time: K calls captured in one CUDA graph, replayed
+    between CUDA events (host overheads of either API left out); 'api_us' is
+    the same K calls issued from Python one by one."""
     import torch
     import torch.nn.functional as F
     from groupconv_atlas_b200 import api
@@ -1201,13 +1203,14 @@ def run_nhwc(args):
             x = torch.rand(s.input, device='cuda', generator=g) * 2 - 1
             wt = (torch.rand(s.weight, device='cuda', generator=g) * 2 - 1) / math.sqrt(9 * cpg)
             xcl = x.contiguous(memory_format=torch.channels_last)
+            wcl = wt.contiguous(memory_format=torch.channels_last)
             ycl = torch.empty(s.output, device='cuda').contiguous(memory_format=torch.channels_last)
             y = torch.empty(s.output, device='cuda')
             calls = {
-                'ours_nhwc': lambda: native.conv_ex(s, xcl, wt, ycl, layout='nhwc', stream=stream.cuda_stream),
-                'ours_nchw': lambda: native.cuda(s, x, wt, y, 3, stream.cuda_stream),
-                'cudnn_channels_last': lambda: F.conv2d(xcl, wt.contiguous(memory_format=torch.channels_last),
-                                                        padding=1, groups=s.groups),
+                'ours_nhwc': lambda: native.conv_ex(s, xcl, wt, ycl, layout='nhwc',
+                                                    stream=torch.cuda.current_stream().cuda_stream),
+                'ours_nchw': lambda: native.cuda(s, x, wt, y, 3, torch.cuda.current_stream().cuda_stream),
+                'cudnn_channels_last': lambda: F.conv2d(xcl, wcl, padding=1, groups=s.groups),
                 'cudnn_nchw': lambda: F.conv2d(x, wt, padding=1, groups=s.groups),
             }
             row = {'shape': [n, c, h, w, cpg]}
@@ -1221,7 +1224,19 @@ def run_nhwc(args):
                     call()
                 b.record(stream)
                 stream.synchronize()
-                row[name] = {'us': a.elapsed_time(b) / args.steps * 1e3, **({'plan': plan} if plan else {})}
+                api_us = a.elapsed_time(b) / args.steps * 1e3
+                graph = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(graph, stream=stream):
+                    for _ in range(args.steps):
+                        call()
+                graph.replay()
+                a.record(stream)
+                graph.replay()
+                b.record(stream)
+                stream.synchronize()
+                row[name] = {'us': a.elapsed_time(b) / args.steps * 1e3, 'api_us': api_us,
+                             **({'plan': plan} if plan else {})}
+                del graph
             # the NHWC result equals the NCHW production result within the FP32 acceptance gate
             m = orc.error_metrics(ycl.contiguous().cpu().numpy(), y.cpu().numpy())
             row['nhwc_matches_nchw'] = m['passed']

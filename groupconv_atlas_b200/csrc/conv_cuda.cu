@@ -97,8 +97,8 @@ std::string format_plan(const PlanRecord &r) {
                       v[0], v[5], v[1], v[2], v[3], v[4]);
         break;
     case PlanRecord::kNhwc:
-        std::snprintf(buf, sizeof(buf), "kernel=nhwc engine=%s grid=%lld block=256 cpg=%lld bias=%lld", r.name, v[0],
-                      v[1], v[2]);
+        std::snprintf(buf, sizeof(buf), "kernel=nhwc engine=%s grid=%lld block=%lld cpg=%lld bias=%lld rows=%lld",
+                      r.name, v[0], v[1], v[2], v[3], v[4]);
         break;
     case PlanRecord::kGeneral:
         std::snprintf(buf, sizeof(buf), "kernel=general grid=%lld block=%lld run=%lld cob=%lld index=%s runs=%lld",
@@ -1312,11 +1312,66 @@ int launch_nhwc(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const
     // Groups of more than 16 channels (a multiple of 8): the tensor-core
     // path reads channels-last pixels directly (each pixel's 8 channels of a
     // step are 32 contiguous bytes) and stores channels-last outputs.
-    if (b && bias == nullptr && act == gcb::kActNone && cpg > 16 && p->cin % 8 == 0 && aligned16(x)) {
+    if (b && bias == nullptr && act == gcb::kActNone && cpg >= 16 && p->cin % 8 == 0 && aligned16(x)) {
         gc_shape q = *p;
         if (tf32_eligible(&q, x, w)) {
             st = launch_tf32(&q, x, w, y, dev, stream, true);
             if (st != GC_UNSUPPORTED) return st;
+        }
+    }
+    // Groups of 1, 2, 4 and 8: threads walk down strips of output rows, the
+    // layer's weights in shared memory (when they fit in 160 KB).
+    const size_t wbytes = static_cast<size_t>(p->cin) * cpg * 9 * 4;
+    if (vec && p->n < (1LL << 30) && (cpg == 1 || cpg == 2 || cpg == 4 || cpg == 8) && wbytes <= 160 * 1024) {
+        gcb::NhwcStripParams P{};
+        P.x = x;
+        P.w = w;
+        P.bias = bias;
+        P.y = y;
+        P.act = act;
+        P.n = static_cast<int>(p->n);
+        P.c = static_cast<int>(p->cin);
+        P.h = static_cast<int>(p->h);
+        P.wd = static_cast<int>(p->w);
+        P.qcols = static_cast<int>(ceil_div(p->w, 4));
+        P.cquads = static_cast<int>(p->cin / 4);
+        const void *fn = cpg == 1   ? reinterpret_cast<const void *>(&gcb::nhwc_strip_kernel<1, false>)
+                         : cpg == 2 ? reinterpret_cast<const void *>(&gcb::nhwc_strip_kernel<2, false>)
+                         : cpg == 4 ? reinterpret_cast<const void *>(&gcb::nhwc_strip_kernel<4, false>)
+                                    : reinterpret_cast<const void *>(&gcb::nhwc_strip_kernel<8, false>);
+        size_t smem = wbytes;
+        int ctas = 0;
+        st = kernel_occupancy(dev, fn, 128, smem, facts.smem_optin, ctas);
+        if (st != GC_OK) return st;
+        if (ctas >= 1) {
+            // longest strips (8, 4, 2 or 1 rows) that still give every
+            // resident thread two items
+            const long long resident = static_cast<long long>(facts.sms) * ctas * 128;
+            const long long cols = p->n * P.qcols * static_cast<long long>(P.cquads);
+            int hb = 8;
+            while (hb > 1 && cols * ceil_div(p->h, hb) < 2 * resident) hb /= 2;
+            bool rw = false;
+            if (hb == 1 && cpg == 1 && wbytes > 16 * 1024 && aligned16(w)) {
+                // depthwise, one-row strips, more than 16 KB of weights for
+                // every CTA to stage: weights per item from global memory
+                rw = true;
+                fn = reinterpret_cast<const void *>(&gcb::nhwc_strip_kernel<1, true>);
+                smem = 0;
+                st = kernel_occupancy(dev, fn, 128, smem, facts.smem_optin, ctas);
+                if (st != GC_OK) return st;
+                if (ctas < 1) return gc_error(GC_DEVICE_ERROR, "NHWC strip kernel does not fit on an SM");
+            }
+            P.hb = hb;
+            P.hstrips = static_cast<int>(ceil_div(p->h, hb));
+            P.items = cols * P.hstrips;
+            const long long blocks =
+                std::min<long long>(ceil_div(P.items, 128), static_cast<long long>(facts.sms) * ctas);
+            void *args[] = {&P};
+            e = launch_pdl(fn, dim3(static_cast<unsigned>(blocks)), dim3(128), args, smem, stream);
+            if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+            record_plan(PlanRecord::kNhwc, rw ? "strip_rw" : "strip", false, blocks, 128, cpg,
+                        bias != nullptr ? 1 : 0, hb);
+            return GC_OK;
         }
     }
     if (vec) {
@@ -1341,7 +1396,7 @@ int launch_nhwc(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const
         void *args[] = {&P};
         e = launch_pdl(fn, dim3(static_cast<unsigned>(blocks)), dim3(256), args, 0, stream);
         if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
-        record_plan(PlanRecord::kNhwc, "vector4x4", false, blocks, cpg, bias != nullptr ? 1 : 0);
+        record_plan(PlanRecord::kNhwc, "vector4x4", false, blocks, 256, cpg, bias != nullptr ? 1 : 0, 1);
         return GC_OK;
     }
     gcb::NhwcScalarParams P{};
@@ -1372,7 +1427,7 @@ int launch_nhwc(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const
     e = launch_pdl(reinterpret_cast<const void *>(&gcb::nhwc_scalar_kernel), dim3(static_cast<unsigned>(blocks)),
                    dim3(256), args, 0, stream);
     if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
-    record_plan(PlanRecord::kNhwc, "scalar", false, blocks, cpg, bias != nullptr ? 1 : 0);
+    record_plan(PlanRecord::kNhwc, "scalar", false, blocks, 256, cpg, bias != nullptr ? 1 : 0, 1);
     return GC_OK;
 }
 

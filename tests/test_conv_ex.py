@@ -133,14 +133,22 @@ def test_nchw_without_bias_is_the_production_path(native, torch_cuda):
 
 
 NHWC_SHAPES = [
-    # (geometry, bias): the vector kernel (3x3 s1 p1, C % 4 == 0) at each group width, and the
-    # scalar kernel for other geometries and channel counts
+    # (geometry, bias): the vector kernels (3x3 s1 p1, C % 4 == 0; one group per warp for groups
+    # of 2, 4 and 8) at each group width, and the scalar kernel for other geometries and
+    # channel counts
     (dict(n=4, cin=144, cout=144, h=56, w=56, groups=144), False),
     (dict(n=2, cin=64, cout=64, h=13, w=15, groups=32), True),
     (dict(n=2, cin=64, cout=64, h=14, w=17, groups=16), False),
     (dict(n=2, cin=128, cout=128, h=9, w=10, groups=16), True),
     (dict(n=1, cin=64, cout=64, h=12, w=12, groups=4), False),
     (dict(n=1, cin=48, cout=48, h=7, w=9, groups=1), True),
+    (dict(n=3, cin=96, cout=96, h=17, w=30, groups=12), False),              # groups of 8, ragged quads
+    (dict(n=2, cin=32, cout=32, h=5, w=6, groups=8), False),                 # groups of 4, 2 pixels past the row
+    (dict(n=1, cin=24, cout=24, h=8, w=9, groups=12), False),                # groups of 2, 9 pixel columns
+    (dict(n=2, cin=256, cout=256, h=7, w=7, groups=64), True),               # groups of 4, item tail
+    (dict(n=8, cin=256, cout=256, h=56, w=54, groups=256), False),           # depthwise, strips of 2 rows
+    (dict(n=4, cin=960, cout=960, h=7, w=7, groups=960), True),              # depthwise, weights per item
+    (dict(n=16, cin=128, cout=128, h=63, w=64, groups=64), True),            # groups of 2, ragged last strip
     (dict(n=2, cin=6, cout=6, h=9, w=9, groups=2), True),                    # C % 4 != 0
     (dict(n=2, cin=96, cout=96, h=23, w=21, groups=96, sh=2, sw=2), False),  # strided depthwise
     (dict(n=1, cin=16, cout=32, h=11, w=10, r=5, s=5, groups=4, ph=2, pw=2), True),
@@ -171,13 +179,14 @@ def test_nhwc(native, torch_cuda, geo, with_bias):
         native.conv_ex(s, dx, dw, dy, bias=db, layout='nhwc', stream=stream.cuda_stream)
         plan = native.last_plan()
         stream.synchronize()
-    tensor = s.b_geometry and s.cpg > 16 and s.cpg % 8 == 0 and not with_bias
+    tensor = s.b_geometry and s.cpg >= 16 and s.cpg % 8 == 0 and not with_bias
     if tensor:
         assert plan.startswith('kernel=tf32x3') and 'layout=nhwc' in plan, plan
     else:
         assert plan.startswith('kernel=nhwc'), plan
         vector = s.b_geometry and s.cin % 4 == 0 and (s.cpg in (1, 2) or s.cpg % 4 == 0)
-        assert ('engine=vector4x4' in plan) == vector, plan
+        engine = 'strip' if s.cpg in (1, 2, 4, 8) else 'vector4x4'
+        assert (f'engine={engine}' in plan) == vector, plan  # 'strip' also matches 'strip_rw'
     y = dy.contiguous().cpu().numpy()  # back to NCHW order
     if with_bias:
         _bias_bound_check(s, x, w, b, y)
