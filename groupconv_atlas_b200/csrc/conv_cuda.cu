@@ -898,15 +898,16 @@ int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out, bool nhwc = false) {
     // Images per block and strips per item.  Every 256-pixel strip costs the
     // same MMA time; two strips per item share the chunk's weights (half the
     // weight work per pixel, fewer halo rows) but finish an item's MMAs
-    // before its epilogue, so they must not cost more waves than +15 %.  Only
-    // 64-channel groups of large planes (one image per block), whose weight
-    // tiles are the largest, gain from it (measured); narrower groups and
-    // stacked small images keep one strip per item.
+    // before its epilogue, so they must not cost more waves than +15 %, and
+    // the item needs at least 4 steps to amortize that epilogue (measured:
+    // 16-channel groups, 2 steps per item, lose 16 % with two strips; 32- and
+    // 64-channel groups of large planes gain up to 10 %).  Stacked small
+    // images keep one strip per item.
     long long best_nb = 1, best_items = 0, best_strips = 0, best_ks = 1;
     int best_sp = 1;
     const long long chunks = cpg / 8;
     double best_cost = -1.0;
-    for (int sp = 1; sp <= (co == 64 ? 2 : 1); ++sp) {
+    for (int sp = 1; sp <= (chunks >= 4 ? 2 : 1); ++sp) {
         if (!tf32_fits(cpg, W, sp, limit)) continue;
         for (long long nb = 1; nb <= N; ++nb) {
             if (sp == 2 && nb > 1) break;

@@ -171,6 +171,8 @@ TF32_SHAPES = [
     # 24/40/48/56-channel groups; wide groups and dense layers in output-channel blocks
     (2, 96, 11, 13, 48), (2, 48, 10, 9, 24), (1, 80, 12, 11, 40), (1, 112, 9, 8, 56),
     (2, 256, 9, 10, 128), (1, 256, 12, 14, 256), (2, 192, 8, 9, 96), (1, 160, 7, 9, 80), (1, 144, 8, 8, 72),
+    # two 256-pixel strips per item: 32- and 48-channel groups of large planes
+    (2, 64, 112, 112, 32), (3, 96, 64, 100, 48),
 ]
 
 
@@ -188,6 +190,16 @@ def test_tf32x3_refuses_rows_beyond_reach(native, torch_cuda):
     with pytest.raises(NativeError) as err:
         run(native, torch_cuda, s, x, wt, kernel='tf32x3')
     assert err.value.status == GC_UNSUPPORTED
+
+
+@pytest.mark.parametrize('n,c,h,w,cpg', [(2, 64, 112, 112, 32), (3, 96, 64, 100, 48)])
+def test_tf32x3_two_strips_per_item(native, torch_cuda, n, c, h, w, cpg):
+    """Groups of 32 and 48 channels on large planes take two strips per item."""
+    s = Shape(n=n, cin=c, cout=c, h=h, w=w, groups=c // cpg)
+    x, wt = inputs(s, 5)
+    y, plan = run(native, torch_cuda, s, x, wt, kernel='tf32x3')
+    assert ' sp=2 ' in plan, plan
+    assert_matches(s, x, wt, y, label=f'{s} {plan}')
 
 
 @pytest.mark.parametrize('n,c,h,w,cpg', TF32_SHAPES)
