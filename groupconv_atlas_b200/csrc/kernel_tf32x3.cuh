@@ -518,8 +518,7 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
         // Converter / epilogue warps.
         const int ctid = tid;  // 0 .. 255
         const uint32_t lbo_x = P.rows_b * 16u;
-        constexpr int kWVals = 72 * CO;  // weights per chunk
-        constexpr int kWPerThread = (kWVals + kConvThreads - 1) / kConvThreads;
+        static_assert(kConvThreads == 256, "weight split: 64 quads of 4 lanes");
         float *const ep = ep0 + warp * kTf32EpiFloats;
         int pending = -1;  // per-CTA item index whose epilogue is due
         bool failed = false;
@@ -575,24 +574,33 @@ __global__ void __launch_bounds__(kTf32Threads, 1)
                 failed = true;
                 return;
             }
-            // Weights: v = ((tap*2 + half)*CO + co)*4 + j enumerates the chunk's
-            // weights w[co][half*4 + j][tap]; hi goes to A row m_hi(co), lo to
-            // m_hi(co) + HALF, at byte tap*M*32 + half*M*16 + row*16 + j*4.
+            // Weights: the chunk's w[co][half*4 + j][tap] (raw [co][72] as
+            // staged) go to A row m_hi(co) (hi) and m_hi(co) + HALF (lo), at
+            // byte tap*M*32 + half*M*16 + row*16 + j*4.  The converter threads
+            // form 64 quads of 4 lanes (lane j of a quad takes input channel
+            // j of each half); kWR quads share an output channel and take
+            // every kWR-th (tap, half) pair, so the addresses are a per-thread
+            // base plus a constant of the unrolled loop (8 consecutive quads
+            // store 128 contiguous bytes).
             {
-                const float *wr = reinterpret_cast<const float *>(wraw0 + s * P.wraw_bytes);
-                unsigned char *const at = a0 + s * P.a_bytes;
-#pragma unroll 9
-                for (int q = 0; q < kWPerThread; ++q) {
-                    const int v = ctid + q * kConvThreads;
-                    if (kWVals % kConvThreads == 0 || v < kWVals) {
-                        const int j = v & 3, co = (v >> 2) % CO, th = (v >> 2) / CO;
-                        const int half = th & 1, tap = th >> 1;
-                        uint32_t hi, lo;
-                        tf32_split(wr[co * 72 + (half * 4 + j) * 9 + tap], hi, lo);
-                        const int row = (co / HALF) * RQ + (co % HALF);
-                        const uint32_t off = tap * M * 32u + half * M * 16u + row * 16u + j * 4u;
-                        *reinterpret_cast<uint32_t *>(at + off) = hi;
-                        *reinterpret_cast<uint32_t *>(at + off + HALF * 16u) = lo;
+                constexpr int kWR = 64 / CO;  // quads per output channel (CO <= 64)
+                const int j = ctid & 3, cq = ctid >> 2;
+                if (cq < kWR * CO) {
+                    const int co = cq % CO, t0 = cq / CO;
+                    const float *wr = reinterpret_cast<const float *>(wraw0 + s * P.wraw_bytes) + co * 72 + j * 9;
+                    unsigned char *const at =
+                        a0 + s * P.a_bytes + ((co / HALF) * RQ + (co % HALF)) * 16 + j * 4;
+#pragma unroll
+                    for (int t = 0; t < (18 + kWR - 1) / kWR; ++t) {
+                        const int th = t0 + t * kWR;  // (tap, half) pair: th = tap*2 + half
+                        if (th < 18) {
+                            const int half = th & 1, tap = th >> 1;
+                            uint32_t hi, lo;
+                            tf32_split(wr[half * 36 + tap], hi, lo);
+                            const uint32_t off = tap * M * 32u + half * M * 16u;
+                            *reinterpret_cast<uint32_t *>(at + off) = hi;
+                            *reinterpret_cast<uint32_t *>(at + off + HALF * 16u) = lo;
+                        }
                     }
                 }
             }
