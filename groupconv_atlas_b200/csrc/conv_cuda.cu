@@ -1313,7 +1313,8 @@ int launch_nhwc(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const
     // Groups of more than 16 channels (a multiple of 8): the tensor-core
     // path reads channels-last pixels directly (each pixel's 8 channels of a
     // step are 32 contiguous bytes) and stores channels-last outputs.
-    if (b && bias == nullptr && act == gcb::kActNone && cpg >= 16 && p->cin % 8 == 0 && aligned16(x)) {
+    if (b && bias == nullptr && act == gcb::kActNone && cpg >= 16 && p->cin % 8 == 0 && aligned16(x) &&
+        aligned16(y)) {
         gc_shape q = *p;
         if (tf32_eligible(&q, x, w)) {
             st = launch_tf32(&q, x, w, y, dev, stream, true);

@@ -358,22 +358,34 @@ __device__ __forceinline__ void tf32_epilogue(const Tf32Params &P, uint32_t acc,
         const int img = blk * P.nb + k;
         const bool valid = o < out_px && hh < P.h && col < P.wd && img < P.n;
         if (NHWC) {
-            // channels last: each store instruction writes the quadrant's
-            // channels of two pixels (16 lanes of consecutive channels each)
             const long long poff =
                 valid ? ((static_cast<long long>(img) * P.h + hh) * P.wd + col) * P.c + static_cast<long long>(g) * CO +
                             quad * HALF
                       : -1;
-            const int j = lane & 15;
+            if (P.ksplit == 1) {
+                // channels last: each lane stores 4 consecutive channels of a
+                // pixel (16 bytes; the quadrant's HALF channels of 32 / (HALF
+                // / 4) pixels per store instruction; y is 16-byte aligned and
+                // C, CO and HALF are multiples of 4)
+                constexpr int V = HALF / 4, PX = 32 / V;
+                const int j0 = 4 * (lane % V), pl = lane / V;
+#pragma unroll
+                for (int it = 0; it < V; ++it) {
+                    const int px = it * PX + pl;
+                    const long long off = __shfl_sync(0xffffffffu, poff, px);
+                    if (off >= 0 && j0 < nco)
+                        st_stream_v4(P.y + off + j0, ep[j0 * 33 + px], ep[(j0 + 1) * 33 + px], ep[(j0 + 2) * 33 + px],
+                                     ep[(j0 + 3) * 33 + px]);
+                }
+            } else {
+                // a part of the input channels: add into the zeroed output,
+                // two pixels (16 lanes of consecutive channels each) per step
+                const int j = lane & 15;
 #pragma unroll 4
-            for (int it = 0; it < 16; ++it) {
-                const int px = 2 * it + (lane >> 4);
-                const long long off = __shfl_sync(0xffffffffu, poff, px);
-                if (off >= 0 && j < nco) {
-                    if (P.ksplit == 1)
-                        st_stream(P.y + off + j, ep[j * 33 + px]);
-                    else
-                        atomicAdd(P.y + off + j, ep[j * 33 + px]);
+                for (int it = 0; it < 16; ++it) {
+                    const int px = 2 * it + (lane >> 4);
+                    const long long off = __shfl_sync(0xffffffffu, poff, px);
+                    if (off >= 0 && j < nco) atomicAdd(P.y + off + j, ep[j * 33 + px]);
                 }
             }
         } else if (valid) {
