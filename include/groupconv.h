@@ -151,10 +151,12 @@ typedef enum {
  *           kernel, any geometry.
  *           GC_B200_NHWC: x and y channels-last (the reference times this
  *           layout only through cuDNN, bench/cuda_boundaries.py:17, and its
- *           ABI rejects it, csrc/common/common.cpp:48): a vectorized kernel
- *           for 3x3/s1/p1 with C % 4 == 0 and 16-byte aligned x and y, a
- *           scalar kernel for every other geometry.  Strides that are neither
- *           -> GC_UNSUPPORTED. */
+ *           ABI rejects it, csrc/common/common.cpp:48).  3x3/s1/p1 layers
+ *           with C % 4 == 0 and 16-byte aligned x and y: groups of 16 or
+ *           more channels (a multiple of 8, no bias or activation) on the
+ *           tcgen05 3xTF32 path, groups of 1, 2, 4 and 8 on the strip kernel,
+ *           others on a vectorized kernel; a scalar kernel for every other
+ *           geometry.  Strides that are neither -> GC_UNSUPPORTED. */
 int gc_b200_conv_ex(const gc_shape *p, const gc_tensor *x, const gc_tensor *w,
                     const gc_tensor *bias, gc_tensor *y, int layout,
                     int activation, void *stream);
