@@ -241,6 +241,27 @@ int encode_nchw_map(CUtensorMap &map, const float *base, long long n, long long 
     return GC_OK;
 }
 
+// 4-D map over a channels-last float tensor: dims (C, W, H, N), box (bc, bw,
+// bh, 1), out-of-range elements read as zero (C % 4 == 0: every stride is a
+// multiple of 16 bytes).
+int encode_nhwc_map(CUtensorMap &map, const float *base, long long n, long long c, long long h, long long w,
+                    int bc, int bw, int bh) {
+    PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    int st = tensor_map_encoder(encode);
+    if (st != GC_OK) return st;
+    cuuint64_t dims[4] = {static_cast<cuuint64_t>(c), static_cast<cuuint64_t>(w), static_cast<cuuint64_t>(h),
+                          static_cast<cuuint64_t>(n)};
+    cuuint64_t strides[3] = {static_cast<cuuint64_t>(c) * 4, static_cast<cuuint64_t>(w * c) * 4,
+                             static_cast<cuuint64_t>(h * w * c) * 4};
+    cuuint32_t box[4] = {static_cast<cuuint32_t>(bc), static_cast<cuuint32_t>(bw), static_cast<cuuint32_t>(bh), 1u};
+    cuuint32_t estride[4] = {1, 1, 1, 1};
+    CUresult r = encode(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<float *>(base), dims, strides, box,
+                        estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return gc_error(GC_DEVICE_ERROR, "cuTensorMapEncodeTiled failed");
+    return GC_OK;
+}
+
 // 2-D map over a row-major float matrix [rows][cols] (cols * 4 a multiple of
 // 16 bytes): box (bw, bh), element (col, row) coordinates.
 int encode_rows_map(CUtensorMap &map, const float *base, long long rows, long long cols, int bw, int bh) {
@@ -1321,6 +1342,49 @@ int launch_nhwc(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const
             if (st != GC_UNSUPPORTED) return st;
         }
     }
+    // Groups of 1 and 2 channels: TMA-staged tiles of 32 channels x up to 32
+    // columns x up to 8 rows, two stages per persistent CTA.
+    if (vec && (cpg == 1 || cpg == 2) && aligned16(w) && (bias == nullptr || aligned16(bias)) && p->n < (1LL << 31) &&
+        p->h * p->w * p->cin < (1LL << 40)) {
+        gcb::NhwcDwTmaParams P{};
+        P.w = w;
+        P.bias = bias;
+        P.y = y;
+        P.act = act;
+        P.n = static_cast<int>(p->n);
+        P.c = static_cast<int>(p->cin);
+        P.h = static_cast<int>(p->h);
+        P.wd = static_cast<int>(p->w);
+        P.wtiles = static_cast<int>(ceil_div(p->w, 32));
+        P.tw = static_cast<int>(ceil_div(p->w, P.wtiles));
+        P.htiles = static_cast<int>(ceil_div(p->h, gcb::kDwTmaMaxTH));
+        P.th = static_cast<int>(ceil_div(p->h, P.htiles));
+        P.cblocks = static_cast<int>(ceil_div(p->cin, gcb::kDwTmaCB));
+        const long long items = p->n * P.htiles * P.wtiles * static_cast<long long>(P.cblocks);
+        if (items < (1LL << 31)) {
+            P.items = static_cast<int>(items);
+            P.box_bytes = static_cast<unsigned>(gcb::kDwTmaCB * (P.tw + 2) * (P.th + 2) * 4);
+            const size_t smem = 2 * static_cast<size_t>(P.box_bytes) + 16;
+            const int threads = 8 * P.tw;
+            const void *fn = cpg == 1 ? reinterpret_cast<const void *>(&gcb::nhwc_dw_tma_kernel<1>)
+                                      : reinterpret_cast<const void *>(&gcb::nhwc_dw_tma_kernel<2>);
+            int ctas = 0;
+            st = kernel_occupancy(dev, fn, threads, smem, facts.smem_optin, ctas);
+            if (st != GC_OK) return st;
+            if (ctas >= 1) {
+                CUtensorMap xmap;
+                std::memset(&xmap, 0, sizeof(xmap));
+                st = encode_nhwc_map(xmap, x, p->n, p->cin, p->h, p->w, gcb::kDwTmaCB, P.tw + 2, P.th + 2);
+                if (st != GC_OK) return st;
+                const long long blocks = std::min<long long>(items, static_cast<long long>(facts.sms) * ctas);
+                void *args[] = {&P, &xmap};
+                e = launch_pdl(fn, dim3(static_cast<unsigned>(blocks)), dim3(threads), args, smem, stream);
+                if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
+                record_plan(PlanRecord::kNhwc, "dw_tma", false, blocks, threads, cpg, bias != nullptr ? 1 : 0, P.th);
+                return GC_OK;
+            }
+        }
+    }
     // Groups of 1, 2, 4 and 8: threads walk down strips of output rows, the
     // layer's weights in shared memory (when they fit in 160 KB).
     const size_t wbytes = static_cast<size_t>(p->cin) * cpg * 9 * 4;
@@ -1337,11 +1401,11 @@ int launch_nhwc(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const
         P.wd = static_cast<int>(p->w);
         P.qcols = static_cast<int>(ceil_div(p->w, 4));
         P.cquads = static_cast<int>(p->cin / 4);
-        const void *fn = cpg == 1   ? reinterpret_cast<const void *>(&gcb::nhwc_strip_kernel<1, false>)
-                         : cpg == 2 ? reinterpret_cast<const void *>(&gcb::nhwc_strip_kernel<2, false>)
-                         : cpg == 4 ? reinterpret_cast<const void *>(&gcb::nhwc_strip_kernel<4, false>)
-                                    : reinterpret_cast<const void *>(&gcb::nhwc_strip_kernel<8, false>);
-        size_t smem = wbytes;
+        const void *fn = cpg == 1   ? reinterpret_cast<const void *>(&gcb::nhwc_strip_kernel<1>)
+                         : cpg == 2 ? reinterpret_cast<const void *>(&gcb::nhwc_strip_kernel<2>)
+                         : cpg == 4 ? reinterpret_cast<const void *>(&gcb::nhwc_strip_kernel<4>)
+                                    : reinterpret_cast<const void *>(&gcb::nhwc_strip_kernel<8>);
+        const size_t smem = wbytes;
         int ctas = 0;
         st = kernel_occupancy(dev, fn, 128, smem, facts.smem_optin, ctas);
         if (st != GC_OK) return st;
@@ -1352,17 +1416,6 @@ int launch_nhwc(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const
             const long long cols = p->n * P.qcols * static_cast<long long>(P.cquads);
             int hb = 8;
             while (hb > 1 && cols * ceil_div(p->h, hb) < 2 * resident) hb /= 2;
-            bool rw = false;
-            if (hb == 1 && cpg == 1 && wbytes > 16 * 1024 && aligned16(w)) {
-                // depthwise, one-row strips, more than 16 KB of weights for
-                // every CTA to stage: weights per item from global memory
-                rw = true;
-                fn = reinterpret_cast<const void *>(&gcb::nhwc_strip_kernel<1, true>);
-                smem = 0;
-                st = kernel_occupancy(dev, fn, 128, smem, facts.smem_optin, ctas);
-                if (st != GC_OK) return st;
-                if (ctas < 1) return gc_error(GC_DEVICE_ERROR, "NHWC strip kernel does not fit on an SM");
-            }
             P.hb = hb;
             P.hstrips = static_cast<int>(ceil_div(p->h, hb));
             P.items = cols * P.hstrips;
@@ -1371,8 +1424,7 @@ int launch_nhwc(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const
             void *args[] = {&P};
             e = launch_pdl(fn, dim3(static_cast<unsigned>(blocks)), dim3(128), args, smem, stream);
             if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
-            record_plan(PlanRecord::kNhwc, rw ? "strip_rw" : "strip", false, blocks, 128, cpg,
-                        bias != nullptr ? 1 : 0, hb);
+            record_plan(PlanRecord::kNhwc, "strip", false, blocks, 128, cpg, bias != nullptr ? 1 : 0, hb);
             return GC_OK;
         }
     }

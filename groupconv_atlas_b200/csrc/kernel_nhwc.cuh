@@ -18,6 +18,8 @@
 //                           chunks of a pixel.  CPG = 1 or 2 at compile
 //                           time, 0 = any multiple of 4 at run time.  Runs
 //                           the layers the strip kernel does not take.
+//   nhwc_dw_tma_kernel<CPG> groups of 1 and 2 channels (below): TMA-staged
+//                           tiles of 32 channels, double-buffered.
 //   nhwc_strip_kernel<CPG>  groups of 1, 2, 4 or 8 channels (below): a thread
 //                           walks down a strip of output rows, each input
 //                           row read once.
@@ -145,9 +147,8 @@ __global__ void __launch_bounds__(256) nhwc_conv_kernel(const __grid_constant__ 
 // three accumulator sets, so HB output rows cost HB + 2 input rows.  Weights
 // come from shared memory, staged once per persistent CTA as [tap][ci][C] so
 // that a warp's lanes read consecutive 16-byte vectors (no bank conflicts).
-// Depthwise layers of few pixels per channel (one-row strips) cannot amortize
-// that staging: there (RW) each thread loads its own 36 weights into
-// registers per item instead.  Consecutive threads take consecutive
+// (Groups of 1 and 2 channels take this kernel only where the TMA-staged one
+// below cannot run: unaligned weights or bias.)  Consecutive threads take consecutive
 // channel quads of the same pixels, so every load and store of a warp is
 // contiguous.
 struct NhwcStripParams {
@@ -164,15 +165,14 @@ struct NhwcStripParams {
     long long items;    // n * hstrips * qcols * cquads
 };
 
-template <int CPG, bool RW>
+template <int CPG>
 __global__ void __launch_bounds__(128, CPG == 8 ? 3 : 4) nhwc_strip_kernel(const __grid_constant__ NhwcStripParams P) {
     constexpr int kChunks = CPG <= 2 ? 1 : CPG / 4;
-    static_assert(!RW || CPG == 1, "register weights: depthwise layers only");
     extern __shared__ __align__(16) float wsm[];  // [tap][ci][C]
     griddep_wait();
     griddep_launch_dependents();
     const long long C = P.c;
-    if (!RW) {
+    {
         // coalesced reads of the dense [Cout][CPG][9] weights, 8 in flight
         // per thread, each scattered to its [tap][ci][C] slot
         const int total = 9 * CPG * P.c;
@@ -205,17 +205,6 @@ __global__ void __launch_bounds__(128, CPG == 8 ? 3 : 4) nhwc_strip_kernel(const
         const long long n = u / P.hstrips;
         const int c0 = 4 * cq, w0 = 4 * qc, h0 = hs * P.hb;
         const int h1 = min(h0 + P.hb, P.h);
-        // RW: the 4 output channels' weights [j][tap] are 9 contiguous 16-byte
-        // vectors, loaded per item (no staging: layers of few pixels)
-        float wr[RW ? 4 * CPG * 9 : 1];
-        if (RW) {
-            const float4 *src = reinterpret_cast<const float4 *>(P.w + static_cast<long long>(c0) * CPG * 9);
-#pragma unroll
-            for (int v = 0; v < (RW ? 9 * CPG : 0); ++v) {
-                const float4 q = __ldg(src + v);
-                wr[4 * v] = q.x, wr[4 * v + 1] = q.y, wr[4 * v + 2] = q.z, wr[4 * v + 3] = q.w;
-            }
-        }
         const int xc = CPG <= 2 ? c0 : c0 - c0 % CPG;  // first input channel read per pixel
         float acc[3][4][4];  // [slot][j][pixel]; slot of output row oh = (oh - h0 + 1) mod 3
 #pragma unroll
@@ -250,15 +239,9 @@ __global__ void __launch_bounds__(128, CPG == 8 ? 3 : 4) nhwc_strip_kernel(const
 #pragma unroll
                                 for (int ci = 0; ci < (CPG <= 2 ? CPG : 4); ++ci) {
                                     // weights of output channels c0 .. c0+3 for input channel ci
-                                    float wj[4];
-                                    if (RW) {
-#pragma unroll
-                                        for (int j = 0; j < 4; ++j) wj[j] = wr[((j * CPG + ci) * 9 + r * 3 + sx) % (RW ? 4 * CPG * 9 : 1)];
-                                    } else {
-                                        const float4 wv = *reinterpret_cast<const float4 *>(
-                                            wsm + ((r * 3 + sx) * CPG + 4 * cb + ci) * C + c0);
-                                        wj[0] = wv.x, wj[1] = wv.y, wj[2] = wv.z, wj[3] = wv.w;
-                                    }
+                                    const float4 wv = *reinterpret_cast<const float4 *>(
+                                        wsm + ((r * 3 + sx) * CPG + 4 * cb + ci) * C + c0);
+                                    const float wj[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
                                     for (int j = 0; j < 4; ++j) {
                                         // element of the pixel vector output channel j reads
@@ -295,6 +278,148 @@ __global__ void __launch_bounds__(128, CPG == 8 ? 3 : 4) nhwc_strip_kernel(const
                 }
             }
         }
+    }
+}
+
+// Depthwise (CPG 1) and 2-channel-group (CPG 2) 3x3/s1/p1 layers on
+// channels-last tensors with TMA staging: a work item
+// is a tile of TH output rows x TW output columns x 32 channels of one image;
+// one elected thread loads the tile's input box (32 channels x TW+2 columns x
+// TH+2 rows, starting at column and row -1) with one 4-D TMA copy, whose
+// out-of-range elements (the zero padding, and channels past C) read as zero.
+// Two stages alternate: the box of the CTA's next item is in flight while the
+// current one is computed.  Thread t owns channels 4 (t % 8) .. +3 of the
+// block and output column t / 8: it walks down the TH rows with a window of
+// 3 x 3 16-byte vectors (three new shared loads per row; a warp's loads are 4
+// columns x 128 contiguous bytes, no bank conflicts), its 36 CPG weights in
+// registers (a quad of channels holds whole groups, so its inputs are its own
+// 4 channels), and writes one 16-byte streaming store per row.
+struct NhwcDwTmaParams {
+    const float *w;
+    const float *bias;  // nullable
+    float *y;
+    int act;
+    int n, c, h, wd;
+    int tw, th;          // output columns / rows per tile (tw <= 32, th <= 8)
+    int wtiles, htiles;  // ceil(wd / tw), ceil(h / th)
+    int cblocks;         // ceil(c / 32)
+    int items;           // n * htiles * wtiles * cblocks
+    unsigned box_bytes;  // 32 * (tw + 2) * (th + 2) * 4
+};
+
+constexpr int kDwTmaCB = 32;  // channels per tile
+constexpr int kDwTmaMaxTH = 8;
+
+__device__ __forceinline__ void dw_tma_decode(const NhwcDwTmaParams &P, int item, int &n, int &h0, int &w0, int &c0) {
+    int t = item;
+    const int cb = t % P.cblocks;
+    t /= P.cblocks;
+    const int wt = t % P.wtiles;
+    t /= P.wtiles;
+    const int ht = t % P.htiles;
+    n = t / P.htiles;
+    h0 = ht * P.th;
+    w0 = wt * P.tw;
+    c0 = cb * kDwTmaCB;
+}
+
+template <int CPG>
+__global__ void __launch_bounds__(256) nhwc_dw_tma_kernel(const __grid_constant__ NhwcDwTmaParams P,
+                                                          const __grid_constant__ CUtensorMap xmap) {
+    extern __shared__ __align__(128) unsigned char dsm[];
+    float *const stage0 = reinterpret_cast<float *>(dsm);
+    uint64_t *const full = reinterpret_cast<uint64_t *>(dsm + 2 * P.box_bytes);
+    const int tid = threadIdx.x;
+    const int q = tid & 7, col = tid >> 3;  // channel quad, output column of the tile
+    const int first = blockIdx.x, stride = gridDim.x;
+    if (tid == 0) {
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    griddep_wait();
+    griddep_launch_dependents();
+    auto issue = [&](int item, int s) {
+        int n, h0, w0, c0;
+        dw_tma_decode(P, item, n, h0, w0, c0);
+        mbar_arrive_expect_tx(&full[s], P.box_bytes);
+        tma_load_4d(reinterpret_cast<unsigned char *>(stage0) + s * P.box_bytes, &xmap, c0, w0 - 1, h0 - 1, n,
+                    &full[s]);
+    };
+    if (tid == 0 && first < P.items) {
+        prefetch_tensormap(&xmap);
+        issue(first, 0);
+    }
+    const int bw = P.tw + 2;  // box columns
+    const long long C = P.c;
+    int it = 0;
+    for (int item = first; item < P.items; item += stride, ++it) {
+        const int s = it & 1;
+        // the next item's box goes to the other stage, free since the
+        // barrier at the end of the previous iteration
+        if (tid == 0 && item + stride < P.items) issue(item + stride, s ^ 1);
+        const bool ok = mbar_wait_bounded(&full[s], static_cast<uint32_t>((it >> 1) & 1));
+        if (!__syncthreads_and(ok)) {
+            if (tid == 0) {
+                raise_status(kStatusTmaTimeout);
+                // the other stage's copy may still be landing: wait for it
+                if (item + stride < P.items)
+                    mbar_wait_bounded(&full[s ^ 1], static_cast<uint32_t>(((it + 1) >> 1) & 1));
+            }
+            return;
+        }
+        int n, h0, w0, c0;
+        dw_tma_decode(P, item, n, h0, w0, c0);
+        const int c = c0 + 4 * q;
+        const bool active = col < P.tw && w0 + col < P.wd && c < P.c;
+        if (active) {
+            // weights [j][ci][tap] of output channels c .. c+3: 9 CPG
+            // contiguous 16-byte vectors
+            float4 wt[9 * CPG];
+            const float4 *wsrc = reinterpret_cast<const float4 *>(P.w + static_cast<long long>(c) * CPG * 9);
+#pragma unroll
+            for (int v = 0; v < 9 * CPG; ++v) wt[v] = __ldg(wsrc + v);
+            auto wk = [&](int j, int ci, int k) -> float {
+                const int e = (j * CPG + ci) * 9 + k;
+                return f4(wt[e >> 2], e & 3);
+            };
+            float4 b = make_float4(0, 0, 0, 0);
+            const bool hb = P.bias != nullptr;
+            if (hb) b = __ldg(reinterpret_cast<const float4 *>(P.bias + c));
+            const float *st = stage0 + s * (P.box_bytes / 4) + col * kDwTmaCB + 4 * q;
+            float4 win[3][3];  // [row of the window][tap column]
+#pragma unroll
+            for (int rr = 0; rr < 2; ++rr)
+#pragma unroll
+                for (int sx = 0; sx < 3; ++sx)
+                    win[rr][sx] = *reinterpret_cast<const float4 *>(st + (rr * bw + sx) * kDwTmaCB);
+            float *yrow = P.y + ((static_cast<long long>(n) * P.h + h0) * P.wd + w0 + col) * C + c;
+#pragma unroll
+            for (int r = 0; r < kDwTmaMaxTH; ++r) {
+                if (r >= P.th || h0 + r >= P.h) break;
+#pragma unroll
+                for (int sx = 0; sx < 3; ++sx)
+                    win[(r + 2) % 3][sx] =
+                        *reinterpret_cast<const float4 *>(st + ((r + 2) * bw + sx) * kDwTmaCB);
+                float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                for (int ky = 0; ky < 3; ++ky)
+#pragma unroll
+                    for (int sx = 0; sx < 3; ++sx) {
+                        const float4 xv = win[(r + ky) % 3][sx];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+#pragma unroll
+                            for (int ci = 0; ci < CPG; ++ci)
+                                a[j] = fmaf(f4(xv, (j / CPG) * CPG + ci), wk(j, ci, ky * 3 + sx), a[j]);
+                    }
+                st_stream_v4(yrow + static_cast<long long>(r) * P.wd * C, epilogue(a[0], hb, b.x, P.act),
+                             epilogue(a[1], hb, b.y, P.act), epilogue(a[2], hb, b.z, P.act),
+                             epilogue(a[3], hb, b.w, P.act));
+            }
+        }
+        __syncthreads();  // every thread is done with stage s before it is refilled
     }
 }
 

@@ -185,8 +185,8 @@ def test_nhwc(native, torch_cuda, geo, with_bias):
     else:
         assert plan.startswith('kernel=nhwc'), plan
         vector = s.b_geometry and s.cin % 4 == 0 and (s.cpg in (1, 2) or s.cpg % 4 == 0)
-        engine = 'strip' if s.cpg in (1, 2, 4, 8) else 'vector4x4'
-        assert (f'engine={engine}' in plan) == vector, plan  # 'strip' also matches 'strip_rw'
+        engine = 'dw_tma' if s.cpg in (1, 2) else 'strip' if s.cpg in (4, 8) else 'vector4x4'
+        assert (f'engine={engine}' in plan) == vector, plan
     y = dy.contiguous().cpu().numpy()  # back to NCHW order
     if with_bias:
         _bias_bound_check(s, x, w, b, y)
@@ -212,6 +212,30 @@ def test_nhwc_unaligned_takes_the_scalar_kernel(native, torch_cuda):
         plan = native.last_plan()
         stream.synchronize()
     assert 'engine=scalar' in plan, plan
+    y64, bound = orc.conv_f64_bound(s, x, w)
+    assert orc.bound_check(dy.contiguous().cpu().numpy(), y64, bound)['passed']
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize('groups', [32, 16])
+def test_nhwc_unaligned_weights_take_the_strip_kernel(native, torch_cuda, groups):
+    """Groups of 1 and 2 channels whose weights are not 16-byte aligned cannot
+    use the TMA-staged kernel (it loads weights as 16-byte vectors): the strip
+    kernel serves them."""
+    torch = torch_cuda
+    s = Shape(n=2, cin=32, cout=32, h=10, w=12, groups=groups)
+    x, w = inputs(s, 9)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        dx = torch.from_numpy(x).cuda().contiguous(memory_format=torch.channels_last)
+        buf = torch.empty(int(np.prod(s.weight)) + 1, device='cuda')
+        buf[1:].copy_(torch.from_numpy(w).cuda().reshape(-1))
+        dw = buf[1:].view(s.weight)  # dense, 4-byte offset
+        dy = torch.full(s.output, float('nan'), device='cuda').contiguous(memory_format=torch.channels_last)
+        native.conv_ex(s, dx, dw, dy, layout='nhwc', stream=stream.cuda_stream)
+        plan = native.last_plan()
+        stream.synchronize()
+    assert 'engine=strip' in plan, plan
     y64, bound = orc.conv_f64_bound(s, x, w)
     assert orc.bound_check(dy.contiguous().cpu().numpy(), y64, bound)['passed']
 
