@@ -1342,10 +1342,16 @@ int launch_nhwc(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const
             if (st != GC_UNSUPPORTED) return st;
         }
     }
-    // Groups of 1 and 2 channels: TMA-staged tiles of 32 channels x up to 32
-    // columns x up to 8 rows, two stages per persistent CTA.
-    if (vec && (cpg == 1 || cpg == 2) && aligned16(w) && (bias == nullptr || aligned16(bias)) && p->n < (1LL << 31) &&
-        p->h * p->w * p->cin < (1LL << 40)) {
+    // Groups of 1, 2 and 4 channels: TMA-staged tiles of 32 channels x up to
+    // 8 rows x up to 32 columns (groups of 1 and 2: a thread per 4 channels of
+    // a column; groups of 4: a thread per channel of 4 columns), two stages
+    // per persistent CTA.  (Groups of 8 on this kernel, 2 columns per thread,
+    // need 138 registers: one CTA per SM, slower than the strip kernel.)
+    if (vec && (cpg == 1 || cpg == 2 || cpg == 4) && aligned16(w) &&
+        (bias == nullptr || aligned16(bias)) && p->n < (1LL << 31)) {
+        const bool quad = cpg <= 2;  // a thread per 4 channels (else per channel)
+        const int nc = 4;  // columns per thread, groups of 4
+        const int max_tw = quad ? 32 : 8 * nc;
         gcb::NhwcDwTmaParams P{};
         P.w = w;
         P.bias = bias;
@@ -1355,8 +1361,10 @@ int launch_nhwc(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const
         P.c = static_cast<int>(p->cin);
         P.h = static_cast<int>(p->h);
         P.wd = static_cast<int>(p->w);
-        P.wtiles = static_cast<int>(ceil_div(p->w, 32));
-        P.tw = static_cast<int>(ceil_div(p->w, P.wtiles));
+        P.wtiles = static_cast<int>(ceil_div(p->w, max_tw));
+        // groups of 4 and 8: a multiple of the thread's columns, so that every
+        // column a thread reads lies inside the box
+        P.tw = static_cast<int>(quad ? ceil_div(p->w, P.wtiles) : round_up(ceil_div(p->w, P.wtiles), nc));
         P.htiles = static_cast<int>(ceil_div(p->h, gcb::kDwTmaMaxTH));
         P.th = static_cast<int>(ceil_div(p->h, P.htiles));
         P.cblocks = static_cast<int>(ceil_div(p->cin, gcb::kDwTmaCB));
@@ -1365,9 +1373,10 @@ int launch_nhwc(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const
             P.items = static_cast<int>(items);
             P.box_bytes = static_cast<unsigned>(gcb::kDwTmaCB * (P.tw + 2) * (P.th + 2) * 4);
             const size_t smem = 2 * static_cast<size_t>(P.box_bytes) + 16;
-            const int threads = 8 * P.tw;
-            const void *fn = cpg == 1 ? reinterpret_cast<const void *>(&gcb::nhwc_dw_tma_kernel<1>)
-                                      : reinterpret_cast<const void *>(&gcb::nhwc_dw_tma_kernel<2>);
+            const int threads = quad ? 8 * P.tw : 32 * static_cast<int>(ceil_div(P.tw, nc));
+            const void *fn = cpg == 1   ? reinterpret_cast<const void *>(&gcb::nhwc_dw_tma_kernel<1>)
+                             : cpg == 2 ? reinterpret_cast<const void *>(&gcb::nhwc_dw_tma_kernel<2>)
+                                        : reinterpret_cast<const void *>(&gcb::nhwc_grp_tma_kernel<4, 4>);
             int ctas = 0;
             st = kernel_occupancy(dev, fn, threads, smem, facts.smem_optin, ctas);
             if (st != GC_OK) return st;
@@ -1380,7 +1389,8 @@ int launch_nhwc(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const
                 void *args[] = {&P, &xmap};
                 e = launch_pdl(fn, dim3(static_cast<unsigned>(blocks)), dim3(threads), args, smem, stream);
                 if (e != cudaSuccess) return gc_error(GC_DEVICE_ERROR, cudaGetErrorString(e));
-                record_plan(PlanRecord::kNhwc, "dw_tma", false, blocks, threads, cpg, bias != nullptr ? 1 : 0, P.th);
+                record_plan(PlanRecord::kNhwc, quad ? "dw_tma" : "grp_tma", false, blocks, threads, cpg,
+                            bias != nullptr ? 1 : 0, P.th);
                 return GC_OK;
             }
         }

@@ -20,6 +20,9 @@
 //                           the layers the strip kernel does not take.
 //   nhwc_dw_tma_kernel<CPG> groups of 1 and 2 channels (below): TMA-staged
 //                           tiles of 32 channels, double-buffered.
+//   nhwc_grp_tma_kernel<CPG,NC> groups of 4 channels (below): the same
+//                           tiles, one output channel x NC columns per
+//                           thread.
 //   nhwc_strip_kernel<CPG>  groups of 1, 2, 4 or 8 channels (below): a thread
 //                           walks down a strip of output rows, each input
 //                           row read once.
@@ -417,6 +420,122 @@ __global__ void __launch_bounds__(256) nhwc_dw_tma_kernel(const __grid_constant_
                 st_stream_v4(yrow + static_cast<long long>(r) * P.wd * C, epilogue(a[0], hb, b.x, P.act),
                              epilogue(a[1], hb, b.y, P.act), epilogue(a[2], hb, b.z, P.act),
                              epilogue(a[3], hb, b.w, P.act));
+            }
+        }
+        __syncthreads();  // every thread is done with stage s before it is refilled
+    }
+}
+
+// Groups of 4 (or 8) channels (channels last, 3x3/s1/p1, C % 4 == 0) with the
+// same TMA-staged tiles and two stages: here a thread owns ONE output channel
+// (t % 32 of the tile's 32) and NC consecutive columns (column group t / 32
+// of 8; tiles of at most 8 NC columns), its 9 CPG weights in registers.  The
+// 4 (or 8) lanes of a group read the same 16-byte input vectors, so a warp's
+// shared load is one 128-byte wavefront; the thread streams the tile's input
+// rows top to bottom, adds each into the three output rows it touches (a ring
+// of three rows of NC sums: 3 NC independent chains) and stores an output row
+// (a warp: 32 consecutive channels of one pixel per store) when its last
+// input row has been added.
+template <int CPG, int NC>
+__global__ void __launch_bounds__(256) nhwc_grp_tma_kernel(const __grid_constant__ NhwcDwTmaParams P,
+                                                           const __grid_constant__ CUtensorMap xmap) {
+    constexpr int V = CPG / 4;  // 16-byte input vectors per pixel of a group
+    extern __shared__ __align__(128) unsigned char dsm[];
+    float *const stage0 = reinterpret_cast<float *>(dsm);
+    uint64_t *const full = reinterpret_cast<uint64_t *>(dsm + 2 * P.box_bytes);
+    const int tid = threadIdx.x;
+    const int cl = tid & 31, col0 = (tid >> 5) * NC;  // channel of the tile, first column of the thread
+    const int first = blockIdx.x, stride = gridDim.x;
+    if (tid == 0) {
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        fence_barrier_init();
+    }
+    __syncthreads();
+    griddep_wait();
+    griddep_launch_dependents();
+    auto issue = [&](int item, int s) {
+        int n, h0, w0, c0;
+        dw_tma_decode(P, item, n, h0, w0, c0);
+        mbar_arrive_expect_tx(&full[s], P.box_bytes);
+        tma_load_4d(reinterpret_cast<unsigned char *>(stage0) + s * P.box_bytes, &xmap, c0, w0 - 1, h0 - 1, n,
+                    &full[s]);
+    };
+    if (tid == 0 && first < P.items) {
+        prefetch_tensormap(&xmap);
+        issue(first, 0);
+    }
+    const int bw = P.tw + 2;
+    const long long C = P.c;
+    int it = 0;
+    for (int item = first; item < P.items; item += stride, ++it) {
+        const int s = it & 1;
+        if (tid == 0 && item + stride < P.items) issue(item + stride, s ^ 1);
+        const bool ok = mbar_wait_bounded(&full[s], static_cast<uint32_t>((it >> 1) & 1));
+        if (!__syncthreads_and(ok)) {
+            if (tid == 0) {
+                raise_status(kStatusTmaTimeout);
+                if (item + stride < P.items)
+                    mbar_wait_bounded(&full[s ^ 1], static_cast<uint32_t>(((it + 1) >> 1) & 1));
+            }
+            return;
+        }
+        int n, h0, w0, c0;
+        dw_tma_decode(P, item, n, h0, w0, c0);
+        const int c = c0 + cl;
+        const int ncols = min(NC, min(P.tw, P.wd - w0) - col0);  // columns of this thread in the image
+        if (ncols > 0 && c < P.c) {
+            float4 wt[9 * V];  // [ci][tap] of output channel c: 9 CPG contiguous floats
+            const float4 *wsrc = reinterpret_cast<const float4 *>(P.w + static_cast<long long>(c) * CPG * 9);
+#pragma unroll
+            for (int v = 0; v < 9 * V; ++v) wt[v] = __ldg(wsrc + v);
+            auto wk = [&](int ci, int k) -> float {
+                const int e = ci * 9 + k;
+                return f4(wt[e >> 2], e & 3);
+            };
+            const bool hb = P.bias != nullptr;
+            const float b = hb ? __ldg(P.bias + c) : 0.0f;
+            // the group's first channel in the tile, at the thread's first column
+            const float *st = stage0 + s * (P.box_bytes / 4) + col0 * kDwTmaCB + (cl - cl % CPG);
+            float *ycol = P.y + ((static_cast<long long>(n) * P.h + h0) * P.wd + w0 + col0) * C + c;
+            const int rows = min(P.th, P.h - h0);  // output rows of this tile
+            float acc[3][NC];                      // sums of output rows oh, slot oh % 3
+#pragma unroll
+            for (int a = 0; a < 3; ++a)
+#pragma unroll
+                for (int u = 0; u < NC; ++u) acc[a][u] = 0.0f;
+#pragma unroll
+            for (int ir = 0; ir < kDwTmaMaxTH + 2; ++ir) {  // box row = input row h0 - 1 + ir
+                if (ir >= rows + 2) break;
+                float4 xv[NC + 2][V];
+#pragma unroll
+                for (int q = 0; q < NC + 2; ++q)
+#pragma unroll
+                    for (int v = 0; v < V; ++v)
+                        xv[q][v] = *reinterpret_cast<const float4 *>(st + (ir * bw + q) * kDwTmaCB + 4 * v);
+#pragma unroll
+                for (int ky = 0; ky < 3; ++ky) {
+                    const int oh = ir - ky;  // output row this input row feeds with kernel row ky
+                    if (oh < 0 || oh >= rows) continue;
+#pragma unroll
+                    for (int sx = 0; sx < 3; ++sx)
+#pragma unroll
+                        for (int ci = 0; ci < CPG; ++ci) {
+                            const float wv = wk(ci, ky * 3 + sx);
+#pragma unroll
+                            for (int u = 0; u < NC; ++u)
+                                acc[oh % 3][u] = fmaf(f4(xv[u + sx][ci >> 2], ci & 3), wv, acc[oh % 3][u]);
+                        }
+                }
+                if (ir >= 2) {  // output row ir - 2 is complete
+                    const int oh = ir - 2;
+                    float *yr = ycol + static_cast<long long>(oh) * P.wd * C;
+#pragma unroll
+                    for (int u = 0; u < NC; ++u) {
+                        if (u < ncols) st_stream(yr + u * C, epilogue(acc[oh % 3][u], hb, b, P.act));
+                        acc[oh % 3][u] = 0.0f;
+                    }
+                }
             }
         }
         __syncthreads();  // every thread is done with stage s before it is refilled

@@ -185,7 +185,7 @@ def test_nhwc(native, torch_cuda, geo, with_bias):
     else:
         assert plan.startswith('kernel=nhwc'), plan
         vector = s.b_geometry and s.cin % 4 == 0 and (s.cpg in (1, 2) or s.cpg % 4 == 0)
-        engine = 'dw_tma' if s.cpg in (1, 2) else 'strip' if s.cpg in (4, 8) else 'vector4x4'
+        engine = {1: 'dw_tma', 2: 'dw_tma', 4: 'grp_tma', 8: 'strip'}.get(s.cpg, 'vector4x4')
         assert (f'engine={engine}' in plan) == vector, plan
     y = dy.contiguous().cpu().numpy()  # back to NCHW order
     if with_bias:
@@ -217,11 +217,11 @@ def test_nhwc_unaligned_takes_the_scalar_kernel(native, torch_cuda):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize('groups', [32, 16])
+@pytest.mark.parametrize('groups', [32, 16, 8, 4])
 def test_nhwc_unaligned_weights_take_the_strip_kernel(native, torch_cuda, groups):
-    """Groups of 1 and 2 channels whose weights are not 16-byte aligned cannot
-    use the TMA-staged kernel (it loads weights as 16-byte vectors): the strip
-    kernel serves them."""
+    """Groups of 1, 2, 4 and 8 channels whose weights are not 16-byte aligned
+    cannot use the TMA-staged kernels (they load weights as 16-byte vectors):
+    the strip kernel serves them."""
     torch = torch_cuda
     s = Shape(n=2, cin=32, cout=32, h=10, w=12, groups=groups)
     x, w = inputs(s, 9)
