@@ -70,6 +70,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
     return done != 0;
 }
 
+// Component k (0..3) of a 16-byte vector (k known at compile time after
+// unrolling).
+__device__ __forceinline__ float f4(const float4 &v, int k) {
+    return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w;
+}
+
 // Waits for the phase with the given parity to complete, for at most
 // limit_ns of global time.  Returns false when it gave up.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,

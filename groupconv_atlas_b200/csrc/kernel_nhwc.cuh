@@ -53,9 +53,6 @@ struct NhwcParams {
 
 __device__ __forceinline__ float4 ldg4(const float *p) { return __ldg(reinterpret_cast<const float4 *>(p)); }
 
-__device__ __forceinline__ float f4(const float4 &v, int k) {
-    return k == 0 ? v.x : k == 1 ? v.y : k == 2 ? v.z : v.w;
-}
 
 template <int CPG>
 __global__ void __launch_bounds__(256) nhwc_conv_kernel(const __grid_constant__ NhwcParams P) {
