@@ -17,15 +17,17 @@
 //                           consecutive threads read consecutive 16-byte
 //                           chunks of a pixel.  CPG = 1 or 2 at compile
 //                           time, 0 = any multiple of 4 at run time.  Runs
-//                           the layers the strip kernel does not take.
+//                           the 3x3/s1/p1 layers the kernels below do not
+//                           take (other group widths, larger weights).
 //   nhwc_dw_tma_kernel<CPG> groups of 1 and 2 channels (below): TMA-staged
 //                           tiles of 32 channels, double-buffered.
 //   nhwc_grp_tma_kernel<CPG,NC> groups of 4 channels (below): the same
 //                           tiles, one output channel x NC columns per
 //                           thread.
-//   nhwc_strip_kernel<CPG>  groups of 1, 2, 4 or 8 channels (below): a thread
-//                           walks down a strip of output rows, each input
-//                           row read once.
+//   nhwc_strip_kernel<CPG>  groups of 8 channels, and of 1, 2 or 4 whose
+//                           weights or bias are not 16-byte aligned (below):
+//                           a thread walks down a strip of output rows, each
+//                           input row read once.
 //   nhwc_scalar_kernel      any geometry (strides, dilations, kernel sizes,
 //                           Cin != Cout), any alignment: one output element
 //                           per thread, consecutive threads on consecutive
