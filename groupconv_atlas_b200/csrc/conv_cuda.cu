@@ -541,11 +541,15 @@ int plan_small(const gc_shape *p, bool tma, bool w_aligned, bool y_aligned, int 
                     const long long slots = static_cast<long long>(facts.sms) * ctas;
                     const double balance = grid_balance(items, slots, facts.sms);
                     const double cell_eff = static_cast<double>(cells) / round_up(cells, 32);
-                    // A CTA overlaps the staging of its next items with compute
-                    // only when it owns several items.
-                    const double per_cta = static_cast<double>(items) / std::min(items, slots);
+                    // An SM overlaps the staging of its next items with compute
+                    // only when it holds several items (in one CTA or several:
+                    // while one CTA waits for its stage, another computes).
+                    const double per_cta =
+                        static_cast<double>(items) / std::min(items, static_cast<long long>(facts.sms));
                     const double halo = static_cast<double>(rows) / bh;
-                    const double warps = ctas * threads / 32.0;
+                    // compute warps per SM (the copy and weight warps of the
+                    // warp-specialized kernel do no FFMAs)
+                    const double warps = ctas * std::ceil(cells / 32.0);
                     // rows computed past the image in the last band
                     const double band_eff = static_cast<double>(H) / (bands * rblocks * vr);
                     double score = balance * issue_efficiency(var, cpg);
