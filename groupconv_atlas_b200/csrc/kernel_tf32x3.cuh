@@ -163,6 +163,31 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// tmem_ld32 split in two: the load is issued here and its registers are
+// valid only after tmem_wait_ld32 on the same array (which takes them as
+// read-write operands, so no use can be scheduled before the wait).
+__device__ __forceinline__ void tmem_ld32_issue(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld32(uint32_t (&r)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                   "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                   "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                   "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+                 :
+                 : "memory");
+}
+
 // 16 consecutive accumulator columns of this warp's 32 TMEM lanes.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     uint32_t r[16];
@@ -339,11 +364,19 @@ __device__ __forceinline__ void tf32_epilogue(const Tf32Params &P, uint32_t acc,
     const int out_px = P.out_rows * P.wp;
     float *const ych = P.y + (static_cast<long long>(g) * CO + quad * HALF) * hw;
     float *const epw = ep + (lane & (HALF - 1)) * 33 + (low ? 0 : 16);
-#pragma unroll 1
+    // the TMEM load of chunk c32 + 1 is in flight while chunk c32 is summed
+    // and stored (two register sets, alternating)
+    const uint32_t tq = acc + colhalf * 128 + (static_cast<uint32_t>(quad * 32) << 16);
+    uint32_t rbuf[2][32];
+    tmem_ld32_issue(tq, rbuf[0]);
+#pragma unroll
     for (int c32 = 0; c32 < 4; ++c32) {
         const int col0 = colhalf * 128 + c32 * 32;
+        tmem_wait_ld32(rbuf[c32 & 1]);
+        if (c32 + 1 < 4) tmem_ld32_issue(tq + (c32 + 1) * 32, rbuf[(c32 + 1) & 1]);
         float v[32];
-        tmem_ld32(acc + col0 + (static_cast<uint32_t>(quad * 32) << 16), v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(rbuf[c32 & 1][i]);
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
             const float send = low ? v[16 + i] : v[i];
