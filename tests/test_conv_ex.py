@@ -282,6 +282,49 @@ def test_bias_and_activation_epilogue(native, torch_cuda, geo, act):
         assert (y == 6.0).any() and (y == 0.0).any()
 
 
+NHWC_EPI_SHAPES = [
+    # channels-last kernels carrying the epilogue: TMA-tiled (groups of 1, 2, 4), strip
+    # (groups of 8), vector (groups of 12), scalar (strided depthwise)
+    dict(n=4, cin=144, cout=144, h=56, w=56, groups=144),
+    dict(n=2, cin=64, cout=64, h=28, w=28, groups=32),
+    dict(n=2, cin=64, cout=64, h=28, w=28, groups=16),
+    dict(n=2, cin=64, cout=64, h=13, w=16, groups=8),
+    dict(n=1, cin=48, cout=48, h=9, w=10, groups=4),
+    dict(n=1, cin=96, cout=96, h=23, w=21, groups=96, sh=2, sw=2),
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize('act', ['relu', 'relu6'])
+@pytest.mark.parametrize('geo', NHWC_EPI_SHAPES, ids=lambda g: '-'.join(f'{k}{v}' for k, v in g.items()))
+def test_nhwc_bias_and_activation_epilogue(native, torch_cuda, geo, act):
+    """Channels-last act(conv + b) against the FP64 oracle, on whichever kernel serves it."""
+    torch = torch_cuda
+    s = Shape(**geo)
+    x, w = inputs(s, 14)
+    x = x * 4.0
+    b = np.linspace(-1.5, 1.5, s.cout).astype(np.float32)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        dx = torch.from_numpy(x).cuda().contiguous(memory_format=torch.channels_last)
+        dw, db = torch.from_numpy(w).cuda(), torch.from_numpy(b).cuda()
+        dy = torch.full(s.output, float('nan'), device='cuda').contiguous(memory_format=torch.channels_last)
+        native.conv_ex(s, dx, dw, dy, bias=db, layout='nhwc', activation=act, stream=stream.cuda_stream)
+        plan = native.last_plan()
+        stream.synchronize()
+    assert plan.startswith('kernel=nhwc'), plan
+    y64, bound = orc.conv_f64_bound(s, x, w)
+    bb = np.broadcast_to(b.astype(np.float64)[None, :, None, None], y64.shape)
+    hi = 6.0 if act == 'relu6' else np.inf
+    expected = np.clip(y64 + bb, 0.0, hi)
+    y = dy.contiguous().cpu().numpy()
+    res = orc.bound_check(y, expected, bound + np.abs(bb))
+    assert res['passed'], (plan, res)
+    assert (y >= 0).all() and (y <= hi).all()
+    if act == 'relu6':
+        assert (y == 6.0).any() and (y == 0.0).any()
+
+
 @pytest.mark.gpu
 def test_activation_without_bias_on_the_production_kernel(native, torch_cuda):
     torch = torch_cuda
