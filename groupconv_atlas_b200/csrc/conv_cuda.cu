@@ -1346,16 +1346,17 @@ int launch_nhwc(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const
             if (st != GC_UNSUPPORTED) return st;
         }
     }
-    // Groups of 1, 2 and 4 channels: TMA-staged tiles of 32 channels x up to
-    // 8 rows x up to 32 columns (groups of 1 and 2: a thread per 4 channels of
-    // a column; groups of 4: a thread per channel of 4 columns), two stages
-    // per persistent CTA.  (Groups of 8 on this kernel, 2 columns per thread,
-    // need 138 registers: one CTA per SM, slower than the strip kernel.)
-    if (vec && (cpg == 1 || cpg == 2 || cpg == 4) && aligned16(w) &&
+    // Groups of 1, 2, 4 and 8 channels: TMA-staged tiles of 32 channels x up
+    // to 8 rows x up to 32 columns (groups of 1 and 2: a thread per 4 channels
+    // of a column; groups of 4: a thread per channel of 4 columns), or 8
+    // columns (groups of 8: a thread per channel of 2 columns, 128-thread
+    // CTAs, so that their 138 registers still leave 3 CTAs per SM), two
+    // stages per persistent CTA.
+    if (vec && (cpg == 1 || cpg == 2 || cpg == 4 || cpg == 8) && aligned16(w) &&
         (bias == nullptr || aligned16(bias)) && p->n < (1LL << 31)) {
         const bool quad = cpg <= 2;  // a thread per 4 channels (else per channel)
-        const int nc = 4;  // columns per thread, groups of 4
-        const int max_tw = quad ? 32 : 8 * nc;
+        const int nc = cpg == 4 ? 4 : 2;  // columns per thread, groups of 4 and 8
+        const int max_tw = quad ? 32 : cpg == 4 ? 8 * nc : 8;
         gcb::NhwcDwTmaParams P{};
         P.w = w;
         P.bias = bias;
@@ -1380,7 +1381,8 @@ int launch_nhwc(const gc_shape *p, int64_t ho, int64_t wo, const float *x, const
             const int threads = quad ? 8 * P.tw : 32 * static_cast<int>(ceil_div(P.tw, nc));
             const void *fn = cpg == 1   ? reinterpret_cast<const void *>(&gcb::nhwc_dw_tma_kernel<1>)
                              : cpg == 2 ? reinterpret_cast<const void *>(&gcb::nhwc_dw_tma_kernel<2>)
-                                        : reinterpret_cast<const void *>(&gcb::nhwc_grp_tma_kernel<4, 4>);
+                             : cpg == 4 ? reinterpret_cast<const void *>(&gcb::nhwc_grp_tma_kernel<4, 4>)
+                                        : reinterpret_cast<const void *>(&gcb::nhwc_grp_tma_kernel<8, 2>);
             int ctas = 0;
             st = kernel_occupancy(dev, fn, threads, smem, facts.smem_optin, ctas);
             if (st != GC_OK) return st;

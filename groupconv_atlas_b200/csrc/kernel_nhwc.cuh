@@ -21,11 +21,11 @@
 //                           take (other group widths, larger weights).
 //   nhwc_dw_tma_kernel<CPG> groups of 1 and 2 channels (below): TMA-staged
 //                           tiles of 32 channels, double-buffered.
-//   nhwc_grp_tma_kernel<CPG,NC> groups of 4 channels (below): the same
-//                           tiles, one output channel x NC columns per
+//   nhwc_grp_tma_kernel<CPG,NC> groups of 4 and 8 channels (below): the
+//                           same tiles, one output channel x NC columns per
 //                           thread.
-//   nhwc_strip_kernel<CPG>  groups of 8 channels, and of 1, 2 or 4 whose
-//                           weights or bias are not 16-byte aligned (below):
+//   nhwc_strip_kernel<CPG>  groups of 1, 2, 4 or 8 channels whose weights or
+//                           bias are not 16-byte aligned (below):
 //                           a thread walks down a strip of output rows, each
 //                           input row read once.
 //   nhwc_scalar_kernel      any geometry (strides, dilations, kernel sizes,
@@ -425,7 +425,7 @@ __global__ void __launch_bounds__(256) nhwc_dw_tma_kernel(const __grid_constant_
     }
 }
 
-// Groups of 4 (or 8) channels (channels last, 3x3/s1/p1, C % 4 == 0) with the
+// Groups of 4 and 8 channels (channels last, 3x3/s1/p1, C % 4 == 0) with the
 // same TMA-staged tiles and two stages: here a thread owns ONE output channel
 // (t % 32 of the tile's 32) and NC consecutive columns (column group t / 32
 // of 8; tiles of at most 8 NC columns), its 9 CPG weights in registers.  The

@@ -185,7 +185,7 @@ def test_nhwc(native, torch_cuda, geo, with_bias):
     else:
         assert plan.startswith('kernel=nhwc'), plan
         vector = s.b_geometry and s.cin % 4 == 0 and (s.cpg in (1, 2) or s.cpg % 4 == 0)
-        engine = {1: 'dw_tma', 2: 'dw_tma', 4: 'grp_tma', 8: 'strip'}.get(s.cpg, 'vector4x4')
+        engine = {1: 'dw_tma', 2: 'dw_tma', 4: 'grp_tma', 8: 'grp_tma'}.get(s.cpg, 'vector4x4')
         assert (f'engine={engine}' in plan) == vector, plan
     y = dy.contiguous().cpu().numpy()  # back to NCHW order
     if with_bias:
