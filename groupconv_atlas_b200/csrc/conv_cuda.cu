@@ -943,15 +943,23 @@ int plan_tf32(const gc_shape *p, int dev, Tf32Plan &out, bool nhwc = false) {
             const long long items = static_cast<long long>(p->groups) * co_blocks * ceil_div(N, nb) * strips;
             if (items >= (1LL << 31)) continue;
             // Too few output tiles for the GPU: split the input channels
-            // into the most parts (dividing the chunks) that still fit one
-            // wave, so that the serial chain of steps per CTA shrinks.
+            // into parts (a divisor of the chunks) so that the
+            // serial chain of steps per CTA shrinks; the split minimizes
+            // waves x (steps per item + 1), the +1 for an item's prologue and
+            // epilogue (measured: N32 C256 7x7 dense 37.1 -> 34.4 us with 8
+            // parts in 3 waves against 2 parts in one wave).
             long long ks = 1;
-            if (sp == 1 && 2 * items <= facts.sms)
-                for (long long d = chunks; d > 1; --d)
-                    if (chunks % d == 0 && items * d <= facts.sms) {
+            if (sp == 1 && 2 * items <= facts.sms) {
+                double best_split = -1.0;
+                for (long long d = 1; d <= chunks; ++d) {
+                    if (chunks % d != 0) continue;
+                    const double c = static_cast<double>(ceil_div(items * d, facts.sms)) * (chunks / d + 1);
+                    if (best_split < 0.0 || c < best_split - 1e-9) {
+                        best_split = c;
                         ks = d;
-                        break;
                     }
+                }
+            }
             // estimated time: waves of items x steps per item
             const double cost = static_cast<double>(ceil_div(items * ks, facts.sms)) * (chunks / ks) * sp *
                                 (sp == 2 ? 0.87 : 1.0);
