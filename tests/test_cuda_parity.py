@@ -112,7 +112,7 @@ def test_b_geometry_shapes(native, torch_cuda, n, c, h, w, cpg, kernel):
 
 
 def test_config1_full(native, torch_cuda):
-    """Config 1 (N1 C32 56x56, groups of 4), full output, all implementations."""
+    """Config 1 (N1 C32 56x56, 8 groups of 4 channels), full output, all implementations."""
     wl = workloads.config1()
     for impl in (0, 1, 2, 3):
         y, plan = run(native, torch_cuda, wl.shape, wl.x, wl.w, impl=impl)
